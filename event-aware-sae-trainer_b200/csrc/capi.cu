@@ -1,0 +1,805 @@
+// C-ABI entry points of libsae_b200.so: argument checks, workspace carving,
+// TMA descriptor set-up and the launch sequence of each step phase.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+#include <string>
+
+#include "dense_kernels.cuh"
+#include "sae_b200.h"
+#include "step_kernels.cuh"
+#include "tile_gemm.cuh"
+
+using namespace sae;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<int64_t> g_launches{0};
+cudaEvent_t g_timer_start[2] = {nullptr, nullptr};
+cudaEvent_t g_timer_stop[2] = {nullptr, nullptr};
+
+void timer_begin(int which, cudaStream_t s) {
+  if (g_timer_start[which] != nullptr) cudaEventRecord(g_timer_start[which], s);
+}
+void timer_end(int which, cudaStream_t s) {
+  if (g_timer_stop[which] != nullptr) cudaEventRecord(g_timer_stop[which], s);
+}
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SAE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return SAE_OK;
+}
+
+#define SAE_TRY(expr)            \
+  do {                           \
+    const int _rc = (expr);      \
+    if (_rc != SAE_OK) return _rc; \
+  } while (0)
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int major = 0;
+};
+
+DeviceInfo device_info() {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && cache[dev].sm_count == 0) {
+    cudaDeviceGetAttribute(&cache[dev].sm_count, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&cache[dev].major, cudaDevAttrComputeCapabilityMajor, dev);
+  }
+  return (dev >= 0 && dev < 64) ? cache[dev] : DeviceInfo{};
+}
+
+// ------------------------------------------------------------ workspace
+struct Layout {
+  size_t theta, xc, pre, mask, tile_cnt, col_tot, col_offs, go, tok_sqerr, tok_cnt, gosum_part,
+      thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part, counters, total;
+};
+
+Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
+  Layout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  const size_t W = static_cast<size_t>((F + 31) / 32);
+  const size_t nT = static_cast<size_t>((B + TILE_N - 1) / TILE_N);
+  L.theta = take(F * 4);
+  L.xc = take(B * d * 2);
+  L.pre = take(B * F * 2);
+  L.mask = take(B * W * 4);
+  L.tile_cnt = take(nT * F * 4);
+  L.col_tot = take(F * 4);
+  L.col_offs = take((F + 1) * 4);
+  L.go = take(B * d * 2);
+  L.tok_sqerr = take(B * 4);
+  L.tok_cnt = take(B * 4);
+  L.gosum_part = take(static_cast<size_t>(DECODE_GRID) * d * 4);
+  L.thr_part = take(nT * F * 4);
+  L.dbenc_part = take(nT * F * 4);
+  L.db_enc = take(F * 4);
+  L.gemv_part = take(static_cast<size_t>(GEMV_GRID) * d * 4);
+  L.csr_tok = take(cap * 4);
+  L.csr_val = take(cap * 4);
+  L.sumsq_part = take(NORM_GRID * 4);
+  L.counters = take(256);
+  L.total = off;
+  return L;
+}
+
+struct Ws {
+  float* theta;
+  bf16* xc;
+  bf16* pre;
+  uint32_t* mask;
+  int* tile_cnt;
+  int* col_tot;
+  int* col_offs;
+  bf16* go;
+  float* tok_sqerr;
+  int* tok_cnt;
+  float* gosum_part;
+  float* thr_part;
+  float* dbenc_part;
+  float* db_enc;
+  float* gemv_part;
+  int* csr_tok;
+  uint32_t* csr_val;
+  float* sumsq_part;
+  int* counters;
+};
+
+Ws carve(void* base, const Layout& L) {
+  auto at = [&](size_t o) { return static_cast<uint8_t*>(base) + o; };
+  Ws w;
+  w.theta = reinterpret_cast<float*>(at(L.theta));
+  w.xc = reinterpret_cast<bf16*>(at(L.xc));
+  w.pre = reinterpret_cast<bf16*>(at(L.pre));
+  w.mask = reinterpret_cast<uint32_t*>(at(L.mask));
+  w.tile_cnt = reinterpret_cast<int*>(at(L.tile_cnt));
+  w.col_tot = reinterpret_cast<int*>(at(L.col_tot));
+  w.col_offs = reinterpret_cast<int*>(at(L.col_offs));
+  w.go = reinterpret_cast<bf16*>(at(L.go));
+  w.tok_sqerr = reinterpret_cast<float*>(at(L.tok_sqerr));
+  w.tok_cnt = reinterpret_cast<int*>(at(L.tok_cnt));
+  w.gosum_part = reinterpret_cast<float*>(at(L.gosum_part));
+  w.thr_part = reinterpret_cast<float*>(at(L.thr_part));
+  w.dbenc_part = reinterpret_cast<float*>(at(L.dbenc_part));
+  w.db_enc = reinterpret_cast<float*>(at(L.db_enc));
+  w.gemv_part = reinterpret_cast<float*>(at(L.gemv_part));
+  w.csr_tok = reinterpret_cast<int*>(at(L.csr_tok));
+  w.csr_val = reinterpret_cast<uint32_t*>(at(L.csr_val));
+  w.sumsq_part = reinterpret_cast<float*>(at(L.sumsq_part));
+  w.counters = reinterpret_cast<int*>(at(L.counters));
+  return w;
+}
+
+// ------------------------------------------------------------------ TMA
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Row-major bf16 [rows, cols] matrix, boxes of box_rows x 64 with 128-byte swizzle.
+int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (fn == nullptr) return fail(SAE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (!aligned16(base) || (cols * 2) % 16 != 0)
+    return fail(SAE_ERR_MISALIGNED, "TMA operand must be 16-byte aligned with 16-byte row pitch");
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {cols * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(TILE_K), box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r =
+      fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box,
+         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SAE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return SAE_OK;
+}
+
+bool tc_eligible(int64_t d, int64_t F, int force_simt) {
+  if (force_simt) return false;
+  const DeviceInfo di = device_info();
+  return di.major == 10 && d % TILE_K == 0 && F % TILE_M == 0 && d <= 65536;
+}
+
+// Launch the feature x token tile GEMM W [F, d] . T [B, d]^T with epilogue e.
+template <class Epi>
+int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64_t d,
+                     const Epi& e, bool use_tc, cudaStream_t stream, int timer = -1) {
+  const int m_tiles = static_cast<int>((F + TILE_M - 1) / TILE_M);
+  const int n_tiles = static_cast<int>((B + TILE_N - 1) / TILE_N);
+  if (use_tc) {
+    CUtensorMap tm_w, tm_t;
+    SAE_TRY(make_tmap(&tm_w, w, F, d, TILE_M));
+    SAE_TRY(make_tmap(&tm_t, tok, B, d, TILE_N));
+    static std::once_flag attr_once;
+    std::call_once(attr_once, [] {
+      cudaFuncSetAttribute(tc_tile_gemm<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(TC_SMEM_BYTES));
+    });
+    const int total = m_tiles * n_tiles;
+    const int grid = std::min(total, device_info().sm_count);
+    if (timer >= 0) timer_begin(timer, stream);
+    tc_tile_gemm<Epi><<<grid, TC_THREADS, TC_SMEM_BYTES, stream>>>(
+        tm_w, tm_t, m_tiles, n_tiles, static_cast<int>(d / TILE_K), e);
+    const int rc = check_launch("tc_tile_gemm");
+    if (timer >= 0) timer_end(timer, stream);
+    return rc;
+  }
+  dim3 grid(n_tiles, m_tiles);
+  if (timer >= 0) timer_begin(timer, stream);
+  simt_tile_gemm<Epi><<<grid, TILE_M, 0, stream>>>(w, tok, static_cast<int>(F),
+                                                   static_cast<int>(B), static_cast<int>(d), e);
+  const int rc = check_launch("simt_tile_gemm");
+  if (timer >= 0) timer_end(timer, stream);
+  return rc;
+}
+
+int grid_for(int64_t n, int threads, int per_sm = 8) {
+  const int64_t want = (n + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(std::max(1, device_info().sm_count)) * per_sm;
+  return static_cast<int>(std::max<int64_t>(1, std::min(want, cap)));
+}
+
+int vec_threads(int64_t d) {
+  const int64_t nv = d / 8;
+  return static_cast<int>(std::min<int64_t>(1024, std::max<int64_t>(32, (nv + 31) / 32 * 32)));
+}
+
+int check_model(const SaeB200Model* m, bool need_shadows) {
+  if (m == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "model is NULL");
+  if (m->d_in <= 0 || m->n_features <= 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "d_in and n_features must be positive");
+  if (!m->W_enc || !m->b_enc || !m->W_dec_fm || !m->b_dec || !m->log_threshold)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "model parameter pointer is NULL");
+  if (need_shadows && (!m->W_enc_bf16 || !m->W_dec_bf16))
+    return fail(SAE_ERR_INVALID_ARGUMENT, "bf16 weight copies are NULL");
+  return SAE_OK;
+}
+
+int check_fused_shape(const SaeB200Model* m) {
+  if (m->d_in % 8 != 0 || m->d_in > 8192)
+    return fail(SAE_ERR_UNSUPPORTED_SHAPE,
+                "fused step needs d_in %% 8 == 0 and d_in <= 8192 (got %lld)",
+                static_cast<long long>(m->d_in));
+  if (m->n_features > (int64_t(1) << 30))
+    return fail(SAE_ERR_UNSUPPORTED_SHAPE, "n_features too large");
+  return SAE_OK;
+}
+
+int check_ws(const Layout& L, void* ws, size_t bytes) {
+  if (ws == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "workspace is NULL");
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
+    return fail(SAE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  if (bytes < L.total)
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "workspace has %zu bytes, needs %zu", bytes, L.total);
+  return SAE_OK;
+}
+
+int check_cfg(const SaeB200StepConfig* c) {
+  if (c == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "config is NULL");
+  if (c->n_tokens <= 0 || c->n_tokens > (int64_t(1) << 30))
+    return fail(SAE_ERR_INVALID_ARGUMENT, "n_tokens out of range");
+  if (c->accum_steps <= 0) return fail(SAE_ERR_INVALID_ARGUMENT, "accum_steps must be >= 1");
+  if (c->csr_capacity < 0 || c->csr_capacity > (int64_t(1) << 31) - 1)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "csr_capacity out of range");
+  if (!(c->ste_bandwidth > 0.f)) return fail(SAE_ERR_INVALID_ARGUMENT, "ste_bandwidth must be > 0");
+  return SAE_OK;
+}
+
+}  // namespace
+
+// =====================================================================
+extern "C" {
+
+int sae_b200_version(void) { return 1; }
+
+int64_t sae_b200_launch_count(void) { return g_launches.load(); }
+
+int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event) {
+  if (kernel != SAE_KERNEL_ENCODER_GEMM && kernel != SAE_KERNEL_GRAD_GEMM)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "unknown kernel id %d", kernel);
+  if ((start_event == nullptr) != (stop_event == nullptr))
+    return fail(SAE_ERR_INVALID_ARGUMENT, "set both timer events or neither");
+  g_timer_start[kernel] = static_cast<cudaEvent_t>(start_event);
+  g_timer_stop[kernel] = static_cast<cudaEvent_t>(stop_event);
+  return SAE_OK;
+}
+
+const char* sae_b200_last_error(void) { return g_last_error.c_str(); }
+
+int sae_b200_get_device_status(int* status_out, int clear) {
+  if (status_out == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "status_out is NULL");
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
+  if (e != cudaSuccess) return fail(SAE_ERR_CUDA, "read status: %s", cudaGetErrorString(e));
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return fail(SAE_ERR_CUDA, "clear status: %s", cudaGetErrorString(e));
+  }
+  *status_out = v;
+  return SAE_OK;
+}
+
+int sae_b200_workspace_bytes(int64_t max_tokens, int64_t d_in, int64_t n_features,
+                             int64_t csr_capacity, size_t* bytes_out) {
+  if (bytes_out == nullptr || max_tokens <= 0 || d_in <= 0 || n_features <= 0 || csr_capacity < 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid workspace query");
+  *bytes_out = make_layout(max_tokens, d_in, n_features, csr_capacity).total;
+  return SAE_OK;
+}
+
+int sae_b200_workspace_offsets(int64_t n_tokens, int64_t d_in, int64_t n_features,
+                               int64_t csr_capacity, size_t* offsets_out) {
+  if (offsets_out == nullptr || n_tokens <= 0 || d_in <= 0 || n_features <= 0 || csr_capacity < 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid workspace query");
+  const Layout L = make_layout(n_tokens, d_in, n_features, csr_capacity);
+  const size_t o[SAE_WS_N_OFFSETS] = {L.theta, L.xc,       L.pre,      L.mask,    L.go,
+                                      L.tok_cnt, L.tok_sqerr, L.col_offs, L.csr_tok, L.csr_val};
+  for (int i = 0; i < SAE_WS_N_OFFSETS; ++i) offsets_out[i] = o[i];
+  return SAE_OK;
+}
+
+int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                           const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                           SaeB200StepStats* stats, float* x_hat_out, uint8_t* fired,
+                           void* stream_) {
+  SAE_TRY(check_model(model, true));
+  SAE_TRY(check_cfg(cfg));
+  SAE_TRY(check_fused_shape(model));
+  if (x == nullptr || stats == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "x/stats is NULL");
+  if (x_dtype != SAE_DTYPE_F32 && x_dtype != SAE_DTYPE_BF16)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "x_dtype must be F32 or BF16");
+  if (!aligned16(x) || !aligned16(model->W_dec_bf16) || !aligned16(model->W_enc_bf16) ||
+      (x_hat_out && !aligned16(x_hat_out)))
+    return fail(SAE_ERR_MISALIGNED, "x, x_hat and bf16 weights must be 16-byte aligned");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int64_t B = cfg->n_tokens, d = model->d_in, F = model->n_features;
+  const Layout L = make_layout(B, d, F, cfg->csr_capacity);
+  SAE_TRY(check_ws(L, workspace, workspace_bytes));
+  const Ws w = carve(workspace, L);
+  const int mask_words = static_cast<int>((F + 31) / 32);
+  const int n_tiles = static_cast<int>((B + TILE_N - 1) / TILE_N);
+
+  // 1. theta, xc
+  {
+    const int g = grid_for(std::max<int64_t>(F, B * d / 8), 256);
+    if (x_dtype == SAE_DTYPE_BF16)
+      prep_kernel<bf16><<<g, 256, 0, stream>>>(static_cast<const bf16*>(x), model->b_dec,
+                                               model->log_threshold, w.theta, w.xc, B,
+                                               static_cast<int>(d), static_cast<int>(F));
+    else
+      prep_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(x), model->b_dec,
+                                                model->log_threshold, w.theta, w.xc, B,
+                                                static_cast<int>(d), static_cast<int>(F));
+    SAE_TRY(check_launch("prep_kernel"));
+  }
+  // 2. encoder GEMM + JumpReLU epilogue
+  {
+    EncodeEpi e{};
+    e.theta = w.theta;
+    e.b_enc = model->b_enc;
+    e.pre = w.pre;
+    e.mask = w.mask;
+    e.tile_cnt = w.tile_cnt;
+    e.n_tokens = static_cast<int>(B);
+    e.n_features = static_cast<int>(F);
+    e.mask_words = mask_words;
+    SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), w.xc, F, B, d, e,
+                             tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_ENCODER_GEMM));
+  }
+  // 3. per-feature scans -> CSR offsets
+  scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(w.tile_cnt, w.col_tot, fired,
+                                                            n_tiles, static_cast<int>(F));
+  SAE_TRY(check_launch("scan_columns_kernel"));
+  scan_offsets_kernel<<<1, 1024, 0, stream>>>(w.col_tot, w.col_offs, static_cast<int>(F),
+                                              cfg->csr_capacity, stats, w.counters);
+  SAE_TRY(check_launch("scan_offsets_kernel"));
+  // 4. gathered decode + residual
+  {
+    const double scale = 1.0 / (static_cast<double>(cfg->accum_steps) * static_cast<double>(B) *
+                                static_cast<double>(d));
+    const int thr = vec_threads(d);
+    if (x_dtype == SAE_DTYPE_BF16)
+      decode_kernel<bf16><<<DECODE_GRID, thr, 0, stream>>>(
+          w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,
+          static_cast<const bf16*>(x), B, static_cast<int>(d), static_cast<int>(F), mask_words,
+          static_cast<float>(scale), w.go, x_hat_out, w.tok_sqerr, w.tok_cnt, w.gosum_part);
+    else
+      decode_kernel<float><<<DECODE_GRID, thr, 0, stream>>>(
+          w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,
+          static_cast<const float*>(x), B, static_cast<int>(d), static_cast<int>(F), mask_words,
+          static_cast<float>(scale), w.go, x_hat_out, w.tok_sqerr, w.tok_cnt, w.gosum_part);
+    SAE_TRY(check_launch("decode_kernel"));
+  }
+  // 5. loss terms
+  forward_stats_kernel<<<1, 1024, 0, stream>>>(w.tok_sqerr, w.tok_cnt, B, static_cast<int>(d),
+                                               cfg->lambda_l0, cfg->al_mu, cfg->target_l0,
+                                               cfg->accum_steps, stats);
+  return check_launch("forward_stats_kernel");
+}
+
+static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
+                           const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                           SaeB200StepStats* stats, bf16* dense_scratch, cudaStream_t stream) {
+  SAE_TRY(check_model(model, true));
+  SAE_TRY(check_cfg(cfg));
+  SAE_TRY(check_fused_shape(model));
+  if (grads == nullptr || stats == nullptr || !grads->W_enc || !grads->b_enc || !grads->b_dec ||
+      !grads->log_threshold)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "gradient pointer is NULL");
+  if (cfg->train_decoder && grads->W_dec_fm == nullptr)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "W_dec gradient is NULL with train_decoder set");
+  const int64_t B = cfg->n_tokens, d = model->d_in, F = model->n_features;
+  const Layout L = make_layout(B, d, F, cfg->csr_capacity);
+  SAE_TRY(check_ws(L, workspace, workspace_bytes));
+  const Ws w = carve(workspace, L);
+  const int n_tiles = static_cast<int>((B + TILE_N - 1) / TILE_N);
+  const int acc = cfg->accumulate ? 1 : 0;
+  float* g_wdec = cfg->train_decoder ? grads->W_dec_fm : nullptr;
+
+  // 1. dense grad_feat GEMM with the STE epilogue (+ CSR fill)
+  {
+    GradEpi e{};
+    e.theta = w.theta;
+    e.pre = w.pre;
+    e.col_offs = w.col_offs;
+    e.tile_base = w.tile_cnt;
+    e.stats = stats;
+    e.eps = cfg->ste_bandwidth;
+    e.n_tokens = static_cast<int>(B);
+    e.n_features = static_cast<int>(F);
+    e.csr_tok = w.csr_tok;
+    e.csr_val = w.csr_val;
+    e.thr_part = w.thr_part;
+    e.dbenc_part = w.dbenc_part;
+    e.dense_dpre = dense_scratch;
+    SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_dec_bf16), w.go, F, B, d, e,
+                             tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_GRAD_GEMM));
+  }
+  // 2. per-feature gradients (threshold STE, b_enc)
+  feature_grads_kernel<<<grid_for(F, 256), 256, 0, stream>>>(
+      w.thr_part, w.dbenc_part, w.theta, n_tiles, static_cast<int>(F), cfg->ste_bandwidth, acc,
+      grads->log_threshold, grads->b_enc, w.db_enc);
+  SAE_TRY(check_launch("feature_grads_kernel"));
+  // 3. b_dec gradient
+  const int thr = vec_threads(d);
+  bdec_gemv_kernel<<<GEMV_GRID, thr, 0, stream>>>(w.db_enc, static_cast<const bf16*>(model->W_enc_bf16),
+                                                  static_cast<int>(F), static_cast<int>(d),
+                                                  w.gemv_part);
+  SAE_TRY(check_launch("bdec_gemv_kernel"));
+  bdec_grad_kernel<<<grid_for(d, 256), 256, 0, stream>>>(w.gosum_part, DECODE_GRID, w.gemv_part,
+                                                         GEMV_GRID, static_cast<int>(d), acc,
+                                                         grads->b_dec);
+  SAE_TRY(check_launch("bdec_grad_kernel"));
+  // 4. weight gradients
+  if (dense_scratch == nullptr) {
+    scatter_weight_grads_kernel<<<device_info().sm_count * 8, thr, 0, stream>>>(
+        w.col_offs, w.csr_tok, w.csr_val, w.go, w.xc, static_cast<int>(F), static_cast<int>(d),
+        acc, g_wdec, grads->W_enc, w.counters, stats);
+    return check_launch("scatter_weight_grads_kernel");
+  }
+  // dense fallback: dW_enc = dpre^T xc, dW_dec = acts^T go
+  {
+    dim3 grid(static_cast<unsigned>((d + GG_T - 1) / GG_T), static_cast<unsigned>((F + GG_T - 1) / GG_T));
+    gemm_generic_kernel<bf16, bf16, float><<<grid, 256, 0, stream>>>(
+        F, d, B, 1.f, dense_scratch, 1, F, w.xc, 1, d, acc ? 1.f : 0.f, grads->W_enc, d, 1,
+        nullptr);
+    SAE_TRY(check_launch("gemm_generic_kernel(dW_enc)"));
+    if (g_wdec != nullptr) {
+      gated_pre_kernel<<<grid_for(B * F, 256), 256, 0, stream>>>(w.pre, w.theta, B, F,
+                                                                 dense_scratch);
+      SAE_TRY(check_launch("gated_pre_kernel"));
+      gemm_generic_kernel<bf16, bf16, float><<<grid, 256, 0, stream>>>(
+          F, d, B, 1.f, dense_scratch, 1, F, w.go, 1, d, acc ? 1.f : 0.f, g_wdec, d, 1, nullptr);
+      SAE_TRY(check_launch("gemm_generic_kernel(dW_dec)"));
+    }
+  }
+  return SAE_OK;
+}
+
+int sae_b200_train_backward(const SaeB200Model* model, const SaeB200Grads* grads,
+                            const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                            SaeB200StepStats* stats, void* stream) {
+  return backward_common(model, grads, cfg, workspace, workspace_bytes, stats, nullptr,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int sae_b200_train_backward_dense(const SaeB200Model* model, const SaeB200Grads* grads,
+                                  const SaeB200StepConfig* cfg, void* workspace,
+                                  size_t workspace_bytes, SaeB200StepStats* stats,
+                                  void* dense_scratch, void* stream) {
+  if (dense_scratch == nullptr || !aligned16(dense_scratch))
+    return fail(SAE_ERR_INVALID_ARGUMENT, "dense_scratch must be a 16-byte aligned buffer");
+  return backward_common(model, grads, cfg, workspace, workspace_bytes, stats,
+                         static_cast<bf16*>(dense_scratch), static_cast<cudaStream_t>(stream));
+}
+
+int sae_b200_grad_norm(const SaeB200Model* model, const SaeB200Grads* grads, float max_norm,
+                       void* workspace, size_t workspace_bytes, SaeB200StepStats* stats,
+                       void* stream_) {
+  SAE_TRY(check_model(model, false));
+  if (grads == nullptr || stats == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (workspace == nullptr || workspace_bytes < NORM_GRID * sizeof(float))
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "grad_norm needs %zu workspace bytes",
+                NORM_GRID * sizeof(float));
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int64_t d = model->d_in, F = model->n_features;
+  GradList gl;
+  gl.p[0] = grads->W_enc;
+  gl.n[0] = F * d;
+  gl.p[1] = grads->b_enc;
+  gl.n[1] = F;
+  gl.p[2] = grads->W_dec_fm;
+  gl.n[2] = F * d;
+  gl.p[3] = grads->b_dec;
+  gl.n[3] = d;
+  gl.p[4] = grads->log_threshold;
+  gl.n[4] = F;
+  for (int k = 0; k < 5; ++k)
+    if (gl.p[k] != nullptr && !aligned16(gl.p[k]))
+      return fail(SAE_ERR_MISALIGNED, "gradient %d must be 16-byte aligned", k);
+  float* part = static_cast<float*>(workspace);
+  grad_sumsq_kernel<<<NORM_GRID, 512, 0, stream>>>(gl, part);
+  SAE_TRY(check_launch("grad_sumsq_kernel"));
+  grad_norm_final_kernel<<<1, 1024, 0, stream>>>(part, NORM_GRID, max_norm, stats);
+  return check_launch("grad_norm_final_kernel");
+}
+
+int sae_b200_adam_step(const SaeB200Model* model, const SaeB200Grads* grads,
+                       const SaeB200AdamState* state, const SaeB200AdamTensor* hyper,
+                       const SaeB200StepStats* stats, void* stream_) {
+  SAE_TRY(check_model(model, false));
+  if (grads == nullptr || state == nullptr || hyper == nullptr)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "NULL argument");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int64_t d = model->d_in, F = model->n_features;
+  float* params[5] = {model->W_enc, model->b_enc, model->W_dec_fm, model->b_dec,
+                      model->log_threshold};
+  const float* gs[5] = {grads->W_enc, grads->b_enc, grads->W_dec_fm, grads->b_dec,
+                        grads->log_threshold};
+  bf16* shadows[5] = {static_cast<bf16*>(model->W_enc_bf16), nullptr,
+                      static_cast<bf16*>(model->W_dec_bf16), nullptr, nullptr};
+  const int64_t rows[5] = {F, F, F, d, F};
+  const int64_t cols[5] = {d, 1, d, 1, 1};
+  for (int k = 0; k < 5; ++k) {
+    const SaeB200AdamTensor& h = hyper[k];
+    if (h.skip) continue;
+    if (gs[k] == nullptr || state->exp_avg[k] == nullptr || state->exp_avg_sq[k] == nullptr)
+      return fail(SAE_ERR_INVALID_ARGUMENT, "tensor %d: gradient or Adam state is NULL", k);
+    if (h.step < 1) return fail(SAE_ERR_INVALID_ARGUMENT, "Adam step must be >= 1");
+    if (h.use_clip && stats == nullptr)
+      return fail(SAE_ERR_INVALID_ARGUMENT, "use_clip needs the stats pointer");
+    AdamScalars s;
+    s.lr = h.lr;
+    s.beta1 = h.beta1;
+    s.beta2 = h.beta2;
+    s.eps = h.eps;
+    s.wd = h.weight_decay;
+    s.grad_scale = h.grad_scale;
+    s.use_clip = h.use_clip;
+    const double bc1 = 1.0 - std::pow(static_cast<double>(h.beta1), h.step);
+    const double bc2 = 1.0 - std::pow(static_cast<double>(h.beta2), h.step);
+    s.step_size = static_cast<float>(h.lr / bc1);
+    s.bc2_sqrt = static_cast<float>(std::sqrt(bc2));
+    const int64_t n = rows[k] * cols[k];
+    const bool row_kernel = cols[k] > 1 && cols[k] % 4 == 0 && cols[k] <= 4096 &&
+                            aligned16(params[k]) && aligned16(gs[k]) &&
+                            aligned16(state->exp_avg[k]) && aligned16(state->exp_avg_sq[k]) &&
+                            (shadows[k] == nullptr || (reinterpret_cast<uintptr_t>(shadows[k]) & 7u) == 0);
+    if (row_kernel) {
+      const int nv_lane = static_cast<int>((cols[k] / 4 + 31) / 32);
+      const int g = grid_for(rows[k] * 32, 256);
+      const int rn = h.renorm_rows ? 1 : 0;
+#define SAE_ADAM_ROWS(MV)                                                                   \
+  adam_rows_kernel<MV><<<g, 256, 0, stream>>>(params[k], gs[k], state->exp_avg[k],           \
+                                              state->exp_avg_sq[k], shadows[k], rows[k],     \
+                                              static_cast<int>(cols[k]), s, stats, rn)
+      if (nv_lane <= 4) SAE_ADAM_ROWS(4);
+      else if (nv_lane <= 8) SAE_ADAM_ROWS(8);
+      else if (nv_lane <= 12) SAE_ADAM_ROWS(12);
+      else if (nv_lane <= 16) SAE_ADAM_ROWS(16);
+      else if (nv_lane <= 24) SAE_ADAM_ROWS(24);
+      else SAE_ADAM_ROWS(32);
+#undef SAE_ADAM_ROWS
+      SAE_TRY(check_launch("adam_rows_kernel"));
+    } else {
+      adam_flat_kernel<<<grid_for(n, 256), 256, 0, stream>>>(params[k], gs[k], state->exp_avg[k],
+                                                             state->exp_avg_sq[k], n, s, stats);
+      SAE_TRY(check_launch("adam_flat_kernel"));
+      if (cols[k] > 1 && h.renorm_rows) {
+        renorm_rows_kernel<<<grid_for(rows[k] * 32, 256), 256, 0, stream>>>(params[k], rows[k],
+                                                                            cols[k], shadows[k]);
+        SAE_TRY(check_launch("renorm_rows_kernel"));
+      } else if (shadows[k] != nullptr) {
+        to_bf16_kernel<<<grid_for(n, 256), 256, 0, stream>>>(params[k], shadows[k], n);
+        SAE_TRY(check_launch("to_bf16_kernel"));
+      }
+    }
+  }
+  return SAE_OK;
+}
+
+int sae_b200_encode_pre(const SaeB200Model* model, const void* x, int x_dtype, int64_t n_tokens,
+                        void* pre_out, int pre_dtype, void* xc_out, int force_simt,
+                        void* workspace, size_t workspace_bytes, void* stream_) {
+  SAE_TRY(check_model(model, pre_dtype == SAE_DTYPE_BF16));
+  if (x == nullptr || pre_out == nullptr || n_tokens <= 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "x/pre_out NULL or n_tokens <= 0");
+  if ((x_dtype != SAE_DTYPE_F32 && x_dtype != SAE_DTYPE_BF16) ||
+      (pre_dtype != SAE_DTYPE_F32 && pre_dtype != SAE_DTYPE_BF16))
+    return fail(SAE_ERR_INVALID_ARGUMENT, "dtype must be F32 or BF16");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int64_t B = n_tokens, d = model->d_in, F = model->n_features;
+  if (pre_dtype == SAE_DTYPE_F32) {
+    if (xc_out == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "fp32 encode_pre needs xc_out");
+    if (x_dtype == SAE_DTYPE_BF16)
+      sub_bias_kernel<bf16, float><<<grid_for(B * d, 256), 256, 0, stream>>>(
+          static_cast<const bf16*>(x), model->b_dec, static_cast<float*>(xc_out), B, d);
+    else
+      sub_bias_kernel<float, float><<<grid_for(B * d, 256), 256, 0, stream>>>(
+          static_cast<const float*>(x), model->b_dec, static_cast<float*>(xc_out), B, d);
+    SAE_TRY(check_launch("sub_bias_kernel"));
+    dim3 grid(static_cast<unsigned>((F + GG_T - 1) / GG_T), static_cast<unsigned>((B + GG_T - 1) / GG_T));
+    gemm_generic_kernel<float, float, float><<<grid, 256, 0, stream>>>(
+        B, F, d, 1.f, static_cast<const float*>(xc_out), d, 1, model->W_enc, d, 1, 0.f,
+        static_cast<float*>(pre_out), F, 1, model->b_enc);
+    return check_launch("gemm_generic_kernel(encode_pre)");
+  }
+  // bf16: xc (bf16) then the tile GEMM with a bias-only epilogue.
+  bf16* xc = static_cast<bf16*>(xc_out);
+  if (xc == nullptr) {
+    const Layout L = make_layout(B, d, F, 0);
+    if (workspace == nullptr || workspace_bytes < L.xc + static_cast<size_t>(B * d * 2))
+      return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "encode_pre needs xc_out or a workspace");
+    xc = carve(workspace, L).xc;
+  }
+  if (d % 8 == 0 && aligned16(x) && aligned16(xc)) {
+    // reuse the step prologue (theta lands in a dummy-free path: no theta needed)
+    if (x_dtype == SAE_DTYPE_BF16)
+      sub_bias_kernel<bf16, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
+          static_cast<const bf16*>(x), model->b_dec, xc, B, d);
+    else
+      sub_bias_kernel<float, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
+          static_cast<const float*>(x), model->b_dec, xc, B, d);
+  } else {
+    if (x_dtype == SAE_DTYPE_BF16)
+      sub_bias_kernel<bf16, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
+          static_cast<const bf16*>(x), model->b_dec, xc, B, d);
+    else
+      sub_bias_kernel<float, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
+          static_cast<const float*>(x), model->b_dec, xc, B, d);
+  }
+  SAE_TRY(check_launch("sub_bias_kernel"));
+  PreOnlyEpi e{};
+  e.b_enc = model->b_enc;
+  e.pre = static_cast<bf16*>(pre_out);
+  e.n_tokens = static_cast<int>(B);
+  e.n_features = static_cast<int>(F);
+  const bool tc = tc_eligible(d, F, force_simt) && aligned16(xc);
+  return launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), xc, F, B, d, e, tc, stream);
+}
+
+int sae_b200_jumprelu_forward(const void* pre, int pre_dtype, const float* log_threshold,
+                              int64_t n_tokens, int64_t n_features, float* feat_out,
+                              float* gate_out, void* stream_) {
+  if (pre == nullptr || log_threshold == nullptr || n_tokens <= 0 || n_features <= 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid jumprelu_forward arguments");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int g = grid_for(n_tokens * n_features, 256);
+  if (pre_dtype == SAE_DTYPE_BF16)
+    jumprelu_fwd_kernel<bf16><<<g, 256, 0, stream>>>(static_cast<const bf16*>(pre), log_threshold,
+                                                     n_tokens, n_features, feat_out, gate_out);
+  else if (pre_dtype == SAE_DTYPE_F32)
+    jumprelu_fwd_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(pre),
+                                                      log_threshold, n_tokens, n_features,
+                                                      feat_out, gate_out);
+  else
+    return fail(SAE_ERR_INVALID_ARGUMENT, "pre_dtype must be F32 or BF16");
+  return check_launch("jumprelu_fwd_kernel");
+}
+
+int sae_b200_jumprelu_backward(const void* pre, int pre_dtype, const float* log_threshold,
+                               int64_t n_tokens, int64_t n_features, const float* grad_feat,
+                               const float* grad_gate, float eps, void* grad_pre_out,
+                               float* grad_log_threshold, void* workspace, size_t workspace_bytes,
+                               void* stream_) {
+  if (pre == nullptr || log_threshold == nullptr || grad_log_threshold == nullptr ||
+      n_tokens <= 0 || n_features <= 0 || !(eps > 0.f))
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid jumprelu_backward arguments");
+  const int64_t slabs = (n_tokens + JB_TOK - 1) / JB_TOK;
+  const size_t need = static_cast<size_t>(slabs * n_features) * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "jumprelu_backward needs %zu workspace bytes", need);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  float* part = static_cast<float*>(workspace);
+  dim3 grid(static_cast<unsigned>((n_features + 31) / 32), static_cast<unsigned>(slabs));
+  if (pre_dtype == SAE_DTYPE_BF16)
+    jumprelu_bwd_kernel<bf16><<<grid, 256, 0, stream>>>(
+        static_cast<const bf16*>(pre), log_threshold, n_tokens, n_features, grad_feat, grad_gate,
+        eps, static_cast<bf16*>(grad_pre_out), part);
+  else if (pre_dtype == SAE_DTYPE_F32)
+    jumprelu_bwd_kernel<float><<<grid, 256, 0, stream>>>(
+        static_cast<const float*>(pre), log_threshold, n_tokens, n_features, grad_feat, grad_gate,
+        eps, static_cast<float*>(grad_pre_out), part);
+  else
+    return fail(SAE_ERR_INVALID_ARGUMENT, "pre_dtype must be F32 or BF16");
+  SAE_TRY(check_launch("jumprelu_bwd_kernel"));
+  jumprelu_bwd_final_kernel<<<grid_for(n_features, 256), 256, 0, stream>>>(
+      part, static_cast<int>(slabs), log_threshold, n_features, eps, grad_log_threshold);
+  return check_launch("jumprelu_bwd_final_kernel");
+}
+
+int sae_b200_gemm(int64_t M, int64_t N, int64_t K, float alpha, const void* A, int a_dtype,
+                  int64_t sam, int64_t sak, const void* B, int b_dtype, int64_t sbn, int64_t sbk,
+                  float beta, void* C, int c_dtype, int64_t scm, int64_t scn, const float* bias_n,
+                  void* stream_) {
+  if (M <= 0 || N <= 0 || K < 0 || A == nullptr || B == nullptr || C == nullptr)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid gemm arguments");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  dim3 grid(static_cast<unsigned>((N + GG_T - 1) / GG_T), static_cast<unsigned>((M + GG_T - 1) / GG_T));
+  if (grid.y > 65535) return fail(SAE_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
+  const int code = a_dtype * 4 + b_dtype * 2 + c_dtype;
+#define SAE_GEMM_CASE(CODE, TA, TB, TC)                                                        \
+  case CODE:                                                                                 \
+    gemm_generic_kernel<TA, TB, TC><<<grid, 256, 0, stream>>>(                               \
+        M, N, K, alpha, static_cast<const TA*>(A), sam, sak, static_cast<const TB*>(B), sbn, \
+        sbk, beta, static_cast<TC*>(C), scm, scn, bias_n);                                   \
+    break;
+  if (a_dtype < 0 || a_dtype > 1 || b_dtype < 0 || b_dtype > 1 || c_dtype < 0 || c_dtype > 1)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "gemm dtype must be F32 or BF16");
+  switch (code) {
+    SAE_GEMM_CASE(0, float, float, float)
+    SAE_GEMM_CASE(1, float, float, bf16)
+    SAE_GEMM_CASE(2, float, bf16, float)
+    SAE_GEMM_CASE(3, float, bf16, bf16)
+    SAE_GEMM_CASE(4, bf16, float, float)
+    SAE_GEMM_CASE(5, bf16, float, bf16)
+    SAE_GEMM_CASE(6, bf16, bf16, float)
+    SAE_GEMM_CASE(7, bf16, bf16, bf16)
+  }
+#undef SAE_GEMM_CASE
+  return check_launch("gemm_generic_kernel");
+}
+
+int sae_b200_column_sum(const void* X, int x_dtype, int64_t rows, int64_t cols, float alpha,
+                        float beta, float* out, void* stream_) {
+  if (X == nullptr || out == nullptr || rows < 0 || cols <= 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid column_sum arguments");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int g = grid_for(cols, 256);
+  if (x_dtype == SAE_DTYPE_BF16)
+    column_sum_kernel<bf16><<<g, 256, 0, stream>>>(static_cast<const bf16*>(X), rows, cols, alpha,
+                                                   beta, out);
+  else if (x_dtype == SAE_DTYPE_F32)
+    column_sum_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(X), rows, cols,
+                                                    alpha, beta, out);
+  else
+    return fail(SAE_ERR_INVALID_ARGUMENT, "x_dtype must be F32 or BF16");
+  return check_launch("column_sum_kernel");
+}
+
+int sae_b200_renorm_rows(float* W, int64_t rows, int64_t cols, void* shadow_bf16, void* stream_) {
+  if (W == nullptr || rows <= 0 || cols <= 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid renorm_rows arguments");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  renorm_rows_kernel<<<grid_for(rows * 32, 256), 256, 0, stream>>>(W, rows, cols,
+                                                                    static_cast<bf16*>(shadow_bf16));
+  return check_launch("renorm_rows_kernel");
+}
+
+int sae_b200_refresh_shadow(const float* src, void* dst_bf16, int64_t n, void* stream_) {
+  if (src == nullptr || dst_bf16 == nullptr || n < 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid refresh_shadow arguments");
+  if (n == 0) return SAE_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  to_bf16_kernel<<<grid_for(n, 256), 256, 0, stream>>>(src, static_cast<bf16*>(dst_bf16), n);
+  return check_launch("to_bf16_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,772 @@
+// Kernels of one fused JumpReLU SAE training step (forward, backward,
+// gradient norm, Adam + renormalisation). The launch order and the buffers
+// they share are set up in capi.cu.
+#pragma once
+#include <cuda_bf16.h>
+#include <cstdint>
+#include "ptx.cuh"
+#include "tile_gemm.cuh"
+
+namespace sae {
+
+using bf16 = __nv_bfloat16;
+
+// Fixed grid sizes: partial sums are reduced in a fixed order, so a given
+// input produces bit-identical results on every run and every B200.
+constexpr int DECODE_GRID = 1184;   // 148 SMs x 8
+constexpr int GEMV_GRID = 296;
+constexpr int NORM_GRID = SAE_GRAD_NORM_WORKSPACE_BYTES / 4;
+constexpr int DECODE_LIST_CAP = 2048;   // active features staged per pass
+
+// ------------------------------------------------------------------ helpers
+__device__ __forceinline__ void unpack8(const uint4 u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const uint32_t l = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return l | (h << 16);
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  u.x = pack2(f[0], f[1]);
+  u.y = pack2(f[2], f[3]);
+  u.z = pack2(f[4], f[5]);
+  u.w = pack2(f[6], f[7]);
+  return u;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum in a fixed order; result valid in every thread.
+__device__ __forceinline__ float block_sum(float v, float* s_tmp) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) s_tmp[wid] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (wid == 0) {
+    t = lane < nw ? s_tmp[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) s_tmp[32] = t;
+  }
+  __syncthreads();
+  return s_tmp[32];
+}
+
+// Block-wide exclusive scan of ints; also returns the block total.
+__device__ __forceinline__ int block_excl_scan(int v, int* s_tmp, int& total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) s_tmp[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int t = lane < nw ? s_tmp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    s_tmp[lane] = t;   // inclusive prefix of warp totals
+  }
+  __syncthreads();
+  total = s_tmp[nw - 1];
+  return (wid > 0 ? s_tmp[wid - 1] : 0) + x - v;
+}
+
+// ---------------------------------------------------------------- prologue
+// theta = exp(log_threshold) (the same expf the reference's CUDA exp uses),
+// xc = bf16(float(x) - b_dec): autocast's cast of the fp32 difference
+// (sae_trainer_rolling.py:586-588).
+template <typename XT>
+__global__ void prep_kernel(const XT* __restrict__ x, const float* __restrict__ b_dec,
+                            const float* __restrict__ log_thr, float* __restrict__ theta,
+                            bf16* __restrict__ xc, int64_t n_tokens, int d, int n_features) {
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t f = tid; f < n_features; f += stride) theta[f] = expf(log_thr[f]);
+  const int64_t nvec = n_tokens * (d / 8);
+  const int dv = d / 8;
+  for (int64_t i = tid; i < nvec; i += stride) {
+    const int c = static_cast<int>(i % dv) * 8;
+    float xv[8];
+    if constexpr (sizeof(XT) == 2) {
+      unpack8(reinterpret_cast<const uint4*>(x)[i], xv);
+    } else {
+      const float4 a = reinterpret_cast<const float4*>(x)[2 * i];
+      const float4 b = reinterpret_cast<const float4*>(x)[2 * i + 1];
+      xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+      xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+    }
+    float r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __fsub_rn(xv[j], b_dec[c + j]);
+    reinterpret_cast<uint4*>(xc)[i] = pack8(r);
+  }
+}
+
+// -------------------------------------------------- encoder tile epilogue
+// pre = bf16(acc + bf16(b_enc)) (cuBLAS addmm with a bf16 bias); gate bit =
+// float(pre) > theta. Stores pre, one 32-feature mask word per token per
+// warp, and the active-token count of each feature in this 256-token tile.
+struct EncodeEpi {
+  const float* theta;
+  const float* b_enc;
+  bf16* pre;
+  uint32_t* mask;
+  int* tile_cnt;
+  int n_tokens, n_features, mask_words;
+  // per-thread tile state
+  int f, n0, lane, word;
+  float th, bias;
+  int cnt;
+  bool row_ok;
+
+  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int row, int q, int ln) {
+    f = m_tile * TILE_M + row;
+    n0 = n_tile * TILE_N;
+    lane = ln;
+    row_ok = f < n_features;
+    th = row_ok ? theta[f] : __int_as_float(0x7f800000);
+    bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
+    word = (m_tile * TILE_M + q * 32) >> 5;
+    cnt = 0;
+  }
+  __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
+    uint32_t myword = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = n0 + c + j;
+      const bool ok = row_ok && t < n_tokens;
+      const bf16 p = __float2bfloat16_rn(v[j] + bias);
+      if (ok) pre[static_cast<size_t>(t) * n_features + f] = p;
+      const bool act = ok && (__bfloat162float(p) > th);
+      const uint32_t bal = __ballot_sync(0xffffffffu, act);
+      if (lane == j) myword = bal;
+      cnt += act ? 1 : 0;
+    }
+    const int t = n0 + c + lane;
+    if (t < n_tokens && word < mask_words)
+      mask[static_cast<size_t>(t) * mask_words + word] = myword;
+  }
+  __device__ __forceinline__ void end_tile() {
+    if (row_ok) tile_cnt[static_cast<size_t>(n0 / TILE_N) * n_features + f] = cnt;
+  }
+};
+
+// pre only (module API encode_pre in bf16 mode).
+struct PreOnlyEpi {
+  const float* b_enc;
+  bf16* pre;
+  int n_tokens, n_features;
+  int f, n0;
+  float bias;
+  bool row_ok;
+  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int row, int, int) {
+    f = m_tile * TILE_M + row;
+    n0 = n_tile * TILE_N;
+    row_ok = f < n_features;
+    bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
+  }
+  __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = n0 + c + j;
+      if (row_ok && t < n_tokens)
+        pre[static_cast<size_t>(t) * n_features + f] = __float2bfloat16_rn(v[j] + bias);
+    }
+  }
+  __device__ __forceinline__ void end_tile() {}
+};
+
+// ------------------------------------------------- backward tile epilogue
+// acc = go . W_dec[f] is the dense grad_feat (bf16 GEMM output in the
+// reference, 643). Per (token, feature):
+//   combined = pre * grad_feat + gate_grad                   (hook, 805-817)
+//   STE sum  += combined   where |pre - theta| < eps          (818-825)
+//   dpre      = grad_feat  where pre > theta                   (grad_pre, gated)
+// The per-feature sums of this tile go to thr_part / dbenc_part; active
+// pairs are appended to the feature-major CSR (token, pre, dpre) at the
+// positions the scan assigned, in token order.
+struct GradEpi {
+  const float* theta;
+  const bf16* pre;
+  const int* col_offs;
+  const int* tile_base;
+  const SaeB200StepStats* stats;
+  float eps;
+  int n_tokens, n_features;
+  int* csr_tok;
+  uint32_t* csr_val;
+  float* thr_part;
+  float* dbenc_part;
+  bf16* dense_dpre;   // non-null: write the gated gradient densely instead of the CSR
+  // per-thread tile state
+  int f, n0, pos;
+  float th, gate_grad, thr_sum, db_sum;
+  bool row_ok, write_csr;
+
+  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int row, int, int) {
+    f = m_tile * TILE_M + row;
+    n0 = n_tile * TILE_N;
+    row_ok = f < n_features;
+    th = row_ok ? theta[f] : 0.f;
+    gate_grad = stats->gate_grad;
+    write_csr = (dense_dpre == nullptr) && (stats->csr_overflow == 0);
+    pos = (row_ok && write_csr)
+              ? col_offs[f] + tile_base[static_cast<size_t>(n_tile) * n_features + f]
+              : 0;
+    thr_sum = 0.f;
+    db_sum = 0.f;
+  }
+  __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
+    if (!row_ok) return;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+      const int t = n0 + c + j;
+      if (t >= n_tokens) break;
+      const float gf = bf16_round(v[j]);
+      const float p = __bfloat162float(pre[static_cast<size_t>(t) * n_features + f]);
+      const float comb = __fadd_rn(__fmul_rn(p, gf), gate_grad);
+      if (fabsf(__fsub_rn(p, th)) < eps) thr_sum += comb;
+      const bool act = p > th;
+      if (dense_dpre != nullptr)
+        dense_dpre[static_cast<size_t>(t) * n_features + f] = __float2bfloat16_rn(act ? gf : 0.f);
+      if (act) {
+        db_sum += gf;
+        if (write_csr) {
+          csr_tok[pos] = t;
+          csr_val[pos] = pack2(p, gf);
+        }
+        ++pos;
+      }
+    }
+  }
+  __device__ __forceinline__ void end_tile() {
+    if (!row_ok) return;
+    const size_t i = static_cast<size_t>(n0 / TILE_N) * n_features + f;
+    thr_part[i] = thr_sum;
+    dbenc_part[i] = db_sum;
+  }
+};
+
+// ------------------------------------------------------------------- scans
+// Per feature: exclusive prefix of the per-tile active counts (in place),
+// the feature's total, and the OR-accumulated fired flag.
+__global__ void scan_columns_kernel(int* __restrict__ tile_cnt, int* __restrict__ col_tot,
+                                    uint8_t* __restrict__ fired, int n_tiles, int n_features) {
+  for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < n_features;
+       f += gridDim.x * blockDim.x) {
+    int run = 0;
+    for (int t = 0; t < n_tiles; ++t) {
+      const size_t i = static_cast<size_t>(t) * n_features + f;
+      const int v = tile_cnt[i];
+      tile_cnt[i] = run;
+      run += v;
+    }
+    col_tot[f] = run;
+    if (fired != nullptr && run > 0) fired[f] = 1;
+  }
+}
+
+// Exclusive scan of the per-feature totals into CSR row offsets (one block).
+__global__ void __launch_bounds__(1024)
+    scan_offsets_kernel(const int* __restrict__ col_tot, int* __restrict__ col_offs, int n_features,
+                        int64_t capacity, SaeB200StepStats* stats, int* counters) {
+  __shared__ int s_tmp[33];
+  const int per = (n_features + blockDim.x - 1) / blockDim.x;
+  const int b = threadIdx.x * per;
+  const int e = min(n_features, b + per);
+  int local = 0;
+  for (int i = b; i < e; ++i) local += col_tot[i];
+  int total = 0;
+  int run = block_excl_scan(local, s_tmp, total);
+  for (int i = b; i < e; ++i) {
+    col_offs[i] = run;
+    run += col_tot[i];
+  }
+  if (threadIdx.x == 0) {
+    col_offs[n_features] = total;
+    stats->nnz = total;
+    stats->csr_overflow = (static_cast<int64_t>(total) > capacity) ? 1 : 0;
+    counters[0] = 0;
+  }
+}
+
+// ------------------------------------------------------------------ decode
+// One block per token (grid-stride), d/8 threads each owning 8 columns.
+// Extracts the token's active features from its mask row in feature order,
+// gathers their bf16 decoder rows with 128-bit loads and accumulates in fp32.
+// Then x_hat = bf16(sum) + b_dec (the reference's bf16 GEMM output plus the
+// fp32 bias, 924), r = x - x_hat, squared error per token, and the loss
+// gradient go = -(scale * 2r) stored as bf16 (what the decoder GEMMs see).
+template <typename XT>
+__global__ void __launch_bounds__(1024)
+    decode_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
+                  const bf16* __restrict__ w_dec, const float* __restrict__ b_dec,
+                  const XT* __restrict__ x, int64_t n_tokens, int d, int n_features,
+                  int mask_words, float go_scale, bf16* __restrict__ go,
+                  float* __restrict__ x_hat, float* __restrict__ tok_sqerr,
+                  int* __restrict__ tok_cnt, float* __restrict__ gosum_part) {
+  __shared__ int s_f[DECODE_LIST_CAP];
+  __shared__ float s_v[DECODE_LIST_CAP];
+  __shared__ int s_itmp[33];
+  __shared__ float s_ftmp[33];
+  const int tid = threadIdx.x;
+  const int nvec = d / 8;
+  const bool has = tid < nvec;
+  const int wpt = (mask_words + blockDim.x - 1) / blockDim.x;
+  const int w0 = min(mask_words, tid * wpt);
+  const int w1 = min(mask_words, w0 + wpt);
+
+  float gsum[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) gsum[j] = 0.f;
+
+  for (int64_t b = blockIdx.x; b < n_tokens; b += gridDim.x) {
+    const uint32_t* mrow = mask + b * mask_words;
+    int mine = 0;
+    for (int w = w0; w < w1; ++w) mine += __popc(mrow[w]);
+    int total = 0;
+    const int my_off = block_excl_scan(mine, s_itmp, total);
+
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+
+    for (int win = 0; win < total; win += DECODE_LIST_CAP) {
+      __syncthreads();
+      if (my_off < win + DECODE_LIST_CAP && my_off + mine > win) {
+        int rank = my_off;
+        for (int w = w0; w < w1; ++w) {
+          uint32_t bits = mrow[w];
+          while (bits) {
+            const int bit = __ffs(bits) - 1;
+            bits &= bits - 1;
+            if (rank >= win && rank < win + DECODE_LIST_CAP) {
+              const int f = w * 32 + bit;
+              s_f[rank - win] = f;
+              s_v[rank - win] = __bfloat162float(pre[b * n_features + f]);
+            }
+            ++rank;
+          }
+        }
+      }
+      __syncthreads();
+      const int n = min(DECODE_LIST_CAP, total - win);
+      if (has) {
+        const uint4* wcol = reinterpret_cast<const uint4*>(w_dec) + tid;
+        int i = 0;
+        for (; i + 4 <= n; i += 4) {
+          uint4 u[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r]) * nvec);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            float wf[8];
+            unpack8(u[r], wf);
+            const float a = s_v[i + r];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+          }
+        }
+        for (; i < n; ++i) {
+          float wf[8];
+          unpack8(__ldg(wcol + static_cast<size_t>(s_f[i]) * nvec), wf);
+          const float a = s_v[i];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+        }
+      }
+    }
+
+    float sq = 0.f;
+    if (has) {
+      float xv[8];
+      const size_t base = static_cast<size_t>(b) * d + tid * 8;
+      if constexpr (sizeof(XT) == 2) {
+        unpack8(*reinterpret_cast<const uint4*>(x + base), xv);
+      } else {
+        const float4 a = *reinterpret_cast<const float4*>(x + base);
+        const float4 c = *reinterpret_cast<const float4*>(x + base + 4);
+        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+        xv[4] = c.x; xv[5] = c.y; xv[6] = c.z; xv[7] = c.w;
+      }
+      float g[8], xh[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        xh[j] = __fadd_rn(bf16_round(acc[j]), b_dec[tid * 8 + j]);
+        const float r = __fsub_rn(xv[j], xh[j]);
+        sq = fmaf(r, r, sq);
+        g[j] = -__fmul_rn(go_scale, __fadd_rn(r, r));
+        gsum[j] += g[j];
+      }
+      *reinterpret_cast<uint4*>(go + base) = pack8(g);
+      if (x_hat != nullptr) {
+        *reinterpret_cast<float4*>(x_hat + base) = make_float4(xh[0], xh[1], xh[2], xh[3]);
+        *reinterpret_cast<float4*>(x_hat + base + 4) = make_float4(xh[4], xh[5], xh[6], xh[7]);
+      }
+    }
+    const float tot_sq = block_sum(sq, s_ftmp);
+    if (tid == 0) {
+      tok_sqerr[b] = tot_sq;
+      tok_cnt[b] = total;
+    }
+  }
+  if (has) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) gosum_part[static_cast<size_t>(blockIdx.x) * d + tid * 8 + j] = gsum[j];
+  }
+}
+
+// Loss terms of the microbatch and the sparsity gradient reaching each gate
+// element (2963-2974): slack = max(0, l0 - target),
+// d sparsity / d gate = (lambda + mu * slack) / accum / B where l0 >= target
+// (torch.clamp passes the gradient at the boundary).
+__global__ void __launch_bounds__(1024)
+    forward_stats_kernel(const float* __restrict__ tok_sqerr, const int* __restrict__ tok_cnt,
+                         int64_t n_tokens, int d, float lambda_l0, float al_mu, float target,
+                         int accum, SaeB200StepStats* stats) {
+  __shared__ float s_tmp[33];
+  __shared__ unsigned long long s_cnt;
+  if (threadIdx.x == 0) s_cnt = 0;
+  float sq = 0.f;
+  unsigned long long cnt = 0;
+  for (int64_t i = threadIdx.x; i < n_tokens; i += blockDim.x) {
+    sq += tok_sqerr[i];
+    cnt += static_cast<unsigned long long>(tok_cnt[i]);
+  }
+  const float total_sq = block_sum(sq, s_tmp);
+  atomicAdd(&s_cnt, cnt);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const float inv_accum = 1.0f / static_cast<float>(accum);
+    const float recon = (total_sq / static_cast<float>(static_cast<double>(n_tokens) * d)) * inv_accum;
+    const float l0 = static_cast<float>(s_cnt) / static_cast<float>(n_tokens);
+    const float diff = l0 - target;
+    const float slack = fmaxf(diff, 0.f);
+    const float sparsity = (lambda_l0 * slack + 0.5f * al_mu * slack * slack) * inv_accum;
+    const float ggrad =
+        diff >= 0.f ? ((lambda_l0 + al_mu * slack) * inv_accum) / static_cast<float>(n_tokens) : 0.f;
+    stats->recon_loss = recon;
+    stats->l0 = l0;
+    stats->sparsity_loss = sparsity;
+    stats->gate_grad = ggrad;
+    stats->loss = recon + sparsity;
+  }
+}
+
+// ------------------------------------------------------- backward reductions
+// Per feature: the threshold STE gradient -(sum / (2 eps)) * theta and the
+// encoder-bias gradient (column sum of the gated grad_feat, 597-600).
+__global__ void feature_grads_kernel(const float* __restrict__ thr_part,
+                                     const float* __restrict__ dbenc_part,
+                                     const float* __restrict__ theta, int n_tiles, int n_features,
+                                     float eps, int accumulate, float* __restrict__ g_logthr,
+                                     float* __restrict__ g_benc, float* __restrict__ db_enc) {
+  for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < n_features;
+       f += gridDim.x * blockDim.x) {
+    float thr = 0.f, db = 0.f;
+    for (int t = 0; t < n_tiles; ++t) {
+      const size_t i = static_cast<size_t>(t) * n_features + f;
+      thr += thr_part[i];
+      db += dbenc_part[i];
+    }
+    const float g = -(thr / (eps + eps)) * theta[f];
+    g_logthr[f] = accumulate ? g_logthr[f] + g : g;
+    g_benc[f] = accumulate ? g_benc[f] + db : db;
+    db_enc[f] = db;
+  }
+}
+
+// Partial GEMV for the reassociated b_dec gradient -(sum_b dpre) W_enc (601).
+__global__ void __launch_bounds__(1024)
+    bdec_gemv_kernel(const float* __restrict__ db_enc, const bf16* __restrict__ w_enc,
+                     int n_features, int d, float* __restrict__ part) {
+  const int nvec = d / 8;
+  const int tid = threadIdx.x;
+  if (tid >= nvec) return;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  const uint4* wv = reinterpret_cast<const uint4*>(w_enc) + tid;
+  for (int f = blockIdx.x; f < n_features; f += gridDim.x) {
+    const float s = db_enc[f];
+    if (s == 0.f) continue;
+    float wf[8];
+    unpack8(__ldg(wv + static_cast<size_t>(f) * nvec), wf);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = fmaf(s, wf[j], acc[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) part[static_cast<size_t>(blockIdx.x) * d + tid * 8 + j] = acc[j];
+}
+
+// b_dec gradient: sum_b go (the fp32 gradient through "+ b_dec", 924) minus
+// the reassociated encoder term.
+__global__ void bdec_grad_kernel(const float* __restrict__ gosum_part, int n_go,
+                                 const float* __restrict__ gemv_part, int n_gemv, int d,
+                                 int accumulate, float* __restrict__ g_bdec) {
+  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < d; k += gridDim.x * blockDim.x) {
+    float s1 = 0.f, s2 = 0.f;
+    for (int i = 0; i < n_go; ++i) s1 += gosum_part[static_cast<size_t>(i) * d + k];
+    for (int i = 0; i < n_gemv; ++i) s2 += gemv_part[static_cast<size_t>(i) * d + k];
+    const float g = s1 - s2;
+    g_bdec[k] = accumulate ? g_bdec[k] + g : g;
+  }
+}
+
+// Sparse decoder / encoder weight gradients over the feature-major CSR:
+//   dW_dec[f] = sum_{(t,f) active} pre[t,f] * go[t]     (index_add_, 645-652)
+//   dW_enc[f] = sum_{(t,f) active} dpre[t,f] * xc[t]    (dpre^T xc, 599)
+// Blocks take features from a global counter; each feature is summed by
+// one block in CSR (token) order, so the result does not depend on timing.
+__global__ void __launch_bounds__(1024)
+    scatter_weight_grads_kernel(const int* __restrict__ col_offs, const int* __restrict__ csr_tok,
+                                const uint32_t* __restrict__ csr_val, const bf16* __restrict__ go,
+                                const bf16* __restrict__ xc, int n_features, int d,
+                                int accumulate, float* __restrict__ g_wdec,
+                                float* __restrict__ g_wenc, int* __restrict__ counter,
+                                const SaeB200StepStats* stats) {
+  if (stats->csr_overflow) return;
+  __shared__ int s_f[2];
+  const int tid = threadIdx.x;
+  const int nvec = d / 8;
+  const bool has = tid < nvec;
+  const uint4* go_v = reinterpret_cast<const uint4*>(go) + tid;
+  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + tid;
+  int it = 0;
+  while (true) {
+    if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
+    __syncthreads();
+    const int f = s_f[it & 1];
+    ++it;
+    if (f >= n_features) break;
+    const int s = col_offs[f], e = col_offs[f + 1];
+    float ad[8], ae[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ad[j] = ae[j] = 0.f;
+    if (has) {
+      int i = s;
+      for (; i + 2 <= e; i += 2) {
+        const int t0 = csr_tok[i], t1 = csr_tok[i + 1];
+        const uint32_t v0 = csr_val[i], v1 = csr_val[i + 1];
+        const uint4 g0 = __ldg(go_v + static_cast<size_t>(t0) * nvec);
+        const uint4 x0 = __ldg(xc_v + static_cast<size_t>(t0) * nvec);
+        const uint4 g1 = __ldg(go_v + static_cast<size_t>(t1) * nvec);
+        const uint4 x1 = __ldg(xc_v + static_cast<size_t>(t1) * nvec);
+        float gf[8], xf[8];
+        float a = __uint_as_float(v0 << 16), q = __uint_as_float(v0 & 0xFFFF0000u);
+        unpack8(g0, gf);
+        unpack8(x0, xf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          ad[j] = fmaf(a, gf[j], ad[j]);
+          ae[j] = fmaf(q, xf[j], ae[j]);
+        }
+        a = __uint_as_float(v1 << 16);
+        q = __uint_as_float(v1 & 0xFFFF0000u);
+        unpack8(g1, gf);
+        unpack8(x1, xf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          ad[j] = fmaf(a, gf[j], ad[j]);
+          ae[j] = fmaf(q, xf[j], ae[j]);
+        }
+      }
+      for (; i < e; ++i) {
+        const int t0 = csr_tok[i];
+        const uint32_t v0 = csr_val[i];
+        float gf[8], xf[8];
+        unpack8(__ldg(go_v + static_cast<size_t>(t0) * nvec), gf);
+        unpack8(__ldg(xc_v + static_cast<size_t>(t0) * nvec), xf);
+        const float a = __uint_as_float(v0 << 16), q = __uint_as_float(v0 & 0xFFFF0000u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          ad[j] = fmaf(a, gf[j], ad[j]);
+          ae[j] = fmaf(q, xf[j], ae[j]);
+        }
+      }
+      const size_t o = static_cast<size_t>(f) * d + tid * 8;
+      if (g_wdec != nullptr) {
+        float4* p = reinterpret_cast<float4*>(g_wdec + o);
+        if (accumulate) {
+          const float4 u = p[0], w = p[1];
+          ad[0] += u.x; ad[1] += u.y; ad[2] += u.z; ad[3] += u.w;
+          ad[4] += w.x; ad[5] += w.y; ad[6] += w.z; ad[7] += w.w;
+        }
+        p[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
+        p[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
+      }
+      float4* p = reinterpret_cast<float4*>(g_wenc + o);
+      if (accumulate) {
+        const float4 u = p[0], w = p[1];
+        ae[0] += u.x; ae[1] += u.y; ae[2] += u.z; ae[3] += u.w;
+        ae[4] += w.x; ae[5] += w.y; ae[6] += w.z; ae[7] += w.w;
+      }
+      p[0] = make_float4(ae[0], ae[1], ae[2], ae[3]);
+      p[1] = make_float4(ae[4], ae[5], ae[6], ae[7]);
+    }
+  }
+}
+
+// ------------------------------------------------------------ grad norm
+struct GradList {
+  const float* p[5];
+  int64_t n[5];
+};
+
+__global__ void __launch_bounds__(512)
+    grad_sumsq_kernel(GradList gl, float* __restrict__ part) {
+  __shared__ float s_tmp[33];
+  float acc = 0.f;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int k = 0; k < 5; ++k) {
+    const float* p = gl.p[k];
+    if (p == nullptr) continue;
+    const int64_t n = gl.n[k];
+    const int64_t n4 = n / 4;
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    for (int64_t i = tid; i < n4; i += stride) {
+      const float4 v = p4[i];
+      acc = fmaf(v.x, v.x, acc);
+      acc = fmaf(v.y, v.y, acc);
+      acc = fmaf(v.z, v.z, acc);
+      acc = fmaf(v.w, v.w, acc);
+    }
+    for (int64_t i = n4 * 4 + tid; i < n; i += stride) acc = fmaf(p[i], p[i], acc);
+  }
+  const float s = block_sum(acc, s_tmp);
+  if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+
+__global__ void grad_norm_final_kernel(const float* __restrict__ part, int n_part, float max_norm,
+                                       SaeB200StepStats* stats) {
+  __shared__ float s_tmp[33];
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < n_part; i += blockDim.x) acc += part[i];
+  const float s = block_sum(acc, s_tmp);
+  if (threadIdx.x == 0) {
+    const float norm = sqrtf(s);
+    const float coef = max_norm / (norm + 1e-6f);
+    stats->grad_norm = norm;
+    stats->clip_coef = fminf(coef, 1.0f);
+  }
+}
+
+// -------------------------------------------------------------------- Adam
+struct AdamScalars {
+  float lr, beta1, beta2, eps, wd, grad_scale, step_size, bc2_sqrt;
+  int use_clip;
+};
+
+__device__ __forceinline__ float adam_update(float p, float g, float& m, float& v,
+                                             const AdamScalars& h, float clip) {
+  if (h.use_clip) g = g * clip;
+  if (h.grad_scale != 1.0f) g = g * h.grad_scale;
+  if (h.wd != 0.f) g = g + p * h.wd;
+  m = h.beta1 * m + (1.f - h.beta1) * g;
+  v = h.beta2 * v + (1.f - h.beta2) * g * g;
+  const float denom = sqrtf(v) / h.bc2_sqrt + h.eps;
+  return p - h.step_size * m / denom;
+}
+
+// One warp per row of a [rows, cols] weight (cols % 4 == 0, cols <= 128*MAXV):
+// Adam on the row, optional renormalisation of the updated row to unit L2
+// norm (clamped at 1e-8), fp32 write-back and bf16 copy.
+template <int MAXV>
+__global__ void __launch_bounds__(256)
+    adam_rows_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                     float* __restrict__ v, bf16* __restrict__ shadow, int64_t rows, int cols,
+                     AdamScalars h, const SaeB200StepStats* stats, int renorm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int nv = cols / 4;
+  const float clip = (h.use_clip && stats != nullptr) ? stats->clip_coef : 1.f;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    float4* p4 = reinterpret_cast<float4*>(p + r * cols);
+    const float4* g4 = reinterpret_cast<const float4*>(g + r * cols);
+    float4* m4 = reinterpret_cast<float4*>(m + r * cols);
+    float4* v4 = reinterpret_cast<float4*>(v + r * cols);
+    float4 pr[MAXV];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int idx = lane + 32 * i;
+      if (idx < nv) {
+        float4 pp = p4[idx];
+        const float4 gg = g4[idx];
+        float4 mm = m4[idx], vv = v4[idx];
+        pp.x = adam_update(pp.x, gg.x, mm.x, vv.x, h, clip);
+        pp.y = adam_update(pp.y, gg.y, mm.y, vv.y, h, clip);
+        pp.z = adam_update(pp.z, gg.z, mm.z, vv.z, h, clip);
+        pp.w = adam_update(pp.w, gg.w, mm.w, vv.w, h, clip);
+        m4[idx] = mm;
+        v4[idx] = vv;
+        pr[i] = pp;
+        ss += pp.x * pp.x + pp.y * pp.y + pp.z * pp.z + pp.w * pp.w;
+      }
+    }
+    float nrm = 1.f;
+    if (renorm) nrm = fmaxf(sqrtf(warp_sum(ss)), 1e-8f);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int idx = lane + 32 * i;
+      if (idx < nv) {
+        float4 pp = pr[i];
+        if (renorm) {
+          pp.x = __fdiv_rn(pp.x, nrm);
+          pp.y = __fdiv_rn(pp.y, nrm);
+          pp.z = __fdiv_rn(pp.z, nrm);
+          pp.w = __fdiv_rn(pp.w, nrm);
+        }
+        p4[idx] = pp;
+        if (shadow != nullptr) {
+          uint2 u;
+          u.x = pack2(pp.x, pp.y);
+          u.y = pack2(pp.z, pp.w);
+          reinterpret_cast<uint2*>(shadow + r * cols)[idx] = u;
+        }
+      }
+    }
+  }
+}
+
+// Elementwise Adam for the vectors (b_enc, b_dec, log_threshold) and for
+// weights too wide for the row kernel.
+__global__ void adam_flat_kernel(float* __restrict__ p, const float* __restrict__ g,
+                                 float* __restrict__ m, float* __restrict__ v, int64_t n,
+                                 AdamScalars h, const SaeB200StepStats* stats) {
+  const float clip = (h.use_clip && stats != nullptr) ? stats->clip_coef : 1.f;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float mm = m[i], vv = v[i];
+    p[i] = adam_update(p[i], g[i], mm, vv, h, clip);
+    m[i] = mm;
+    v[i] = vv;
+  }
+}
+
+}  // namespace sae

@@ -1,0 +1,274 @@
+// Feature-by-token tile GEMM with a pluggable epilogue.
+//
+//   D[f, t] = sum_k W[f, k] * T[t, k]        W: [F, d] bf16, T: [B, d] bf16
+//
+// Rows of D are dictionary features, columns are tokens. Both operands are
+// K-major (d contiguous), which is the natural layout of W_enc [F, d], of the
+// feature-major decoder [F, d] and of the token batches [B, d]. With features
+// on the TMEM lanes, every per-feature reduction an epilogue needs (threshold
+// STE sums, encoder-bias gradient, per-tile active counts) stays inside one
+// thread, and per-token quantities fall out of warp ballots.
+//
+// Two mainloops produce the same 128 x 256 tiles and call the same epilogue:
+//   * tc_tile_gemm: persistent, warp-specialised tcgen05 kernel. TMA (no
+//     multicast) streams 128x64 / 256x64 bf16 slabs through a 4-stage
+//     mbarrier ring; one thread issues tcgen05.mma into a double-buffered
+//     TMEM accumulator (2 x 256 columns); four epilogue warps drain the
+//     other accumulator with tcgen05.ld while the next tile accumulates.
+//   * simt_tile_gemm: plain CUDA-core kernel with full predication, for
+//     shapes TMA cannot describe (d not a multiple of 64, F not a multiple
+//     of 128) and for small problems.
+#pragma once
+#include <cuda.h>
+#include "ptx.cuh"
+
+namespace sae {
+
+constexpr int TILE_M = 128;   // features per tile (TMEM lanes)
+constexpr int TILE_N = 256;   // tokens per tile (TMEM columns per accumulator)
+constexpr int TILE_K = 64;    // d per pipeline stage (one 128-byte swizzle row)
+constexpr int TC_STAGES = 4;
+constexpr int TC_A_BYTES = TILE_M * TILE_K * 2;   // 16 KiB
+constexpr int TC_B_BYTES = TILE_N * TILE_K * 2;   // 32 KiB
+constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
+constexpr int TC_THREADS = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr int TC_GROUP_M = 16;    // feature tiles per rasterisation group
+constexpr int TC_BARRIER_BYTES = 256;
+constexpr size_t TC_SMEM_BYTES = TC_STAGES * TC_STAGE_BYTES + TC_BARRIER_BYTES + 1024;
+constexpr uint32_t TC_TMEM_COLS = 2 * TILE_N;     // two fp32 accumulators
+
+struct TileCoord {
+  int m, n;
+};
+
+// Tiles are visited in groups of TC_GROUP_M feature tiles; inside a group the
+// feature tile varies fastest, so the CTAs running at any moment share a few
+// token slabs and a few weight slabs in L2.
+__device__ __forceinline__ TileCoord tile_coord(int t, int m_tiles, int n_tiles) {
+  const int per_group = TC_GROUP_M * n_tiles;
+  const int g = t / per_group;
+  const int r = t - g * per_group;
+  const int m0 = g * TC_GROUP_M;
+  const int gm = min(TC_GROUP_M, m_tiles - m0);
+  TileCoord c;
+  c.m = m0 + r % gm;
+  c.n = r / gm;
+  return c;
+}
+
+// Epilogue contract (Epi):
+//   begin_tile(m_tile, n_tile, row, quarter, lane)   row = feature within tile
+//   chunk(col, v[32])   v[j] = D[row, col + j], col in {0, 32, ..., 224};
+//                       called by all 32 lanes of a warp together (ballots)
+//   end_tile()
+template <class Epi>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_tile_gemm(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_t,
+                 int m_tiles, int n_tiles, int k_blocks, const Epi epi) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + TC_STAGES * TC_A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + TC_STAGES;
+  uint64_t* acc_full = bars + 2 * TC_STAGES;
+  uint64_t* acc_empty = bars + 2 * TC_STAGES + 2;
+  uint64_t* drain = bars + 2 * TC_STAGES + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * TC_STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);   // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TC_TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_t);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int total = m_tiles * n_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      uint32_t issued = 0, issued_parity = 0;
+      bool ok = true;
+      int kit = 0;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const TileCoord tc = tile_coord(t, m_tiles, n_tiles);
+        for (int kb = 0; kb < k_blocks; ++kb, ++kit) {
+          const int s = kit % TC_STAGES;
+          const uint32_t ph = (kit / TC_STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], TC_STAGE_BYTES);
+          tma_load_2d(s_a + s * TC_A_BYTES, &tm_w, &full[s], kb * TILE_K, tc.m * TILE_M);
+          tma_load_2d(s_b + s * TC_B_BYTES, &tm_t, &full[s], kb * TILE_K, tc.n * TILE_N);
+          issued |= 1u << s;
+          issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
+        }
+      }
+      if (!ok) {
+        // Unwinding: let every copy this thread started land before the CTA
+        // (and its shared memory) goes away.
+        for (int s = 0; s < TC_STAGES; ++s)
+          if ((issued >> s) & 1u) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // --------------------------------------------------------- MMA issue
+      constexpr uint32_t idesc = idesc_bf16_f32(TILE_M, TILE_N);
+      bool ok = true, any_mma = false;
+      int kit = 0, it = 0;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], aph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TILE_N);
+        for (int kb = 0; kb < k_blocks; ++kb, ++kit) {
+          const int s = kit % TC_STAGES;
+          const uint32_t ph = (kit / TC_STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = smem_desc_k_sw128(s_a + s * TC_A_BYTES);
+          const uint64_t bdesc = smem_desc_k_sw128(s_b + s * TC_B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < TILE_K / 16; ++kk) {
+            // 16 bf16 = 32 bytes further along the swizzled row: +2 in the
+            // descriptor's 16-byte address units.
+            tc_mma_bf16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          }
+          any_mma = true;
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);
+      }
+      if (!ok && any_mma) {
+        tc_commit(drain);
+        mbar_wait(drain, 0, nullptr);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;   // TMEM lane quarter this warp can address
+    const int row = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], aph, abort_flag)) break;
+      tc_fence_after();
+      const TileCoord tc = tile_coord(t, m_tiles, n_tiles);
+      Epi e = epi;
+      e.begin_tile(tc.m, tc.n, row, q, lane);
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * TILE_N);
+#pragma unroll 1
+      for (int c = 0; c < TILE_N; c += 32) {
+        float v[32];
+        tmem_ld_32cols(t_row + c, v);
+        if (c == TILE_N - 32) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+        e.chunk(c, v);
+      }
+      e.end_tile();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TC_TMEM_COLS);
+  }
+}
+
+// CUDA-core version of the same tile: one thread per feature row, 32 token
+// columns per pass, operands staged through shared memory in 32-wide K slabs.
+// T may be any of bf16 / fp32 through the loader functor below.
+constexpr int SIMT_K = 32;
+
+template <class Epi>
+__global__ void __launch_bounds__(TILE_M)
+    simt_tile_gemm(const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ tok,
+                   int n_rows, int n_cols, int k_dim, const Epi epi) {
+  __shared__ float s_w[TILE_M][SIMT_K + 1];
+  __shared__ float s_t[32][SIMT_K + 1];
+  const int m_tile = blockIdx.y, n_tile = blockIdx.x;
+  const int row = threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int q = threadIdx.x >> 5;
+  const int f = m_tile * TILE_M + row;
+
+  Epi e = epi;
+  e.begin_tile(m_tile, n_tile, row, q, lane);
+  for (int c = 0; c < TILE_N; c += 32) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    for (int k0 = 0; k0 < k_dim; k0 += SIMT_K) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < TILE_M * SIMT_K; i += TILE_M) {
+        const int r = i / SIMT_K, kk = i % SIMT_K;
+        const int gf = m_tile * TILE_M + r, gk = k0 + kk;
+        s_w[r][kk] = (gf < n_rows && gk < k_dim)
+                         ? __bfloat162float(w[static_cast<size_t>(gf) * k_dim + gk])
+                         : 0.f;
+      }
+      for (int i = threadIdx.x; i < 32 * SIMT_K; i += TILE_M) {
+        const int r = i / SIMT_K, kk = i % SIMT_K;
+        const int gt = n_tile * TILE_N + c + r, gk = k0 + kk;
+        s_t[r][kk] = (gt < n_cols && gk < k_dim)
+                         ? __bfloat162float(tok[static_cast<size_t>(gt) * k_dim + gk])
+                         : 0.f;
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int kk = 0; kk < SIMT_K; ++kk) {
+        const float a = s_w[row][kk];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaf(a, s_t[j][kk], v[j]);
+      }
+    }
+    (void)f;
+    e.chunk(c, v);
+  }
+  e.end_tile();
+}
+
+}  // namespace sae

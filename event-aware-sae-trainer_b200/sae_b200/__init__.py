@@ -1,0 +1,14 @@
+"""B200-native JumpReLU SAE training step (sm_100a CUDA behind a C ABI).
+
+Public API:
+  B200JumpReLUSAE, make_sae, install   -- the reference SAE module's API
+  B200Adam, FusedStep                  -- optimizer and the fused training step
+  superposition_batch                  -- the benchmark's synthetic activations
+"""
+from ._lib import SaeB200Error, load as load_library  # noqa: F401
+from .sae import B200JumpReLUSAE, install, make_sae  # noqa: F401
+from .step import B200Adam, FusedStep, reference_param_groups  # noqa: F401
+from .data import superposition_batch  # noqa: F401
+
+__all__ = ["B200JumpReLUSAE", "make_sae", "install", "B200Adam", "FusedStep",
+           "reference_param_groups", "superposition_batch", "SaeB200Error", "load_library"]

@@ -1,0 +1,317 @@
+"""The training step of the reference loop on libsae_b200.
+
+``B200Adam`` is a ``torch.optim.Optimizer`` with torch Adam's parameter groups,
+hyper-parameter keys (``lr``, ``betas``, ``eps``, ``weight_decay``) and state
+keys (``step``, ``exp_avg``, ``exp_avg_sq``), so the reference scheduler's
+per-step writes to ``group["lr"/"betas"/"weight_decay"]``
+(sae_scheduler.py:726-731, 1601-1620) and the revival code's writes to
+``optimizer.state[p]["exp_avg"][mask]`` (sae_trainer_rolling.py:2803-2810,
+3116-3118) keep working. Its update is classic L2 Adam (torch.optim.Adam with
+weight_decay, not AdamW), one library call for all five tensors.
+
+``FusedStep`` is the loop body of ``train_sae_on_activations``
+(sae_trainer_rolling.py:2840-3090) as a handful of library calls per
+microbatch: encoder GEMM + JumpReLU epilogue, gathered decode + loss,
+grad_feat GEMM + STE epilogue + sparse weight gradients, global gradient norm,
+Adam fused with the decoder-column / encoder-row renormalisation. No [B, F]
+tensor other than the bf16 pre-activations is ever written.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Callable, Optional
+
+import torch
+
+from . import _lib as L
+from .sae import B200JumpReLUSAE, _require_cuda, _stream
+
+PARAM_ORDER = ("W_enc.weight", "W_enc.bias", "W_dec.weight", "b_dec", "log_threshold")
+
+
+def _sae_params(sae: B200JumpReLUSAE):
+    return (sae.W_enc.weight, sae.W_enc.bias, sae.W_dec.weight, sae.b_dec, sae.log_threshold)
+
+
+def reference_param_groups(sae: B200JumpReLUSAE, lr: float, decoder_wd: float = 1e-4):
+    """The trainer's four groups (sae_trainer_rolling.py:2536-2540)."""
+    return [{"params": list(sae.W_enc.parameters()), "weight_decay": 0},
+            {"params": list(sae.W_dec.parameters()), "weight_decay": decoder_wd},
+            {"params": [sae.b_dec], "weight_decay": 0},
+            {"params": [sae.log_threshold], "weight_decay": 0}]
+
+
+class B200Adam(torch.optim.Optimizer):
+    """L2-decay Adam over the five SAE tensors, computed by sae_b200_adam_step.
+
+    ``renorm=True`` fuses the decoder-column and encoder-row renormalisation
+    that the trainer runs right after ``optimizer.step()``
+    (sae_trainer_rolling.py:3086-3090) into the same pass.
+    """
+
+    def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, *,
+                 sae: B200JumpReLUSAE, renorm: bool = False, fused=None, foreach=None):
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        super().__init__(params, defaults)
+        self.sae = sae
+        self.renorm = renorm
+        self._index = {id(p): i for i, p in enumerate(_sae_params(sae))}
+        for group in self.param_groups:
+            for p in group["params"]:
+                if id(p) not in self._index:
+                    raise ValueError("B200Adam only optimises the parameters of its SAE")
+        sae._state_probe = self._state_versions
+
+    def _state_versions(self):
+        out = []
+        for i in (0, 2):
+            p = _sae_params(self.sae)[i]
+            st = self.state.get(p, {})
+            if "exp_avg" in st:
+                out.extend((st["exp_avg"]._version, st["exp_avg_sq"]._version))
+        return out
+
+    def _init_state(self, p):
+        st = self.state[p]
+        if "exp_avg" not in st:
+            st["step"] = torch.tensor(0.0)
+            st["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+        return st
+
+    def load_state_dict(self, state_dict):
+        super().load_state_dict(state_dict)
+        # Loaded state may come from torch.optim.Adam with a [d, F]-contiguous
+        # decoder state; move it to the feature-major layout of W_dec.weight.
+        w_dec = self.sae.W_dec.weight
+        st = self.state.get(w_dec, {})
+        for k in ("exp_avg", "exp_avg_sq"):
+            if k in st and not st[k].t().is_contiguous():
+                st[k] = st[k].t().contiguous().t()
+        for p, s in self.state.items():
+            if "step" in s and torch.is_tensor(s["step"]) and s["step"].is_cuda:
+                s["step"] = s["step"].detach().cpu()
+        self.sae.mark_weights_dirty()
+
+    @torch.no_grad()
+    def step(self, closure=None, *, stats: Optional[torch.Tensor] = None,
+             grad_scale_enc: float = 1.0):
+        """One Adam update. ``stats`` (the device StepStats of a FusedStep)
+        makes the update apply the clip coefficient computed on the device;
+        ``grad_scale_enc`` is the W_enc dampening factor (3069-3074)."""
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        sae = self.sae
+        params = _sae_params(sae)
+        hyper = (L.AdamTensor * 5)()
+        state = L.AdamState()
+        grads = [None] * 5
+        any_update = False
+        for group in self.param_groups:
+            b1, b2 = group["betas"]
+            for p in group["params"]:
+                i = self._index[id(p)]
+                h = hyper[i]
+                if p.grad is None:
+                    h.skip = 1
+                    continue
+                _require_cuda(p, p.grad)
+                st = self._init_state(p)
+                st["step"] += 1
+                g = p.grad
+                if i == 2:
+                    if not g.t().is_contiguous():
+                        g = g.t().contiguous().t()
+                        p.grad = g
+                elif not g.is_contiguous():
+                    g = g.contiguous()
+                grads[i] = g
+                h.lr = float(group["lr"])
+                h.beta1 = float(b1)
+                h.beta2 = float(b2)
+                h.eps = float(group["eps"])
+                h.weight_decay = float(group["weight_decay"])
+                h.grad_scale = float(grad_scale_enc) if i in (0, 1) else 1.0
+                h.step = int(round(float(st["step"])))
+                h.use_clip = 1 if stats is not None else 0
+                h.skip = 0
+                h.renorm_rows = 1 if (self.renorm and i in (0, 2)) else 0
+                state.exp_avg[i] = st["exp_avg"].data_ptr()
+                state.exp_avg_sq[i] = st["exp_avg_sq"].data_ptr()
+                any_update = True
+        for i in range(5):
+            if grads[i] is None:
+                hyper[i].skip = 1
+        if not any_update:
+            return loss
+        model = sae._model_struct(need_shadows=True)
+        g = L.Grads(*(L.ptr(x) for x in grads))
+        L.call("sae_b200_adam_step", ctypes.byref(model), ctypes.byref(g), ctypes.byref(state),
+               hyper, L.ptr(stats), _stream())
+        if hyper[0].skip == 0 and hyper[2].skip == 0:
+            sae._shadows_written()
+        else:
+            sae.mark_weights_dirty()
+        return loss
+
+
+def _csr_capacity_default(tokens: int) -> int:
+    per_token = int(os.environ.get("SAE_B200_CSR_PER_TOKEN", "512"))
+    return max(1024, tokens * per_token)
+
+
+class FusedStep:
+    """Per-microbatch fused forward/backward plus the optimizer step."""
+
+    def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int,
+                 csr_capacity: Optional[int] = None, force_simt: bool = False):
+        _require_cuda(sae.W_enc.weight)
+        if not isinstance(optimizer, B200Adam) or optimizer.sae is not sae:
+            raise TypeError("FusedStep needs the B200Adam built over the same SAE")
+        self.sae = sae
+        self.opt = optimizer
+        self.max_tokens = int(max_tokens)
+        self.csr_capacity = int(csr_capacity or _csr_capacity_default(self.max_tokens))
+        self.force_simt = bool(force_simt)
+        dev = sae.W_enc.weight.device
+        self.device = dev
+        F, d = sae.n_features, sae.d_in
+        self.ws_bytes = L.workspace_bytes(self.max_tokens, d, F, self.csr_capacity)
+        self.ws = torch.empty(self.ws_bytes, device=dev, dtype=torch.uint8)
+        self.stats = torch.zeros(L.STATS_FLOATS, device=dev, dtype=torch.int32)
+        self.norm_ws = torch.empty(L.GRAD_NORM_WORKSPACE_BYTES, device=dev, dtype=torch.uint8)
+        self.fired = torch.zeros(F, device=dev, dtype=torch.uint8)
+        self._dense_scratch = None
+        # Gradient buffers, bound as the parameters' .grad (W_dec's is the
+        # [d, F] view of a feature-major buffer).
+        self.g_W_enc = torch.zeros(F, d, device=dev)
+        self.g_b_enc = torch.zeros(F, device=dev)
+        self.g_W_dec_fm = torch.zeros(F, d, device=dev)
+        self.g_b_dec = torch.zeros(d, device=dev)
+        self.g_log_thr = torch.zeros(F, device=dev)
+        self._host_stats = torch.zeros(L.STATS_FLOATS, dtype=torch.int32).pin_memory() \
+            if torch.cuda.is_available() else None
+        self.nnz_last = 0
+        self.dense_fallbacks = 0
+
+    # ------------------------------------------------------------ pieces
+    def _bind_grads(self):
+        sae = self.sae
+        sae.W_enc.weight.grad = self.g_W_enc
+        sae.W_enc.bias.grad = self.g_b_enc
+        train_dec = sae.W_dec.weight.requires_grad
+        sae.W_dec.weight.grad = self.g_W_dec_fm.t() if train_dec else None
+        sae.b_dec.grad = self.g_b_dec
+        sae.log_threshold.grad = self.g_log_thr
+
+    def _grads_struct(self) -> L.Grads:
+        train_dec = self.sae.W_dec.weight.requires_grad
+        return L.Grads(L.ptr(self.g_W_enc), L.ptr(self.g_b_enc),
+                       L.ptr(self.g_W_dec_fm) if train_dec else 0, L.ptr(self.g_b_dec),
+                       L.ptr(self.g_log_thr))
+
+    def _cfg(self, n_tokens, accum_steps, first, lambda_l0, al_mu, target_l0) -> L.StepConfig:
+        return L.StepConfig(int(n_tokens), self.csr_capacity, float(lambda_l0), float(al_mu),
+                            float(target_l0), float(self.sae.ste_bandwidth), int(accum_steps),
+                            0 if first else 1, 1 if self.sae.W_dec.weight.requires_grad else 0,
+                            1 if self.force_simt else 0)
+
+    def read_stats(self) -> dict:
+        """One device->host copy of the StepStats (synchronises the stream)."""
+        self._host_stats.copy_(self.stats, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        raw = L.StepStats.from_buffer_copy(self._host_stats.numpy().tobytes())
+        return {k: getattr(raw, k) for k in L.STATS_FIELDS}
+
+    def microbatch(self, x: torch.Tensor, *, accum_steps: int = 1, first: bool = True,
+                   lambda_l0: float = 0.0, al_mu: float = 0.0, target_l0: float = 0.0,
+                   x_hat_out: Optional[torch.Tensor] = None) -> dict:
+        """Forward + backward of one microbatch; gradients overwrite (first) or
+        add. Reads the forward statistics back once (this also chooses the
+        sparse or the dense weight-gradient path -- an active set larger than
+        the workspace is never truncated) and returns them."""
+        sae = self.sae
+        _require_cuda(x)
+        if x.dim() != 2 or x.shape[1] != sae.d_in:
+            raise ValueError(f"x must be [tokens, {sae.d_in}]")
+        n = x.shape[0]
+        if n > self.max_tokens:
+            raise ValueError(f"microbatch of {n} tokens exceeds max_tokens={self.max_tokens}")
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            x = x.float()
+        x = x.contiguous()
+        if first:
+            self.fired.zero_()
+        cfg = self._cfg(n, accum_steps, first, lambda_l0, al_mu, target_l0)
+        model = sae._model_struct(need_shadows=True)
+        stream = _stream()
+        L.call("sae_b200_train_forward", ctypes.byref(model), L.ptr(x),
+               L.DTYPE_BF16 if x.dtype == torch.bfloat16 else L.DTYPE_F32, ctypes.byref(cfg),
+               L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), L.ptr(x_hat_out),
+               L.ptr(self.fired), stream)
+        st = self.read_stats()
+        self.nnz_last = st["nnz"]
+        grads = self._grads_struct()
+        if st["csr_overflow"]:
+            self.dense_fallbacks += 1
+            need = n * sae.n_features
+            if self._dense_scratch is None or self._dense_scratch.numel() < need:
+                self._dense_scratch = torch.empty(need, device=self.device, dtype=torch.bfloat16)
+            L.call("sae_b200_train_backward_dense", ctypes.byref(model), ctypes.byref(grads),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
+                   L.ptr(self._dense_scratch), stream)
+        else:
+            sae._sparse_decode_calls += 1
+            L.call("sae_b200_train_backward", ctypes.byref(model), ctypes.byref(grads),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), stream)
+        self._bind_grads()
+        return st
+
+    def grad_norm(self, max_norm: float = 1.0) -> None:
+        """Global L2 norm of all gradients + clip coefficient, on the device."""
+        model = self.sae._model_struct(need_shadows=False)
+        grads = self._grads_struct()
+        L.call("sae_b200_grad_norm", ctypes.byref(model), ctypes.byref(grads), float(max_norm),
+               L.ptr(self.norm_ws), self.norm_ws.numel(), L.ptr(self.stats), _stream())
+
+    def optimizer_step(self, wenc_factor: float = 1.0) -> None:
+        self.opt.step(stats=self.stats, grad_scale_enc=wenc_factor if wenc_factor < 1.0 else 1.0)
+
+    # ---------------------------------------------------------- full step
+    def step(self, batch: torch.Tensor, *, microbatch_tokens: Optional[int] = None,
+             lambda_l0: float = 0.0, al_mu: float = 0.0, target_l0: float = 0.0,
+             max_norm: float = 1.0,
+             wenc_dampen: Optional[Callable[[float], float]] = None) -> dict:
+        """One optimizer step over ``batch`` split into microbatches, in the
+        reference loop's order; returns recon / l0 / grad_norm as floats after
+        the same single stats read-back the loop does before Adam (3064-3066)."""
+        mb = int(microbatch_tokens or batch.shape[0])
+        n = batch.shape[0]
+        if n % mb != 0:
+            raise ValueError("batch tokens must be divisible by microbatch_tokens")
+        accum = n // mb
+        recon = 0.0
+        l0 = 0.0
+        loss = 0.0
+        for i in range(accum):
+            s = self.microbatch(batch[i * mb:(i + 1) * mb], accum_steps=accum, first=(i == 0),
+                                lambda_l0=lambda_l0, al_mu=al_mu, target_l0=target_l0)
+            recon += s["recon_loss"] * accum     # accum_recon_t (3057)
+            l0 += s["l0"]                        # accum_l0_t (3058)
+            loss += s["loss"]
+        self.grad_norm(max_norm)
+        s = self.read_stats()
+        l0_step = l0 / accum
+        factor = 1.0 if wenc_dampen is None else float(wenc_dampen(l0_step))
+        self.optimizer_step(factor)
+        return {"recon_loss": recon / accum, "l0": l0_step, "grad_norm": s["grad_norm"],
+                "clip_coef": s["clip_coef"], "nnz": s["nnz"], "loss": loss,
+                "wenc_factor": factor}
+
+    @property
+    def fired_mask(self) -> torch.Tensor:
+        """Features that fired in this step's microbatches (fired_accum, 3016)."""
+        return self.fired.view(torch.bool)

@@ -1,0 +1,250 @@
+/*
+ * sae_b200.h -- C ABI of the B200 (sm_100a) JumpReLU sparse-autoencoder step.
+ *
+ * The library replaces the per-step SAE compute of the event-aware SAE trainer
+ * (sae_trainer_rolling.py): encoder pre-activation with the JumpReLU gate,
+ * decode + reconstruction loss, the backward pass with the straight-through
+ * threshold estimator, global gradient clipping and the L2-decay Adam step
+ * followed by decoder-column / encoder-row renormalisation.
+ *
+ * Conventions
+ *  - Every pointer in a struct or argument is a DEVICE pointer unless noted.
+ *  - All work is enqueued on the caller's stream; nothing here synchronises
+ *    the device or allocates memory. Scratch comes from a caller-provided
+ *    workspace sized by sae_b200_workspace_bytes().
+ *  - Every entry point returns 0 (SAE_OK) or one of the SAE_ERR_* codes
+ *    below; none throws or aborts. sae_b200_last_error() gives a message.
+ *  - bf16 arrays are passed as void* (IEEE bfloat16, little-endian).
+ *  - The decoder is stored feature-major: W_dec_fm[f, :] is decoder column f
+ *    of the reference's W_dec.weight [d, F] (W_dec.weight == W_dec_fm^T).
+ *
+ * Citations are to the reference project's files (path:line).
+ */
+#ifndef SAE_B200_H
+#define SAE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+#define SAE_OK 0
+#define SAE_ERR_INVALID_ARGUMENT 1   /* null pointer, negative size, bad dtype */
+#define SAE_ERR_UNSUPPORTED_SHAPE 2  /* shape outside what the kernels handle */
+#define SAE_ERR_MISALIGNED 3         /* pointer / stride not 16-byte aligned */
+#define SAE_ERR_WORKSPACE_TOO_SMALL 4
+#define SAE_ERR_CSR_OVERFLOW 5       /* more active pairs than csr_capacity */
+#define SAE_ERR_CUDA 6               /* a CUDA runtime call failed */
+#define SAE_ERR_DEVICE_TIMEOUT 7     /* a bounded device-side wait ran out */
+#define SAE_ERR_NO_DEVICE 8
+
+#define SAE_DTYPE_F32 0
+#define SAE_DTYPE_BF16 1
+
+/* Parameters of one JumpReLU SAE (reference: _JumpReLUSAE.__init__,
+ * sae_trainer_rolling.py:772-800). */
+typedef struct SaeB200Model {
+  int64_t d_in;
+  int64_t n_features;
+  float* W_enc;          /* [F, d]  encoder weight (nn.Linear rows) */
+  float* b_enc;          /* [F]     encoder bias */
+  float* W_dec_fm;       /* [F, d]  decoder, feature-major */
+  float* b_dec;          /* [d]     decoder bias / encoder pre-bias */
+  float* log_threshold;  /* [F] */
+  void* W_enc_bf16;      /* [F, d]  bf16 copy fed to the tensor cores */
+  void* W_dec_bf16;      /* [F, d]  bf16 copy of W_dec_fm */
+} SaeB200Model;
+
+/* Gradients, same shapes and layouts as SaeB200Model's fp32 arrays. */
+typedef struct SaeB200Grads {
+  float* W_enc;
+  float* b_enc;
+  float* W_dec_fm;  /* may be NULL when the decoder is frozen */
+  float* b_dec;
+  float* log_threshold;
+} SaeB200Grads;
+
+/* One microbatch of the training step (reference loop body,
+ * sae_trainer_rolling.py:2914-3016). */
+typedef struct SaeB200StepConfig {
+  int64_t n_tokens;        /* tokens in this microbatch (rows of x) */
+  int64_t csr_capacity;    /* active (token, feature) pairs the workspace holds */
+  float lambda_l0;         /* scheduler.lambda_l0 */
+  float al_mu;             /* sae_cfg.al_mu */
+  float target_l0;         /* sae_cfg.target_l0 */
+  float ste_bandwidth;     /* sae.ste_bandwidth (epsilon of the STE band) */
+  int32_t accum_steps;     /* microbatches per optimizer step */
+  int32_t accumulate;      /* 0: gradients overwrite, 1: gradients add */
+  int32_t train_decoder;   /* 0: frozen decoder (no W_dec gradient) */
+  int32_t force_simt;      /* 1: CUDA-core tile GEMM even where tcgen05 applies */
+} SaeB200StepConfig;
+
+/* Step statistics, written on the device; copy back with one memcpy. */
+typedef struct SaeB200StepStats {
+  float recon_loss;     /* mean((x - x_hat)^2) / accum_steps        (2964-2965) */
+  float l0;             /* mean active features per token            (2958,2969) */
+  float sparsity_loss;  /* (lambda*s + mu/2*s^2)/accum, s = max(0, l0-target) */
+  float gate_grad;      /* d loss / d gate element                             */
+  float loss;           /* recon_loss + sparsity_loss                          */
+  float grad_norm;      /* pre-clip global L2 norm of all gradients   (3049)   */
+  float clip_coef;      /* min(1, max_norm / (grad_norm + 1e-6))               */
+  int32_t nnz;          /* active (token, feature) pairs in this microbatch    */
+  int32_t csr_overflow; /* 1 when nnz > csr_capacity: use the dense backward   */
+  int32_t reserved[7];
+} SaeB200StepStats;
+
+/* Adam hyper-parameters for one parameter tensor. The five tensors are, in
+ * order: W_enc, b_enc, W_dec_fm, b_dec, log_threshold (the reference's four
+ * param groups, sae_trainer_rolling.py:2536-2541, flattened). */
+typedef struct SaeB200AdamTensor {
+  float lr, beta1, beta2, eps, weight_decay;
+  float grad_scale;    /* host factor on the gradient (W_enc dampening, 3069-3074) */
+  int32_t step;        /* Adam step count AFTER this update (>= 1) */
+  int32_t use_clip;    /* 1: also multiply the gradient by stats->clip_coef */
+  int32_t skip;        /* 1: leave this tensor untouched (frozen / no grad) */
+  int32_t renorm_rows; /* 1: renormalise rows to unit L2 norm afterwards */
+} SaeB200AdamTensor;
+
+typedef struct SaeB200AdamState {
+  float* exp_avg[5];
+  float* exp_avg_sq[5];
+} SaeB200AdamState;
+
+/* ----------------------------------------------------------------- basics */
+int sae_b200_version(void);
+const char* sae_b200_last_error(void);
+/* Reads (and optionally clears) the device status word that bounded waits
+ * set when they give up. Synchronises the calling thread with the device. */
+int sae_b200_get_device_status(int* status_out, int clear);
+
+/* Number of kernels this library has launched in the process so far. */
+int64_t sae_b200_launch_count(void);
+
+/* Optional timing hook: while set, the library records start_event before and
+ * stop_event after every launch of the chosen kernel on the launch stream
+ * (cudaEvent_t handles owned by the caller; NULL, NULL clears it).
+ * kernel: SAE_KERNEL_ENCODER_GEMM (tile GEMM of sae_b200_train_forward) or
+ * SAE_KERNEL_GRAD_GEMM (tile GEMM of sae_b200_train_backward). */
+#define SAE_KERNEL_ENCODER_GEMM 0
+#define SAE_KERNEL_GRAD_GEMM 1
+int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event);
+
+/* Bytes of scratch the training step needs for up to max_tokens tokens. */
+int sae_b200_workspace_bytes(int64_t max_tokens, int64_t d_in, int64_t n_features,
+                             int64_t csr_capacity, size_t* bytes_out);
+
+/* Byte offsets, inside the workspace of a step over n_tokens tokens, of the
+ * intermediates a caller may inspect after sae_b200_train_forward/backward:
+ * [0] theta f32 [F]        [1] xc bf16 [B, d]      [2] pre bf16 [B, F]
+ * [3] mask u32 [B, ceil(F/32)] (bit f%32 of word f/32: feature f active)
+ * [4] go bf16 [B, d]       [5] per-token active count i32 [B]
+ * [6] per-token squared error f32 [B]   [7] CSR row offsets i32 [F + 1]
+ * [8] CSR token ids i32 [nnz]           [9] CSR values u32 [nnz]
+ *     (low half: bf16 pre-activation, high half: bf16 gated grad_feat) */
+#define SAE_WS_N_OFFSETS 10
+int sae_b200_workspace_offsets(int64_t n_tokens, int64_t d_in, int64_t n_features,
+                               int64_t csr_capacity, size_t* offsets_out /* [10] */);
+
+/* ------------------------------------------------------- fused hot path */
+/* Forward of one microbatch: theta = exp(log_threshold); xc = x - b_dec;
+ * pre = xc W_enc^T + b_enc (bf16, tcgen05); gate = pre > theta; active sets;
+ * x_hat = gathered decode + b_dec; residual loss; sparsity term.
+ * Replaces _EncoderPreBias.forward (sae_trainer_rolling.py:584-590),
+ * _jumprelu_forward (827-901), decode/_SparseDecode.forward (922-950,
+ * 628-637) and the loss lines 2954-2974.
+ * x: [n_tokens, d] of x_dtype. x_hat_out: optional fp32 [n_tokens, d].
+ * fired: [F] uint8, OR-accumulated (reference fired_accum, 3016). */
+int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                           const SaeB200StepConfig* cfg, void* workspace,
+                           size_t workspace_bytes, SaeB200StepStats* stats,
+                           float* x_hat_out, uint8_t* fired, void* stream);
+
+/* Backward of the microbatch last passed to sae_b200_train_forward (same
+ * workspace): dense grad_feat GEMM with the STE epilogue, sparse scatter of
+ * dW_enc / dW_dec over the active pairs, b_enc / b_dec / log_threshold
+ * gradients. Replaces loss.backward() through _SparseDecode.backward
+ * (639-654), the hooks 784-825 and _EncoderPreBias.backward (592-607).
+ * When stats->csr_overflow is set on the device the sparse scatter is
+ * skipped; the caller then runs sae_b200_train_backward_dense. */
+int sae_b200_train_backward(const SaeB200Model* model, const SaeB200Grads* grads,
+                            const SaeB200StepConfig* cfg, void* workspace,
+                            size_t workspace_bytes, SaeB200StepStats* stats, void* stream);
+
+/* Same gradients without the capacity limit, for microbatches whose active
+ * set overflowed csr_capacity. dense_scratch: bf16 [n_tokens, F] device
+ * buffer owned by the caller. */
+int sae_b200_train_backward_dense(const SaeB200Model* model, const SaeB200Grads* grads,
+                                  const SaeB200StepConfig* cfg, void* workspace,
+                                  size_t workspace_bytes, SaeB200StepStats* stats,
+                                  void* dense_scratch, void* stream);
+
+/* Global gradient norm and clip coefficient (torch.nn.utils.clip_grad_norm_,
+ * called at sae_trainer_rolling.py:3049). Writes stats->grad_norm and
+ * stats->clip_coef; the scaling itself is applied inside sae_b200_adam_step.
+ * workspace: SAE_GRAD_NORM_WORKSPACE_BYTES of scratch (not the step workspace,
+ * whose forward intermediates it would overwrite). */
+#define SAE_GRAD_NORM_WORKSPACE_BYTES (592 * 4)
+int sae_b200_grad_norm(const SaeB200Model* model, const SaeB200Grads* grads, float max_norm,
+                       void* workspace, size_t workspace_bytes, SaeB200StepStats* stats,
+                       void* stream);
+
+/* L2-decay Adam (torch.optim.Adam, sae_trainer_rolling.py:2536-2541, 3076)
+ * fused with the decoder-column / encoder-row renormalisation (778-782,
+ * 3086-3090) and the refresh of the bf16 weight copies. */
+int sae_b200_adam_step(const SaeB200Model* model, const SaeB200Grads* grads,
+                       const SaeB200AdamState* state, const SaeB200AdamTensor* hyper /*[5], host*/,
+                       const SaeB200StepStats* stats, void* stream);
+
+/* ------------------------------------------ dense pieces of the module API */
+/* pre = (x - b_dec) W_enc^T + b_enc. pre_dtype BF16: computed the autocast way
+ * (bf16 operands, fp32 accumulate, bf16 result) on the tile GEMM. pre_dtype
+ * F32: fp32 throughout. xc_out (optional, pre_dtype): the saved x - b_dec.
+ * Replaces _EncoderPreBias.forward / _pre (567-590, 903-908). */
+int sae_b200_encode_pre(const SaeB200Model* model, const void* x, int x_dtype, int64_t n_tokens,
+                        void* pre_out, int pre_dtype, void* xc_out, int force_simt,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* gate = 1[pre > exp(log_threshold)], feat = pre * gate (fp32 outputs).
+ * Replaces the forward of _jumprelu_forward (827-901). */
+int sae_b200_jumprelu_forward(const void* pre, int pre_dtype, const float* log_threshold,
+                              int64_t n_tokens, int64_t n_features, float* feat_out,
+                              float* gate_out, void* stream);
+
+/* Straight-through backward of the JumpReLU (hooks 784-825 / _JumpReLUWithGate
+ * 700-731): grad_pre = grad_feat * gate; combined = pre * grad_feat + grad_gate;
+ * grad_log_threshold += -sum_t where(|pre - theta| < eps, combined) / (2 eps) * theta.
+ * grad_feat / grad_gate may be NULL (treated as zero); grad_pre_out may be NULL. */
+int sae_b200_jumprelu_backward(const void* pre, int pre_dtype, const float* log_threshold,
+                               int64_t n_tokens, int64_t n_features, const float* grad_feat,
+                               const float* grad_gate, float eps, void* grad_pre_out,
+                               float* grad_log_threshold, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* General strided product on CUDA cores: C = alpha * A B^T + beta * C (+ bias[n]).
+ * A[m, k] at A + m*sam + k*sak; B[n, k] at B + n*sbn + k*sbk; C[m, n] at
+ * C + m*scm + n*scn (strides in elements). beta == 0 never reads C. */
+int sae_b200_gemm(int64_t M, int64_t N, int64_t K, float alpha, const void* A, int a_dtype,
+                  int64_t sam, int64_t sak, const void* B, int b_dtype, int64_t sbn,
+                  int64_t sbk, float beta, void* C, int c_dtype, int64_t scm, int64_t scn,
+                  const float* bias_n, void* stream);
+
+/* out[c] = beta * out[c] + alpha * sum_r X[r, c]  (X row-major [rows, cols]). */
+int sae_b200_column_sum(const void* X, int x_dtype, int64_t rows, int64_t cols, float alpha,
+                        float beta, float* out, void* stream);
+
+/* Rows of W [rows, cols] to unit L2 norm (norm clamped at 1e-8), optionally
+ * refreshing a bf16 copy. Replaces _normalize_decoder (778-782) on the
+ * feature-major decoder and the W_enc row renorm (3089-3090). */
+int sae_b200_renorm_rows(float* W, int64_t rows, int64_t cols, void* shadow_bf16, void* stream);
+
+/* dst (bf16) = src (fp32), n elements: refresh of a bf16 weight copy. */
+int sae_b200_refresh_shadow(const float* src, void* dst_bf16, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAE_B200_H */

@@ -1,0 +1,254 @@
+"""Parity of the fused CUDA training step against the CPU oracle.
+
+Inputs and initial parameters are the reference's own (tests/golden). The
+oracle runs in its "bf16" precision, i.e. with the reference's CUDA autocast
+rounding points and float64 accumulation. Tolerances:
+  * thresholds: bit-identical to torch's CUDA exp (the reference's GPU path)
+    and within one float32 ulp of numpy's exp; the oracle is then given the
+    kernel's thresholds, since bf16 pre-activations lie on a grid and a
+    one-ulp threshold change moves grid points across the gate / STE band;
+  * active sets: bit-exact against the kernel's own pre-activations and
+    thresholds (gate == pre > theta, mask bits == gate, counts == popcount);
+    against the oracle, differences only where pre sits within one bf16 ulp
+    of theta;
+  * pre: <= 1 bf16 ulp; x_hat, loss, gradients: relative L2 error < 2e-2
+    (bf16 operands, different fp32 accumulation order);
+  * Adam + renorm: parameters within 2.5 * lr elementwise (one Adam step moves
+    an element by at most ~lr; a gradient sign flip on a near-zero gradient
+    moves it by 2 lr).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle import sae_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 2e-2
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def build(g, *, force_simt=False, csr_capacity=None, renorm=True):
+    from sae_b200 import B200Adam, B200JumpReLUSAE, FusedStep, reference_param_groups
+    d, F = int(g["d"]), int(g["F"])
+    sae = B200JumpReLUSAE(d, F)
+    with torch.no_grad():
+        sae.W_enc.weight.copy_(torch.from_numpy(g["p0_W_enc"]).float())
+        sae.W_enc.bias.copy_(torch.from_numpy(g["p0_b_enc"]).float())
+        sae.W_dec.weight.copy_(torch.from_numpy(g["p0_W_dec"]).float())
+        sae.b_dec.copy_(torch.from_numpy(g["p0_b_dec"]).float())
+        sae.log_threshold.copy_(torch.from_numpy(g["p0_log_threshold"]).float())
+    sae = sae.cuda()
+    sae.ste_bandwidth = float(g["eps"])
+    opt = B200Adam(reference_param_groups(sae, float(g["lr"])), lr=float(g["lr"]),
+                   betas=(0.9, 0.999), sae=sae, renorm=renorm)
+    n = int(g["n_micro"])
+    B = g["x0"].shape[0]
+    fs = FusedStep(sae, opt, max_tokens=B, csr_capacity=csr_capacity, force_simt=force_simt)
+    return sae, opt, fs
+
+
+def oracle_params(g):
+    return O.Params(*(g[f"p0_{k}"].astype(np.float32) for k in O.PARAM_NAMES))
+
+
+def oracle_cfg(g):
+    lr = float(g["lr"])
+    return O.StepConfig(lambda_l0=float(g["lam"]), al_mu=float(g["mu"]),
+                        target_l0=float(g["target"]), ste_bandwidth=float(g["eps"]),
+                        accum_steps=int(g["n_micro"]), lr=(lr,) * 4,
+                        wenc_factor=float(g["wenc_factor"]))
+
+
+def workspace_views(fs, n_tokens):
+    from sae_b200 import _lib as L
+    sae = fs.sae
+    d, F = sae.d_in, sae.n_features
+    off = L.workspace_offsets(n_tokens, d, F, fs.csr_capacity)
+    W = (F + 31) // 32
+
+    def view(name, dtype, count):
+        o = off[name]
+        nbytes = count * torch.tensor([], dtype=dtype).element_size()
+        return fs.ws[o:o + nbytes].view(dtype)
+
+    return {
+        "theta": view("theta", torch.float32, F),
+        "xc": view("xc", torch.bfloat16, n_tokens * d).view(n_tokens, d),
+        "pre": view("pre", torch.bfloat16, n_tokens * F).view(n_tokens, F),
+        "mask": view("mask", torch.int32, n_tokens * W).view(n_tokens, W),
+        "go": view("go", torch.bfloat16, n_tokens * d).view(n_tokens, d),
+        "tok_cnt": view("tok_cnt", torch.int32, n_tokens),
+        "col_offs": view("col_offs", torch.int32, F + 1),
+    }
+
+
+def kernel_theta(fs, n_tokens):
+    """The thresholds the kernels used in the last forward (theta of the
+    parameters before the optimizer step)."""
+    return workspace_views(fs, n_tokens)["theta"].cpu().numpy().copy()
+
+
+def unpack_mask(mask, F):
+    m = mask.cpu().numpy().view(np.uint32)
+    bits = ((m[:, :, None] >> np.arange(32, dtype=np.uint32)) & 1).reshape(m.shape[0], -1)
+    return bits[:, :F].astype(bool)
+
+
+CASES = [
+    ("super_f32_tiles", False),   # d % 64 == 0, F % 128 == 0: tcgen05 tile GEMMs
+    ("super_f32_tiles", True),    # same shape through the CUDA-core tile GEMM
+    ("super_f32_odd", False),     # F = 160: CUDA-core tile GEMM with ragged tiles
+    ("ste_f64", False),           # in-band-heavy STE shape (d=16, F=32)
+]
+
+
+@pytest.mark.parametrize("name,force_simt", CASES)
+def test_forward_matches_oracle_and_active_set_is_exact(name, force_simt):
+    g = load_golden(name)
+    sae, opt, fs = build(g, force_simt=force_simt)
+    x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
+    cfg = oracle_cfg(g)
+    st = fs.microbatch(x, accum_steps=1, first=True, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu,
+                       target_l0=cfg.target_l0)
+    torch.cuda.synchronize()
+    from sae_b200 import _lib as L
+    assert L.device_status() == 0
+    B, F = x.shape[0], sae.n_features
+    v = workspace_views(fs, B)
+    pre = v["pre"].float().cpu().numpy()
+    theta = v["theta"].cpu().numpy()
+    # thresholds: torch's CUDA exp bit for bit; numpy's exp within one ulp
+    lt = torch.from_numpy(g["p0_log_threshold"].astype(np.float32)).cuda()
+    np.testing.assert_array_equal(theta, lt.exp().cpu().numpy())
+    np.testing.assert_allclose(theta, np.exp(g["p0_log_threshold"].astype(np.float32)),
+                               rtol=2.5e-7)
+    # active set, bit-exact given the kernel's pre and theta
+    gate = pre > theta
+    bits = unpack_mask(v["mask"], F)
+    np.testing.assert_array_equal(bits, gate)
+    np.testing.assert_array_equal(v["tok_cnt"].cpu().numpy(), gate.sum(1))
+    assert st["nnz"] == int(gate.sum())
+    assert int(v["col_offs"][-1]) == int(gate.sum())
+    # against the oracle
+    fw = O.forward(g["x0"], oracle_params(g), cfg, "bf16", theta=theta)
+    ulp = np.abs(fw.pre) * 2.0 ** -7 + 1e-30
+    assert np.all(np.abs(pre - fw.pre) <= ulp * 1.01)
+    flip = gate != (fw.pre > fw.theta)
+    near = np.abs(fw.pre - fw.theta) <= np.abs(fw.theta) * 2.0 ** -7 + 1e-6
+    assert not np.any(flip & ~near), "gate differs away from the threshold"
+    assert st["l0"] == pytest.approx(float(gate.sum(1).mean()), rel=1e-6)
+    assert st["recon_loss"] == pytest.approx(fw.recon_loss, rel=BF16_TOL)
+    assert fs.fired_mask.cpu().numpy().tolist() == gate.any(0).tolist()
+
+
+@pytest.mark.parametrize("name,force_simt", CASES)
+def test_full_step_matches_oracle(name, force_simt):
+    g = load_golden(name)
+    sae, opt, fs = build(g, force_simt=force_simt)
+    cfg = oracle_cfg(g)
+    x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
+    wf = float(g["wenc_factor"])
+    out = fs.step(x, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu, target_l0=cfg.target_l0,
+                  wenc_dampen=(lambda l0: wf))
+    torch.cuda.synchronize()
+    p0 = oracle_params(g)
+    ref = O.train_step([g["x0"].astype(np.float32)], p0, O.AdamState.zeros_like(p0), cfg, "bf16",
+                       theta=kernel_theta(fs, x.shape[0]))
+    grads = {"W_enc": fs.g_W_enc, "b_enc": fs.g_b_enc, "W_dec": fs.g_W_dec_fm.t(),
+             "b_dec": fs.g_b_dec, "log_threshold": fs.g_log_thr}
+    for k, t in grads.items():
+        err = _rel(t.cpu().numpy(), getattr(ref.grads, k))
+        assert err < BF16_TOL, f"{k}: rel err {err:.3g}"
+    assert out["grad_norm"] == pytest.approx(ref.grad_norm, rel=BF16_TOL)
+    lr = float(g["lr"])
+    now = {"W_enc": sae.W_enc.weight, "b_enc": sae.W_enc.bias, "W_dec": sae.W_dec.weight,
+           "b_dec": sae.b_dec, "log_threshold": sae.log_threshold}
+    for k, t in now.items():
+        diff = np.abs(t.detach().cpu().numpy() - getattr(ref.params, k))
+        assert diff.max() <= 2.5 * lr + 1e-6, f"{k}: max |diff| {diff.max():.3g}"
+    # the bf16 copies the next step reads are the updated weights
+    np.testing.assert_array_equal(sae._shadow_enc.float().cpu().numpy(),
+                                  O.bf16(sae.W_enc.weight.detach().cpu().numpy()))
+    np.testing.assert_array_equal(sae._shadow_dec.float().cpu().numpy(),
+                                  O.bf16(sae.W_dec.weight.detach().t().cpu().numpy()))
+    # unit decoder columns / encoder rows after the fused renormalisation
+    np.testing.assert_allclose(sae.W_dec.weight.detach().norm(dim=0).cpu().numpy(), 1.0, atol=1e-5)
+    np.testing.assert_allclose(sae.W_enc.weight.detach().norm(dim=1).cpu().numpy(), 1.0, atol=1e-5)
+
+
+@pytest.mark.parametrize("n", [2, 4])
+def test_microbatch_accumulation_matches_oracle(n):
+    g = load_golden(f"ste_f64_accum{n}")
+    sae, opt, fs = build(g)
+    cfg = oracle_cfg(g)
+    xs = [g[f"x{i}"].astype(np.float32) for i in range(n)]
+    x = torch.from_numpy(np.concatenate(xs)).cuda()
+    fs.max_tokens = x.shape[0]
+    out = fs.step(x, microbatch_tokens=xs[0].shape[0], lambda_l0=cfg.lambda_l0,
+                  al_mu=cfg.al_mu, target_l0=cfg.target_l0)
+    p0 = oracle_params(g)
+    ref = O.train_step(xs, p0, O.AdamState.zeros_like(p0), cfg, "bf16",
+                       theta=kernel_theta(fs, xs[-1].shape[0]))
+    for k, t in {"W_enc": fs.g_W_enc, "log_threshold": fs.g_log_thr, "b_dec": fs.g_b_dec,
+                 "W_dec": fs.g_W_dec_fm.t(), "b_enc": fs.g_b_enc}.items():
+        assert _rel(t.cpu().numpy(), getattr(ref.grads, k)) < BF16_TOL, k
+    assert out["l0"] == pytest.approx(ref.l0, rel=1e-2)
+
+
+def test_dense_fallback_matches_sparse_path():
+    """An active set larger than the workspace's CSR capacity takes the dense
+    weight-gradient path; the result must match the sparse path."""
+    g = load_golden("super_f32_tiles")
+    cfg = oracle_cfg(g)
+    x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
+    res = []
+    for cap in (None, 16):
+        sae, opt, fs = build(g, csr_capacity=cap)
+        fs.microbatch(x, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu, target_l0=cfg.target_l0)
+        torch.cuda.synchronize()
+        res.append((fs.dense_fallbacks, fs.g_W_enc.clone(), fs.g_W_dec_fm.clone(),
+                    fs.g_b_dec.clone(), fs.g_log_thr.clone()))
+    assert res[0][0] == 0 and res[1][0] == 1
+    for a, b in zip(res[0][1:], res[1][1:]):
+        assert _rel(b.cpu().numpy(), a.cpu().numpy()) < 1e-5
+
+
+def test_step_is_deterministic():
+    g = load_golden("super_f32_tiles")
+    cfg = oracle_cfg(g)
+    x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
+    outs = []
+    for _ in range(2):
+        sae, opt, fs = build(g)
+        fs.step(x, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu, target_l0=cfg.target_l0)
+        torch.cuda.synchronize()
+        outs.append([t.clone() for t in (fs.g_W_enc, fs.g_W_dec_fm, fs.g_b_dec, fs.g_log_thr,
+                                         sae.W_enc.weight.detach(), sae.W_dec.weight.detach())])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+def test_bf16_input_matches_oracle():
+    """The trainer feeds bf16 activations (provider shards, 1606-1609)."""
+    g = load_golden("super_f32_tiles")
+    sae, opt, fs = build(g)
+    cfg = oracle_cfg(g)
+    xb = torch.from_numpy(g["x0"].astype(np.float32)).to(torch.bfloat16)
+    st = fs.microbatch(xb.cuda(), lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu,
+                       target_l0=cfg.target_l0)
+    fw = O.forward(xb.float().numpy(), oracle_params(g), cfg, "bf16",
+                   theta=kernel_theta(fs, xb.shape[0]))
+    assert st["recon_loss"] == pytest.approx(fw.recon_loss, rel=BF16_TOL)
+    ref = O.backward(xb.float().numpy(), oracle_params(g), fw, cfg, "bf16")
+    assert _rel(fs.g_W_enc.cpu().numpy(), ref.W_enc) < BF16_TOL
+    assert _rel(fs.g_log_thr.cpu().numpy(), ref.log_threshold) < BF16_TOL

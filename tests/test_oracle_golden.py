@@ -1,0 +1,138 @@
+"""The CPU oracle against the reference's own outputs (tests/golden/*.npz).
+
+The fixtures were produced by tests/golden/make_golden.py from the reference
+module and loop body; these tests pin oracle/sae_oracle.py to them so that the
+GPU parity tests, which compare against the oracle, inherit the pin.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from conftest import load_golden
+from oracle import sae_oracle as O
+
+
+def _params(g, tag="p0"):
+    return O.Params(*(g[f"{tag}_{k}"] for k in O.PARAM_NAMES))
+
+
+def _cfg(g):
+    lr = float(g["lr"])
+    return O.StepConfig(lambda_l0=float(g["lam"]), al_mu=float(g["mu"]),
+                        target_l0=float(g["target"]), ste_bandwidth=float(g["eps"]),
+                        accum_steps=int(g["n_micro"]), lr=(lr,) * 4,
+                        wenc_factor=float(g["wenc_factor"]))
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+CASES = [("ste_f64", "fp64", 1e-10), ("ste_f64_accum2", "fp64", 1e-10),
+         ("ste_f64_accum4", "fp64", 1e-10), ("super_f32_odd", "fp32", 2e-5),
+         ("super_f32_tiles", "fp32", 2e-5)]
+
+
+@pytest.mark.parametrize("name,precision,tol", CASES)
+def test_oracle_step_matches_reference(name, precision, tol):
+    g = load_golden(name)
+    cfg = _cfg(g)
+    n = int(g["n_micro"])
+    xs = [g[f"x{i}"] for i in range(n)]
+    p0 = _params(g)
+    res = O.train_step(xs, p0, O.AdamState.zeros_like(p0), cfg, precision)
+
+    for i, fw in enumerate(res.fw):
+        assert fw.l0 == pytest.approx(float(g["l0"][i]), abs=1e-9)
+        assert fw.recon_loss == pytest.approx(float(g["recon"][i]), rel=tol * 10)
+        assert _rel(fw.pre, g[f"pre{i}"]) < tol
+        assert _rel(fw.x_hat, g[f"x_hat{i}"]) < tol
+    # STE threshold gradient, encoder / decoder gradients, b_dec (reassociated).
+    for k in O.PARAM_NAMES:
+        assert _rel(getattr(res.grads, k), g[f"grad_{k}"]) < tol * 50, k
+    assert res.grad_norm == pytest.approx(float(g["grad_norm"]), rel=tol * 10)
+    # Adam (L2 decay, per-group), clip, dampening, renormalisations.
+    for k in O.PARAM_NAMES:
+        assert _rel(getattr(res.params, k), g[f"p1_{k}"]) < tol * 10, k
+
+
+def test_threshold_band_is_populated():
+    """The STE fixture must exercise the band (else the test above is vacuous)."""
+    g = load_golden("ste_f64")
+    p0 = _params(g)
+    fw = O.forward(g["x0"], p0, _cfg(g), "fp64")
+    in_band = np.abs(fw.pre - fw.theta) < float(g["eps"])
+    assert in_band.sum() > 100
+    assert np.abs(g["grad_log_threshold"]).max() > 0
+
+
+def test_accumulation_matches_single_batch():
+    """Microbatch accumulation sums the per-microbatch STE contributions
+    (tests/test_ste_equivalence.py:128-154 of the reference)."""
+    single = load_golden("ste_f64")["grad_log_threshold"]
+    for n in (2, 4):
+        acc = load_golden(f"ste_f64_accum{n}")["grad_log_threshold"]
+        # the sparsity term uses each microbatch's own l0, so only the
+        # reconstruction-driven part is invariant; the fixtures agree to the
+        # size of the sparsity difference
+        assert _rel(acc, single) < 0.2
+
+
+def test_gate_known_answer():
+    """pre = [0.05, 0.2, -1, 0.5], theta = 0.1 -> feat = [0, 0.2, 0, 0.5]
+    (reference tests/test_sae_model.py:41-55)."""
+    g = load_golden("gate_known_answer")
+    theta = np.exp(g["log_threshold"])
+    pre = g["pre"]
+    gate = (pre > theta).astype(np.float32)
+    np.testing.assert_array_equal(gate, g["gate"])
+    np.testing.assert_array_equal(pre * gate, g["feat"])
+    np.testing.assert_allclose(g["feat"], [[0.0, 0.2, 0.0, 0.5]], atol=1e-7)
+
+
+def test_bf16_rounding_is_round_to_nearest_even():
+    x = np.array([1.0, 1.00390625, 1.005859375, 1.0078125, -2.5, 3.0e-41, np.inf],
+                 dtype=np.float32)
+    got = O.bf16(x)
+    # 1 + 2^-8 is a tie between 1 and 1 + 2^-7 -> even (1.0)
+    np.testing.assert_array_equal(got[:4], [1.0, 1.0, 1.0078125, 1.0078125])
+    assert got[4] == -2.5 and got[6] == np.inf
+
+
+def test_cfg1_summary_matches_reference():
+    """The CPU-runnable benchmark configuration (d=256, F=8192, B=4096):
+    inputs regenerated from their seeds, reference init rebuilt by the
+    module's constructor, one full step in fp32."""
+    torch = pytest.importorskip("torch")
+    from sae_b200 import make_sae
+
+    g = load_golden("cfg1_f32")
+    d, F = int(g["d"]), int(g["F"])
+    x = O.superposition_batch(4096, d, 8192, 50, math.log(16.0), 0.3, seed=0)
+    assert float(x.astype(np.float64).sum()) == pytest.approx(float(g["x_sum"]), rel=1e-9)
+    sae = make_sae(d, F, seed=0)
+    with torch.no_grad():
+        sae.b_dec.copy_(torch.from_numpy(x.mean(0)))
+        sae.log_threshold.fill_(math.log(0.05))
+    p0 = O.Params(sae.W_enc.weight.detach().numpy().copy(), sae.W_enc.bias.detach().numpy().copy(),
+                  sae.W_dec.weight.detach().numpy().copy(), sae.b_dec.detach().numpy().copy(),
+                  sae.log_threshold.detach().numpy().copy())
+    for k in O.PARAM_NAMES:
+        assert float(getattr(p0, k).astype(np.float64).sum()) == pytest.approx(
+            float(g[f"p0_{k}_sum"]), rel=1e-6, abs=1e-6), k
+    cfg = _cfg(g)
+    res = O.train_step([x], p0, O.AdamState.zeros_like(p0), cfg, "fp32")
+    rows = g["rows"]
+    assert res.fw[0].l0 == pytest.approx(float(g["l0"][0]), rel=1e-6)
+    assert res.recon_loss == pytest.approx(float(g["recon"][0]), rel=1e-5)
+    assert res.grad_norm == pytest.approx(float(g["grad_norm"]), rel=1e-4)
+    for k in ("b_enc", "b_dec", "log_threshold"):
+        assert _rel(getattr(res.grads, k), g[f"grad_{k}"]) < 1e-3, k
+        assert _rel(getattr(res.params, k), g[f"p1_{k}"]) < 1e-5, k
+    assert _rel(res.grads.W_enc[rows], g["grad_W_enc_rows"]) < 1e-3
+    assert _rel(res.grads.W_dec[:, rows].T, g["grad_W_dec_rows"]) < 1e-3
+    assert _rel(res.params.W_enc[rows], g["p1_W_enc_rows"]) < 1e-5
+    assert _rel(res.params.W_dec[:, rows].T, g["p1_W_dec_rows"]) < 1e-5
