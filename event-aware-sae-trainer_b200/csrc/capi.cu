@@ -735,6 +735,85 @@ int sae_b200_jumprelu_backward(const void* pre, int pre_dtype, const float* log_
   return check_launch("jumprelu_bwd_final_kernel");
 }
 
+}  // extern "C"
+
+// ------------------------------------------------ allocation-free variant
+// Scratch for sae_b200_jumprelu_backward_static: the per-slab partial sums of
+// the threshold gradient live in this fixed device array instead of a
+// caller-provided workspace. It is part of the library image, so every GPU
+// that loads the library holds these 4 MiB until the process exits. Host code
+// must not use the symbol itself as a device pointer; it passes the address
+// that cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) float g_jumprelu_bwd_scratch[SAE_JUMPRELU_BWD_STATIC_FLOATS];
+
+namespace {
+
+// Device address of g_jumprelu_bwd_scratch, looked up once per device (with
+// that device current) on the first call made there.
+int static_scratch_address(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(SAE_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(SAE_ERR_NO_DEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_jumprelu_bwd_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(SAE_ERR_CUDA, "cudaGetSymbolAddress(jumprelu scratch): %s",
+                  cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return SAE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sae_b200_jumprelu_backward_static(const void* pre, int pre_dtype, const float* log_threshold,
+                                      int64_t n_tokens, int64_t n_features,
+                                      const float* grad_feat, const float* grad_gate, float eps,
+                                      void* grad_pre_out, float* grad_log_threshold,
+                                      void* stream_) {
+  if (pre == nullptr || log_threshold == nullptr || grad_log_threshold == nullptr ||
+      n_tokens <= 0 || n_features <= 0 || !(eps > 0.f))
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid jumprelu_backward_static arguments");
+  if (pre_dtype != SAE_DTYPE_BF16 && pre_dtype != SAE_DTYPE_F32)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "pre_dtype must be F32 or BF16");
+  const int64_t slabs = (n_tokens + JB_TOK - 1) / JB_TOK;
+  if (n_features > SAE_JUMPRELU_BWD_STATIC_FLOATS ||
+      slabs > SAE_JUMPRELU_BWD_STATIC_FLOATS / n_features)
+    return fail(SAE_ERR_UNSUPPORTED_SHAPE,
+                "jumprelu_backward_static holds at most %d partial sums: ceil(n_tokens/%d) * "
+                "n_features = %lld * %lld is too large; use sae_b200_jumprelu_backward with a "
+                "workspace",
+                SAE_JUMPRELU_BWD_STATIC_FLOATS, JB_TOK, static_cast<long long>(slabs),
+                static_cast<long long>(n_features));
+  float* part = nullptr;
+  SAE_TRY(static_scratch_address(&part));
+  // Every (slab, feature) partial is written by the first kernel before the
+  // second reads it, so nothing left over from an earlier call is ever read
+  // and the array needs no clearing.
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  dim3 grid(static_cast<unsigned>((n_features + 31) / 32), static_cast<unsigned>(slabs));
+  if (pre_dtype == SAE_DTYPE_BF16)
+    jumprelu_bwd_kernel<bf16><<<grid, 256, 0, stream>>>(
+        static_cast<const bf16*>(pre), log_threshold, n_tokens, n_features, grad_feat, grad_gate,
+        eps, static_cast<bf16*>(grad_pre_out), part);
+  else
+    jumprelu_bwd_kernel<float><<<grid, 256, 0, stream>>>(
+        static_cast<const float*>(pre), log_threshold, n_tokens, n_features, grad_feat, grad_gate,
+        eps, static_cast<float*>(grad_pre_out), part);
+  SAE_TRY(check_launch("jumprelu_bwd_kernel(static scratch)"));
+  jumprelu_bwd_final_kernel<<<grid_for(n_features, 256), 256, 0, stream>>>(
+      part, static_cast<int>(slabs), log_threshold, n_features, eps, grad_log_threshold);
+  return check_launch("jumprelu_bwd_final_kernel(static scratch)");
+}
+
 int sae_b200_gemm(int64_t M, int64_t N, int64_t K, float alpha, const void* A, int a_dtype,
                   int64_t sam, int64_t sak, const void* B, int b_dtype, int64_t sbn, int64_t sbk,
                   float beta, void* C, int c_dtype, int64_t scm, int64_t scn, const float* bias_n,

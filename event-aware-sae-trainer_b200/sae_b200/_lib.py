@@ -25,6 +25,7 @@ SAE_ERR_DEVICE_TIMEOUT = 7
 SAE_ERR_NO_DEVICE = 8
 
 GRAD_NORM_WORKSPACE_BYTES = 592 * 4
+JUMPRELU_BWD_STATIC_FLOATS = 1 << 20   # scratch size of sae_b200_jumprelu_backward_static
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -143,6 +144,9 @@ _SIGNATURES = {
     "sae_b200_jumprelu_backward": (
         [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_float, c_void_p,
          c_void_p, c_void_p, c_size_t, c_void_p], c_int),
+    "sae_b200_jumprelu_backward_static": (
+        [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_float, c_void_p,
+         c_void_p, c_void_p], c_int),
     "sae_b200_gemm": (
         [c_int64, c_int64, c_int64, c_float, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int,
          c_int64, c_int64, c_float, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p], c_int),

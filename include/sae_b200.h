@@ -223,6 +223,33 @@ int sae_b200_jumprelu_backward(const void* pre, int pre_dtype, const float* log_
                                float* grad_log_threshold, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of sae_b200_jumprelu_backward. (No counterpart in
+ * the reference trainer; it exists for callers of this library.)
+ * Some callers cannot hand the library a workspace: a host framework that has
+ * already reserved the GPU's memory for its own caching allocator (so that an
+ * extra cudaMalloc would fail or fragment it), or a latency-critical caller
+ * that must not make the implicitly synchronising cudaMalloc/cudaFree calls.
+ * This entry point takes the same inputs and outputs but keeps its scratch --
+ * the per-slab partial sums of the threshold gradient -- in a fixed array of
+ * SAE_JUMPRELU_BWD_STATIC_FLOATS floats (4 MiB) compiled into the library, so
+ * it allocates nothing. Every GPU that loads the library holds that array
+ * until the process exits.
+ *  - Limit: ceil(n_tokens / 256) * n_features must not exceed
+ *    SAE_JUMPRELU_BWD_STATIC_FLOATS (e.g. 65536 tokens x 4096 features);
+ *    larger calls return SAE_ERR_UNSUPPORTED_SHAPE and do nothing.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress, with that device current); make that first call
+ *    before capturing any stream into a CUDA graph.
+ *  - All calls share the one array, and each call overwrites the part it
+ *    reads before reading it. Calls that can run at the same time on the GPU
+ *    (different streams without ordering, or several host threads) race on
+ *    the array and give wrong results; order them on one stream. */
+#define SAE_JUMPRELU_BWD_STATIC_FLOATS (1 << 20)
+int sae_b200_jumprelu_backward_static(const void* pre, int pre_dtype, const float* log_threshold,
+                                      int64_t n_tokens, int64_t n_features,
+                                      const float* grad_feat, const float* grad_gate, float eps,
+                                      void* grad_pre_out, float* grad_log_threshold, void* stream);
+
 /* General strided product on CUDA cores: C = alpha * A B^T + beta * C (+ bias[n]).
  * A[m, k] at A + m*sam + k*sak; B[n, k] at B + n*sbn + k*sbk; C[m, n] at
  * C + m*scm + n*scn (strides in elements). beta == 0 never reads C. */
