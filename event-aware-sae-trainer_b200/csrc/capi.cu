@@ -182,20 +182,22 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// Row-major bf16 [rows, cols] matrix, boxes of box_rows x 64 with 128-byte swizzle.
-int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// Row-major bf16 [rows, cols] matrix in boxes of box_rows x box_cols.
+int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+              uint32_t box_cols = TILE_K,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_tiled();
   if (fn == nullptr) return fail(SAE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (!aligned16(base) || (cols * 2) % 16 != 0)
     return fail(SAE_ERR_MISALIGNED, "TMA operand must be 16-byte aligned with 16-byte row pitch");
   const cuuint64_t gdim[2] = {cols, rows};
   const cuuint64_t gstride[1] = {cols * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(TILE_K), box_rows};
+  const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estride[2] = {1, 1};
   const CUresult r =
       fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box,
-         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SAE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return SAE_OK;
 }
@@ -207,25 +209,35 @@ bool tc_eligible(int64_t d, int64_t F, int force_simt) {
 }
 
 // Launch the feature x token tile GEMM W [F, d] . T [B, d]^T with epilogue e.
+// aux: the token-major [B, F] bf16 tensor the epilogue reads (AUX_LOAD) or
+// writes (AUX_STORE) through the 64 KiB side tile.
 template <class Epi>
 int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64_t d,
-                     const Epi& e, bool use_tc, cudaStream_t stream, int timer = -1) {
+                     const Epi& e, bool use_tc, cudaStream_t stream, int timer = -1,
+                     const bf16* aux = nullptr) {
   const int m_tiles = static_cast<int>((F + TILE_M - 1) / TILE_M);
   const int n_tiles = static_cast<int>((B + TILE_N - 1) / TILE_N);
   if (use_tc) {
-    CUtensorMap tm_w, tm_t;
+    constexpr size_t smem = TcConfig<Epi::kAux>::SMEM;
+    CUtensorMap tm_w, tm_t, tm_aux;
     SAE_TRY(make_tmap(&tm_w, w, F, d, TILE_M));
     SAE_TRY(make_tmap(&tm_t, tok, B, d, TILE_N));
+    if (Epi::kAux != AUX_NONE) {
+      if (aux == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "tile GEMM side tensor is NULL");
+      SAE_TRY(make_tmap(&tm_aux, aux, B, F, TILE_N, TILE_M, CU_TENSOR_MAP_SWIZZLE_NONE));
+    } else {
+      tm_aux = tm_w;
+    }
     static std::once_flag attr_once;
     std::call_once(attr_once, [] {
       cudaFuncSetAttribute(tc_tile_gemm<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(TC_SMEM_BYTES));
+                           static_cast<int>(smem));
     });
     const int total = m_tiles * n_tiles;
     const int grid = std::min(total, device_info().sm_count);
     if (timer >= 0) timer_begin(timer, stream);
-    tc_tile_gemm<Epi><<<grid, TC_THREADS, TC_SMEM_BYTES, stream>>>(
-        tm_w, tm_t, m_tiles, n_tiles, static_cast<int>(d / TILE_K), e);
+    tc_tile_gemm<Epi><<<grid, TC_THREADS, smem, stream>>>(
+        tm_w, tm_t, tm_aux, m_tiles, n_tiles, static_cast<int>(d / TILE_K), e);
     const int rc = check_launch("tc_tile_gemm");
     if (timer >= 0) timer_end(timer, stream);
     return rc;
@@ -391,7 +403,8 @@ int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype
     e.n_features = static_cast<int>(F);
     e.mask_words = mask_words;
     SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), w.xc, F, B, d, e,
-                             tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_ENCODER_GEMM));
+                             tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_ENCODER_GEMM,
+                             w.pre));
   }
   // 3. per-feature scans -> CSR offsets
   scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(w.tile_cnt, w.col_tot, fired,
@@ -460,7 +473,8 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
     e.dbenc_part = w.dbenc_part;
     e.dense_dpre = dense_scratch;
     SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_dec_bf16), w.go, F, B, d, e,
-                             tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_GRAD_GEMM));
+                             tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_GRAD_GEMM,
+                             w.pre));
   }
   // 2. per-feature gradients (threshold STE, b_enc)
   feature_grads_kernel<<<grid_for(F, 256), 256, 0, stream>>>(
@@ -473,9 +487,8 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
                                                   static_cast<int>(F), static_cast<int>(d),
                                                   w.gemv_part);
   SAE_TRY(check_launch("bdec_gemv_kernel"));
-  bdec_grad_kernel<<<grid_for(d, 256), 256, 0, stream>>>(w.gosum_part, DECODE_GRID, w.gemv_part,
-                                                         GEMV_GRID, static_cast<int>(d), acc,
-                                                         grads->b_dec);
+  bdec_grad_kernel<<<static_cast<unsigned>((d + 31) / 32), 1024, 0, stream>>>(
+      w.gosum_part, DECODE_GRID, w.gemv_part, GEMV_GRID, static_cast<int>(d), acc, grads->b_dec);
   SAE_TRY(check_launch("bdec_grad_kernel"));
   // 4. weight gradients
   if (dense_scratch == nullptr) {
@@ -659,30 +672,21 @@ int sae_b200_encode_pre(const SaeB200Model* model, const void* x, int x_dtype, i
       return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "encode_pre needs xc_out or a workspace");
     xc = carve(workspace, L).xc;
   }
-  if (d % 8 == 0 && aligned16(x) && aligned16(xc)) {
-    // reuse the step prologue (theta lands in a dummy-free path: no theta needed)
-    if (x_dtype == SAE_DTYPE_BF16)
-      sub_bias_kernel<bf16, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
-          static_cast<const bf16*>(x), model->b_dec, xc, B, d);
-    else
-      sub_bias_kernel<float, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
-          static_cast<const float*>(x), model->b_dec, xc, B, d);
-  } else {
-    if (x_dtype == SAE_DTYPE_BF16)
-      sub_bias_kernel<bf16, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
-          static_cast<const bf16*>(x), model->b_dec, xc, B, d);
-    else
-      sub_bias_kernel<float, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
-          static_cast<const float*>(x), model->b_dec, xc, B, d);
-  }
+  if (x_dtype == SAE_DTYPE_BF16)
+    sub_bias_kernel<bf16, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
+        static_cast<const bf16*>(x), model->b_dec, xc, B, d);
+  else
+    sub_bias_kernel<float, bf16><<<grid_for(B * d, 256), 256, 0, stream>>>(
+        static_cast<const float*>(x), model->b_dec, xc, B, d);
   SAE_TRY(check_launch("sub_bias_kernel"));
   PreOnlyEpi e{};
   e.b_enc = model->b_enc;
   e.pre = static_cast<bf16*>(pre_out);
   e.n_tokens = static_cast<int>(B);
   e.n_features = static_cast<int>(F);
-  const bool tc = tc_eligible(d, F, force_simt) && aligned16(xc);
-  return launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), xc, F, B, d, e, tc, stream);
+  const bool tc = tc_eligible(d, F, force_simt) && aligned16(xc) && aligned16(pre_out);
+  return launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), xc, F, B, d, e, tc, stream,
+                          -1, static_cast<const bf16*>(pre_out));
 }
 
 int sae_b200_jumprelu_forward(const void* pre, int pre_dtype, const float* log_threshold,

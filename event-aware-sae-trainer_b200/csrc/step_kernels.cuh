@@ -130,6 +130,7 @@ __global__ void prep_kernel(const XT* __restrict__ x, const float* __restrict__ 
 // float(pre) > theta. Stores pre, one 32-feature mask word per token per
 // warp, and the active-token count of each feature in this 256-token tile.
 struct EncodeEpi {
+  static constexpr int kAux = AUX_STORE;   // pre goes out through a TMA store
   const float* theta;
   const float* b_enc;
   bf16* pre;
@@ -137,15 +138,19 @@ struct EncodeEpi {
   int* tile_cnt;
   int n_tokens, n_features, mask_words;
   // per-thread tile state
-  int f, n0, lane, word;
+  int f, n0, lane, word, row;
   float th, bias;
   int cnt;
   bool row_ok;
+  bf16* aux;
 
-  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int row, int q, int ln) {
-    f = m_tile * TILE_M + row;
+  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int r, int q, int ln,
+                                             bf16* aux_tile) {
+    row = r;
+    f = m_tile * TILE_M + r;
     n0 = n_tile * TILE_N;
     lane = ln;
+    aux = aux_tile;
     row_ok = f < n_features;
     th = row_ok ? theta[f] : __int_as_float(0x7f800000);
     bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
@@ -159,7 +164,10 @@ struct EncodeEpi {
       const int t = n0 + c + j;
       const bool ok = row_ok && t < n_tokens;
       const bf16 p = __float2bfloat16_rn(v[j] + bias);
-      if (ok) pre[static_cast<size_t>(t) * n_features + f] = p;
+      if (aux != nullptr)
+        aux[(c + j) * TILE_M + row] = p;   // rows past n_tokens are clipped by the store
+      else if (ok)
+        pre[static_cast<size_t>(t) * n_features + f] = p;
       const bool act = ok && (__bfloat162float(p) > th);
       const uint32_t bal = __ballot_sync(0xffffffffu, act);
       if (lane == j) myword = bal;
@@ -176,15 +184,20 @@ struct EncodeEpi {
 
 // pre only (module API encode_pre in bf16 mode).
 struct PreOnlyEpi {
+  static constexpr int kAux = AUX_STORE;
   const float* b_enc;
   bf16* pre;
   int n_tokens, n_features;
-  int f, n0;
+  int f, n0, row;
   float bias;
   bool row_ok;
-  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int row, int, int) {
-    f = m_tile * TILE_M + row;
+  bf16* aux;
+  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int r, int, int,
+                                             bf16* aux_tile) {
+    row = r;
+    f = m_tile * TILE_M + r;
     n0 = n_tile * TILE_N;
+    aux = aux_tile;
     row_ok = f < n_features;
     bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
   }
@@ -192,8 +205,11 @@ struct PreOnlyEpi {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int t = n0 + c + j;
-      if (row_ok && t < n_tokens)
-        pre[static_cast<size_t>(t) * n_features + f] = __float2bfloat16_rn(v[j] + bias);
+      const bf16 p = __float2bfloat16_rn(v[j] + bias);
+      if (aux != nullptr)
+        aux[(c + j) * TILE_M + row] = p;
+      else if (row_ok && t < n_tokens)
+        pre[static_cast<size_t>(t) * n_features + f] = p;
     }
   }
   __device__ __forceinline__ void end_tile() {}
@@ -221,13 +237,18 @@ struct GradEpi {
   float* thr_part;
   float* dbenc_part;
   bf16* dense_dpre;   // non-null: write the gated gradient densely instead of the CSR
+  static constexpr int kAux = AUX_LOAD;   // the pre tile arrives in shared memory by TMA
   // per-thread tile state
-  int f, n0, pos;
+  int f, n0, pos, row;
   float th, gate_grad, thr_sum, db_sum;
   bool row_ok, write_csr;
+  const bf16* aux;
 
-  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int row, int, int) {
-    f = m_tile * TILE_M + row;
+  __device__ __forceinline__ void begin_tile(int m_tile, int n_tile, int r, int, int,
+                                             const bf16* aux_tile) {
+    row = r;
+    aux = aux_tile;
+    f = m_tile * TILE_M + r;
     n0 = n_tile * TILE_N;
     row_ok = f < n_features;
     th = row_ok ? theta[f] : 0.f;
@@ -241,12 +262,26 @@ struct GradEpi {
   }
   __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
     if (!row_ok) return;
-#pragma unroll 8
+    // All 32 pre-activation loads of the chunk are issued before any is used,
+    // so a warp keeps 32 loads (32 x 64 contiguous bytes) in flight.
+    const int t0 = n0 + c;
+    const int nj = min(32, n_tokens - t0);
+    float pv[32];
+    if (aux != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) pv[j] = __bfloat162float(aux[(c + j) * TILE_M + row]);
+    } else {
+      const bf16* pcol = pre + static_cast<size_t>(t0) * n_features + f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        pv[j] = (j < nj) ? __bfloat162float(pcol[static_cast<size_t>(j) * n_features]) : 0.f;
+    }
+#pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const int t = n0 + c + j;
-      if (t >= n_tokens) break;
+      if (j >= nj) break;
+      const int t = t0 + j;
       const float gf = bf16_round(v[j]);
-      const float p = __bfloat162float(pre[static_cast<size_t>(t) * n_features + f]);
+      const float p = pv[j];
       const float comb = __fadd_rn(__fmul_rn(p, gf), gate_grad);
       if (fabsf(__fsub_rn(p, th)) < eps) thr_sum += comb;
       const bool act = p > th;
@@ -524,14 +559,32 @@ __global__ void __launch_bounds__(1024)
 
 // b_dec gradient: sum_b go (the fp32 gradient through "+ b_dec", 924) minus
 // the reassociated encoder term.
-__global__ void bdec_grad_kernel(const float* __restrict__ gosum_part, int n_go,
-                                 const float* __restrict__ gemv_part, int n_gemv, int d,
-                                 int accumulate, float* __restrict__ g_bdec) {
-  for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < d; k += gridDim.x * blockDim.x) {
-    float s1 = 0.f, s2 = 0.f;
-    for (int i = 0; i < n_go; ++i) s1 += gosum_part[static_cast<size_t>(i) * d + k];
-    for (int i = 0; i < n_gemv; ++i) s2 += gemv_part[static_cast<size_t>(i) * d + k];
-    const float g = s1 - s2;
+// Block = 32 columns x 32 row lanes; each lane sums every 32nd partial row,
+// then the 32 lane sums are added in a fixed order.
+__global__ void __launch_bounds__(1024)
+    bdec_grad_kernel(const float* __restrict__ gosum_part, int n_go,
+                     const float* __restrict__ gemv_part, int n_gemv, int d, int accumulate,
+                     float* __restrict__ g_bdec) {
+  __shared__ float s1[32][33];
+  __shared__ float s2[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int k = blockIdx.x * 32 + tx;
+  float a = 0.f, b = 0.f;
+  if (k < d) {
+    for (int i = ty; i < n_go; i += 32) a += gosum_part[static_cast<size_t>(i) * d + k];
+    for (int i = ty; i < n_gemv; i += 32) b += gemv_part[static_cast<size_t>(i) * d + k];
+  }
+  s1[ty][tx] = a;
+  s2[ty][tx] = b;
+  __syncthreads();
+  if (ty == 0 && k < d) {
+    float x = 0.f, y = 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      x += s1[r][tx];
+      y += s2[r][tx];
+    }
+    const float g = x - y;
     g_bdec[k] = accumulate ? g_bdec[k] + g : g;
   }
 }

@@ -11,10 +11,12 @@
 //
 // Two mainloops produce the same 128 x 256 tiles and call the same epilogue:
 //   * tc_tile_gemm: persistent, warp-specialised tcgen05 kernel. TMA (no
-//     multicast) streams 128x64 / 256x64 bf16 slabs through a 4-stage
+//     multicast) streams 128x64 / 256x64 bf16 slabs through a 3-4 stage
 //     mbarrier ring; one thread issues tcgen05.mma into a double-buffered
 //     TMEM accumulator (2 x 256 columns); four epilogue warps drain the
-//     other accumulator with tcgen05.ld while the next tile accumulates.
+//     other accumulator with tcgen05.ld while the next tile accumulates. A
+//     64 KiB token-major side tile can be TMA-loaded for the epilogue or
+//     TMA-stored from it.
 //   * simt_tile_gemm: plain CUDA-core kernel with full predication, for
 //     shapes TMA cannot describe (d not a multiple of 64, F not a multiple
 //     of 128) and for small problems.
@@ -23,19 +25,53 @@
 #include "ptx.cuh"
 
 namespace sae {
+using bf16 = __nv_bfloat16;
+}
+
+namespace sae {
 
 constexpr int TILE_M = 128;   // features per tile (TMEM lanes)
 constexpr int TILE_N = 256;   // tokens per tile (TMEM columns per accumulator)
 constexpr int TILE_K = 64;    // d per pipeline stage (one 128-byte swizzle row)
-constexpr int TC_STAGES = 4;
 constexpr int TC_A_BYTES = TILE_M * TILE_K * 2;   // 16 KiB
 constexpr int TC_B_BYTES = TILE_N * TILE_K * 2;   // 32 KiB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_THREADS = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
 constexpr int TC_GROUP_M = 16;    // feature tiles per rasterisation group
 constexpr int TC_BARRIER_BYTES = 256;
-constexpr size_t TC_SMEM_BYTES = TC_STAGES * TC_STAGE_BYTES + TC_BARRIER_BYTES + 1024;
 constexpr uint32_t TC_TMEM_COLS = 2 * TILE_N;     // two fp32 accumulators
+
+// Auxiliary [TILE_N tokens][TILE_M features] bf16 tile (64 KiB) that rides
+// along with each output tile: loaded by TMA for epilogues that read a
+// token-major [B, F] tensor (AUX_LOAD), or written by the epilogue and stored
+// by TMA for epilogues that produce one (AUX_STORE).
+enum AuxMode { AUX_NONE = 0, AUX_LOAD = 1, AUX_STORE = 2 };
+constexpr int TC_AUX_BYTES = TILE_N * TILE_M * 2;
+
+template <int AUX>
+struct TcConfig {
+  static constexpr int STAGES = AUX == AUX_NONE ? 4 : 3;
+  static constexpr size_t SMEM = STAGES * TC_STAGE_BYTES + (AUX == AUX_NONE ? 0 : TC_AUX_BYTES) +
+                                 TC_BARRIER_BYTES + 1024;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t x,
+                                             int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
 
 struct TileCoord {
   int m, n;
@@ -57,33 +93,44 @@ __device__ __forceinline__ TileCoord tile_coord(int t, int m_tiles, int n_tiles)
 }
 
 // Epilogue contract (Epi):
-//   begin_tile(m_tile, n_tile, row, quarter, lane)   row = feature within tile
+//   static constexpr int kAux                   AUX_NONE / AUX_LOAD / AUX_STORE
+//   begin_tile(m_tile, n_tile, row, quarter, lane, aux)   row = feature in tile;
+//       aux = the tile's [TILE_N][TILE_M] bf16 shared-memory buffer, or nullptr
+//       (CUDA-core path: the epilogue then uses global memory directly)
 //   chunk(col, v[32])   v[j] = D[row, col + j], col in {0, 32, ..., 224};
 //                       called by all 32 lanes of a warp together (ballots)
 //   end_tile()
 template <class Epi>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_tile_gemm(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_t,
-                 int m_tiles, int n_tiles, int k_blocks, const Epi epi) {
+                 const __grid_constant__ CUtensorMap tm_aux, int m_tiles, int n_tiles,
+                 int k_blocks, const Epi epi) {
+  constexpr int AUX = Epi::kAux;
+  constexpr int STAGES = TcConfig<AUX>::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* s_a = smem;
-  uint8_t* s_b = smem + TC_STAGES * TC_A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
+  uint8_t* s_b = smem + STAGES * TC_A_BYTES;
+  bf16* s_aux = reinterpret_cast<bf16*>(smem + STAGES * TC_STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * TC_STAGE_BYTES +
+                                               (AUX == AUX_NONE ? 0 : TC_AUX_BYTES));
   uint64_t* full = bars;
-  uint64_t* empty = bars + TC_STAGES;
-  uint64_t* acc_full = bars + 2 * TC_STAGES;
-  uint64_t* acc_empty = bars + 2 * TC_STAGES + 2;
-  uint64_t* drain = bars + 2 * TC_STAGES + 4;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * TC_STAGES + 5);
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint64_t* aux_full = bars + 2 * STAGES + 5;
+  uint64_t* aux_empty = bars + 2 * STAGES + 6;
+  uint64_t* epi_bar = bars + 2 * STAGES + 7;   // barrier among the 128 epilogue threads
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -92,6 +139,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&acc_empty[a], 4);   // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
+    mbar_init(aux_full, 1);
+    mbar_init(aux_empty, 4);
+    mbar_init(epi_bar, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -102,6 +152,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_t);
+    if (AUX != AUX_NONE) prefetch_tmap(&tm_aux);
   }
   tc_fence_before();
   __syncthreads();
@@ -113,13 +164,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (lane == 0) {
       // ---------------------------------------------------------- producer
       uint32_t issued = 0, issued_parity = 0;
-      bool ok = true;
-      int kit = 0;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      bool ok = true, aux_issued = false;
+      uint32_t aux_parity = 0;
+      int kit = 0, it = 0;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
         const TileCoord tc = tile_coord(t, m_tiles, n_tiles);
         for (int kb = 0; kb < k_blocks; ++kb, ++kit) {
-          const int s = kit % TC_STAGES;
-          const uint32_t ph = (kit / TC_STAGES) & 1;
+          const int s = kit % STAGES;
+          const uint32_t ph = (kit / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
             ok = false;
             break;
@@ -130,12 +182,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           issued |= 1u << s;
           issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
         }
+        if (AUX == AUX_LOAD && ok) {
+          // After the tile's operand loads, so the previous tile's epilogue
+          // (which frees the buffer) is not waited on ahead of the mainloop.
+          const uint32_t ph = it & 1;
+          if (!mbar_wait(aux_empty, ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(aux_full, TC_AUX_BYTES);
+          tma_load_2d(s_aux, &tm_aux, aux_full, tc.m * TILE_M, tc.n * TILE_N);
+          aux_issued = true;
+          aux_parity = ph;
+        }
       }
       if (!ok) {
         // Unwinding: let every copy this thread started land before the CTA
         // (and its shared memory) goes away.
-        for (int s = 0; s < TC_STAGES; ++s)
+        for (int s = 0; s < STAGES; ++s)
           if ((issued >> s) & 1u) mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr);
+        if (aux_issued) mbar_wait(aux_full, aux_parity, nullptr);
       }
     }
   } else if (warp == 1) {
@@ -154,8 +220,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TILE_N);
         for (int kb = 0; kb < k_blocks; ++kb, ++kit) {
-          const int s = kit % TC_STAGES;
-          const uint32_t ph = (kit / TC_STAGES) & 1;
+          const int s = kit % STAGES;
+          const uint32_t ph = (kit / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             ok = false;
             break;
@@ -184,15 +250,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;   // TMEM lane quarter this warp can address
     const int row = q * 32 + lane;
+    const bool issuer = (warp == 2 && lane == 0);
+    uint32_t epi_phase = 0;
+    // All 128 epilogue threads meet here; a bounded mbarrier wait (not
+    // bar.sync) so that an aborting CTA cannot strand the others.
+    auto epi_sync = [&]() -> bool {
+      mbar_arrive(epi_bar);
+      const bool r = mbar_wait(epi_bar, epi_phase, abort_flag);
+      epi_phase ^= 1;
+      return r;
+    };
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
+      if (AUX == AUX_STORE) {
+        // The previous tile's TMA store must have finished reading the buffer.
+        if (issuer) bulk_wait_read_all();
+        if (!epi_sync()) break;
+      }
       if (!mbar_wait(&acc_full[acc], aph, abort_flag)) break;
+      if (AUX == AUX_LOAD && !mbar_wait(aux_full, it & 1, abort_flag)) break;
       tc_fence_after();
       const TileCoord tc = tile_coord(t, m_tiles, n_tiles);
       Epi e = epi;
-      e.begin_tile(tc.m, tc.n, row, q, lane);
+      e.begin_tile(tc.m, tc.n, row, q, lane, AUX == AUX_NONE ? nullptr : s_aux);
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * TILE_N);
 #pragma unroll 1
@@ -206,8 +288,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         e.chunk(c, v);
       }
+      if (AUX == AUX_LOAD) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(aux_empty);
+      }
       e.end_tile();
+      if (AUX == AUX_STORE) {
+        fence_proxy_async_smem();
+        if (!epi_sync()) break;
+        if (issuer) tma_store_2d(&tm_aux, s_aux, tc.m * TILE_M, tc.n * TILE_N);
+      }
     }
+    if (AUX == AUX_STORE && issuer) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -236,7 +328,7 @@ __global__ void __launch_bounds__(TILE_M)
   const int f = m_tile * TILE_M + row;
 
   Epi e = epi;
-  e.begin_tile(m_tile, n_tile, row, q, lane);
+  e.begin_tile(m_tile, n_tile, row, q, lane, nullptr);
   for (int c = 0; c < TILE_N; c += 32) {
     float v[32];
 #pragma unroll

@@ -364,7 +364,9 @@ class B200JumpReLUSAE(nn.Module):
         """Encoder pre-activation (903-908); the reassociated Function unless x
         needs a gradient, in which case the plain x W^T path runs."""
         _require_cuda(x)
-        if torch.is_grad_enabled() and not x.requires_grad:
+        if not x.requires_grad:
+            # Under no_grad this is the same forward (bf16 tile GEMM under
+            # autocast) without the autograd record.
             return _EncoderPre.apply(x, self.W_enc.weight, self.W_enc.bias, self.b_dec, self)
         xc = x - self.b_dec
         pre = _PlainLinear.apply(xc, self.W_enc.weight, self.W_enc.bias)
