@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -202,6 +203,15 @@ int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
   return SAE_OK;
 }
 
+// SAE_B200_PAIR=0 keeps the tile GEMMs on single CTAs (tcgen05 cta_group::1).
+bool pair_mode_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SAE_B200_PAIR");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
 bool tc_eligible(int64_t d, int64_t F, int force_simt) {
   if (force_simt) return false;
   const DeviceInfo di = device_info();
@@ -227,6 +237,45 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
       SAE_TRY(make_tmap(&tm_aux, aux, B, F, TILE_N, TILE_M, CU_TENSOR_MAP_SWIZZLE_NONE));
     } else {
       tm_aux = tm_w;
+    }
+    if (F % (2 * TILE_M) == 0 && pair_mode_enabled()) {
+      // Paired CTAs: one 256-feature x 256-token tile per cluster of two.
+      constexpr size_t smem2 = Tc2Config<Epi::kAux>::SMEM;
+      static std::once_flag attr2_once;
+      static int max_clusters = 0;
+      std::call_once(attr2_once, [] {
+        cudaFuncSetAttribute(tc2_tile_gemm<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem2));
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(2 * std::max(1, device_info().sm_count / 2));
+        lc.blockDim = dim3(TC_THREADS);
+        lc.dynamicSmemBytes = smem2;
+        cudaLaunchAttribute at;
+        at.id = cudaLaunchAttributeClusterDimension;
+        at.val.clusterDim.x = 2;
+        at.val.clusterDim.y = 1;
+        at.val.clusterDim.z = 1;
+        lc.attrs = &at;
+        lc.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, tc2_tile_gemm<Epi>, &lc) != cudaSuccess) n = 0;
+        cudaGetLastError();
+        max_clusters = n;
+      });
+      if (max_clusters > 0) {
+        // Each CTA of the pair loads half of the 256-token slab.
+        CUtensorMap tm_t_half;
+        SAE_TRY(make_tmap(&tm_t_half, tok, B, d, TILE_N / 2));
+        const int m_pairs = static_cast<int>(F / (2 * TILE_M));
+        const int total_pairs = m_pairs * n_tiles;
+        const int clusters = std::min(total_pairs, max_clusters);
+        if (timer >= 0) timer_begin(timer, stream);
+        tc2_tile_gemm<Epi><<<2 * clusters, TC_THREADS, smem2, stream>>>(
+            tm_w, tm_t_half, tm_aux, m_pairs, n_tiles, static_cast<int>(d / TILE_K), e);
+        const int rc = check_launch("tc2_tile_gemm");
+        if (timer >= 0) timer_end(timer, stream);
+        return rc;
+      }
     }
     static std::once_flag attr_once;
     std::call_once(attr_once, [] {
@@ -417,17 +466,24 @@ int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype
   {
     const double scale = 1.0 / (static_cast<double>(cfg->accum_steps) * static_cast<double>(B) *
                                 static_cast<double>(d));
-    const int thr = vec_threads(d);
-    if (x_dtype == SAE_DTYPE_BF16)
-      decode_kernel<bf16><<<DECODE_GRID, thr, 0, stream>>>(
-          w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,
-          static_cast<const bf16*>(x), B, static_cast<int>(d), static_cast<int>(F), mask_words,
-          static_cast<float>(scale), w.go, x_hat_out, w.tok_sqerr, w.tok_cnt, w.gosum_part);
-    else
-      decode_kernel<float><<<DECODE_GRID, thr, 0, stream>>>(
-          w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,
-          static_cast<const float*>(x), B, static_cast<int>(d), static_cast<int>(F), mask_words,
-          static_cast<float>(scale), w.go, x_hat_out, w.tok_sqerr, w.tok_cnt, w.gosum_part);
+    const int V = vec_threads(d);
+    const int G = std::min(4, std::max(1, 512 / V));   // row groups per token
+    const size_t dyn = static_cast<size_t>(G - 1) * V * 2 * sizeof(float4);
+#define SAE_DECODE(XT, GG)                                                                   \
+  decode_kernel<XT, GG><<<DECODE_GRID, V * GG, dyn, stream>>>(                              \
+      w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,             \
+      static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), mask_words,   \
+      static_cast<float>(scale), w.go, x_hat_out, w.tok_sqerr, w.tok_cnt, w.gosum_part)
+    if (x_dtype == SAE_DTYPE_BF16) {
+      if (G >= 4) SAE_DECODE(bf16, 4);
+      else if (G == 2 || G == 3) SAE_DECODE(bf16, 2);
+      else SAE_DECODE(bf16, 1);
+    } else {
+      if (G >= 4) SAE_DECODE(float, 4);
+      else if (G == 2 || G == 3) SAE_DECODE(float, 2);
+      else SAE_DECODE(float, 1);
+    }
+#undef SAE_DECODE
     SAE_TRY(check_launch("decode_kernel"));
   }
   // 5. loss terms
@@ -492,9 +548,19 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
   SAE_TRY(check_launch("bdec_grad_kernel"));
   // 4. weight gradients
   if (dense_scratch == nullptr) {
-    scatter_weight_grads_kernel<<<device_info().sm_count * 8, thr, 0, stream>>>(
-        w.col_offs, w.csr_tok, w.csr_val, w.go, w.xc, static_cast<int>(F), static_cast<int>(d),
-        acc, g_wdec, grads->W_enc, w.counters, stats);
+    // Features have few active tokens each (tens), so one row group is best;
+    // the split variants serve dictionaries with very busy features.
+    const int G = cfg->n_tokens / std::max<int64_t>(1, F) > 64 ? 2 : 1;
+    const size_t dyn = static_cast<size_t>(G - 1) * thr * 4 * sizeof(float4);
+    const int grid = device_info().sm_count * 8;
+#define SAE_SCATTER(GG)                                                                        \
+  scatter_weight_grads_kernel<GG><<<grid, thr * GG, dyn, stream>>>(                           \
+      w.col_offs, w.csr_tok, w.csr_val, w.go, w.xc, static_cast<int>(F), static_cast<int>(d), \
+      acc, g_wdec, grads->W_enc, w.counters, stats)
+    if (G >= 4) SAE_SCATTER(4);
+    else if (G >= 2) SAE_SCATTER(2);
+    else SAE_SCATTER(1);
+#undef SAE_SCATTER
     return check_launch("scatter_weight_grads_kernel");
   }
   // dense fallback: dW_enc = dpre^T xc, dW_dec = acts^T go

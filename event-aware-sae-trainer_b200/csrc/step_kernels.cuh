@@ -349,13 +349,17 @@ __global__ void __launch_bounds__(1024)
 }
 
 // ------------------------------------------------------------------ decode
-// One block per token (grid-stride), d/8 threads each owning 8 columns.
-// Extracts the token's active features from its mask row in feature order,
-// gathers their bf16 decoder rows with 128-bit loads and accumulates in fp32.
-// Then x_hat = bf16(sum) + b_dec (the reference's bf16 GEMM output plus the
-// fp32 bias, 924), r = x - x_hat, squared error per token, and the loss
-// gradient go = -(scale * 2r) stored as bf16 (what the decoder GEMMs see).
-template <typename XT>
+// One block per token (grid-stride). The block is G row groups of V threads;
+// thread (g, c) owns columns [8c, 8c + 8) and decoder rows g, g + G, ... of the
+// token's active list, so a token with thousands of active features is
+// gathered G x 8 rows at a time per column slice. The active features are
+// extracted from the token's mask row in feature order, their bf16 decoder
+// rows gathered with 128-bit loads and accumulated in fp32; the G partial
+// sums are combined in a fixed order. Then x_hat = bf16(sum) + b_dec (the
+// reference's bf16 GEMM output plus the fp32 bias, 924), r = x - x_hat,
+// squared error per token, and the loss gradient go = -(scale * 2r) stored as
+// bf16 (what the decoder GEMMs see).
+template <typename XT, int G>
 __global__ void __launch_bounds__(1024)
     decode_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
                   const bf16* __restrict__ w_dec, const float* __restrict__ b_dec,
@@ -367,9 +371,13 @@ __global__ void __launch_bounds__(1024)
   __shared__ float s_v[DECODE_LIST_CAP];
   __shared__ int s_itmp[33];
   __shared__ float s_ftmp[33];
+  extern __shared__ float4 s_part[];   // (G - 1) x V x 2 float4
   const int tid = threadIdx.x;
+  const int V = blockDim.x / G;
+  const int g = tid / V;
+  const int col = tid - g * V;
   const int nvec = d / 8;
-  const bool has = tid < nvec;
+  const bool has = col < nvec;
   const int wpt = (mask_words + blockDim.x - 1) / blockDim.x;
   const int w0 = min(mask_words, tid * wpt);
   const int w1 = min(mask_words, w0 + wpt);
@@ -410,22 +418,23 @@ __global__ void __launch_bounds__(1024)
       __syncthreads();
       const int n = min(DECODE_LIST_CAP, total - win);
       if (has) {
-        const uint4* wcol = reinterpret_cast<const uint4*>(w_dec) + tid;
-        int i = 0;
-        for (; i + 4 <= n; i += 4) {
-          uint4 u[4];
+        const uint4* wcol = reinterpret_cast<const uint4*>(w_dec) + col;
+        int i = g;
+        for (; i + 7 * G < n; i += 8 * G) {
+          uint4 u[8];
 #pragma unroll
-          for (int r = 0; r < 4; ++r) u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r]) * nvec);
+          for (int r = 0; r < 8; ++r)
+            u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r * G]) * nvec);
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
+          for (int r = 0; r < 8; ++r) {
             float wf[8];
             unpack8(u[r], wf);
-            const float a = s_v[i + r];
+            const float a = s_v[i + r * G];
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
           }
         }
-        for (; i < n; ++i) {
+        for (; i < n; i += G) {
           float wf[8];
           unpack8(__ldg(wcol + static_cast<size_t>(s_f[i]) * nvec), wf);
           const float a = s_v[i];
@@ -434,11 +443,28 @@ __global__ void __launch_bounds__(1024)
         }
       }
     }
+    if constexpr (G > 1) {
+      __syncthreads();
+      if (g > 0 && has) {
+        s_part[((g - 1) * V + col) * 2] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        s_part[((g - 1) * V + col) * 2 + 1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      }
+      __syncthreads();
+      if (g == 0 && has) {
+#pragma unroll
+        for (int h = 0; h < G - 1; ++h) {
+          const float4 a = s_part[(h * V + col) * 2];
+          const float4 c = s_part[(h * V + col) * 2 + 1];
+          acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+          acc[4] += c.x; acc[5] += c.y; acc[6] += c.z; acc[7] += c.w;
+        }
+      }
+    }
 
     float sq = 0.f;
-    if (has) {
+    if (g == 0 && has) {
       float xv[8];
-      const size_t base = static_cast<size_t>(b) * d + tid * 8;
+      const size_t base = static_cast<size_t>(b) * d + col * 8;
       if constexpr (sizeof(XT) == 2) {
         unpack8(*reinterpret_cast<const uint4*>(x + base), xv);
       } else {
@@ -447,16 +473,16 @@ __global__ void __launch_bounds__(1024)
         xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
         xv[4] = c.x; xv[5] = c.y; xv[6] = c.z; xv[7] = c.w;
       }
-      float g[8], xh[8];
+      float gv[8], xh[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        xh[j] = __fadd_rn(bf16_round(acc[j]), b_dec[tid * 8 + j]);
+        xh[j] = __fadd_rn(bf16_round(acc[j]), b_dec[col * 8 + j]);
         const float r = __fsub_rn(xv[j], xh[j]);
         sq = fmaf(r, r, sq);
-        g[j] = -__fmul_rn(go_scale, __fadd_rn(r, r));
-        gsum[j] += g[j];
+        gv[j] = -__fmul_rn(go_scale, __fadd_rn(r, r));
+        gsum[j] += gv[j];
       }
-      *reinterpret_cast<uint4*>(go + base) = pack8(g);
+      *reinterpret_cast<uint4*>(go + base) = pack8(gv);
       if (x_hat != nullptr) {
         *reinterpret_cast<float4*>(x_hat + base) = make_float4(xh[0], xh[1], xh[2], xh[3]);
         *reinterpret_cast<float4*>(x_hat + base + 4) = make_float4(xh[4], xh[5], xh[6], xh[7]);
@@ -468,9 +494,10 @@ __global__ void __launch_bounds__(1024)
       tok_cnt[b] = total;
     }
   }
-  if (has) {
+  if (g == 0 && has) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) gosum_part[static_cast<size_t>(blockIdx.x) * d + tid * 8 + j] = gsum[j];
+    for (int j = 0; j < 8; ++j)
+      gosum_part[static_cast<size_t>(blockIdx.x) * d + col * 8 + j] = gsum[j];
   }
 }
 
@@ -592,8 +619,24 @@ __global__ void __launch_bounds__(1024)
 // Sparse decoder / encoder weight gradients over the feature-major CSR:
 //   dW_dec[f] = sum_{(t,f) active} pre[t,f] * go[t]     (index_add_, 645-652)
 //   dW_enc[f] = sum_{(t,f) active} dpre[t,f] * xc[t]    (dpre^T xc, 599)
-// Blocks take features from a global counter; each feature is summed by
-// one block in CSR (token) order, so the result does not depend on timing.
+// Blocks take features from a global counter. A block is G row groups of V
+// threads: thread (g, c) owns columns [8c, 8c + 8) and entries g, g + G, ... of
+// the feature's CSR row; the G partial sums are added in a fixed order, so
+// the result does not depend on timing.
+__device__ __forceinline__ void scatter_fma(uint32_t v, const uint4 gu, const uint4 xu,
+                                            float (&ad)[8], float (&ae)[8]) {
+  const float a = __uint_as_float(v << 16), q = __uint_as_float(v & 0xFFFF0000u);
+  float gf[8], xf[8];
+  unpack8(gu, gf);
+  unpack8(xu, xf);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    ad[j] = fmaf(a, gf[j], ad[j]);
+    ae[j] = fmaf(q, xf[j], ae[j]);
+  }
+}
+
+template <int G>
 __global__ void __launch_bounds__(1024)
     scatter_weight_grads_kernel(const int* __restrict__ col_offs, const int* __restrict__ csr_tok,
                                 const uint32_t* __restrict__ csr_val, const bf16* __restrict__ go,
@@ -603,11 +646,15 @@ __global__ void __launch_bounds__(1024)
                                 const SaeB200StepStats* stats) {
   if (stats->csr_overflow) return;
   __shared__ int s_f[2];
+  extern __shared__ float4 s_part[];   // (G - 1) x V x 4 float4
   const int tid = threadIdx.x;
+  const int V = blockDim.x / G;
+  const int g = tid / V;
+  const int col = tid - g * V;
   const int nvec = d / 8;
-  const bool has = tid < nvec;
-  const uint4* go_v = reinterpret_cast<const uint4*>(go) + tid;
-  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + tid;
+  const bool has = col < nvec;
+  const uint4* go_v = reinterpret_cast<const uint4*>(go) + col;
+  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + col;
   int it = 0;
   while (true) {
     if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
@@ -620,47 +667,56 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll
     for (int j = 0; j < 8; ++j) ad[j] = ae[j] = 0.f;
     if (has) {
-      int i = s;
-      for (; i + 2 <= e; i += 2) {
-        const int t0 = csr_tok[i], t1 = csr_tok[i + 1];
-        const uint32_t v0 = csr_val[i], v1 = csr_val[i + 1];
-        const uint4 g0 = __ldg(go_v + static_cast<size_t>(t0) * nvec);
-        const uint4 x0 = __ldg(xc_v + static_cast<size_t>(t0) * nvec);
-        const uint4 g1 = __ldg(go_v + static_cast<size_t>(t1) * nvec);
-        const uint4 x1 = __ldg(xc_v + static_cast<size_t>(t1) * nvec);
-        float gf[8], xf[8];
-        float a = __uint_as_float(v0 << 16), q = __uint_as_float(v0 & 0xFFFF0000u);
-        unpack8(g0, gf);
-        unpack8(x0, xf);
+      int i = s + g;
+      for (; i + 3 * G < e; i += 4 * G) {
+        int t[4];
+        uint32_t v[4];
+        uint4 gu[4], xu[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          ad[j] = fmaf(a, gf[j], ad[j]);
-          ae[j] = fmaf(q, xf[j], ae[j]);
+        for (int r = 0; r < 4; ++r) {
+          t[r] = csr_tok[i + r * G];
+          v[r] = csr_val[i + r * G];
         }
-        a = __uint_as_float(v1 << 16);
-        q = __uint_as_float(v1 & 0xFFFF0000u);
-        unpack8(g1, gf);
-        unpack8(x1, xf);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          ad[j] = fmaf(a, gf[j], ad[j]);
-          ae[j] = fmaf(q, xf[j], ae[j]);
+        for (int r = 0; r < 4; ++r) {
+          gu[r] = __ldg(go_v + static_cast<size_t>(t[r]) * nvec);
+          xu[r] = __ldg(xc_v + static_cast<size_t>(t[r]) * nvec);
         }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) scatter_fma(v[r], gu[r], xu[r], ad, ae);
       }
-      for (; i < e; ++i) {
+      for (; i < e; i += G) {
         const int t0 = csr_tok[i];
-        const uint32_t v0 = csr_val[i];
-        float gf[8], xf[8];
-        unpack8(__ldg(go_v + static_cast<size_t>(t0) * nvec), gf);
-        unpack8(__ldg(xc_v + static_cast<size_t>(t0) * nvec), xf);
-        const float a = __uint_as_float(v0 << 16), q = __uint_as_float(v0 & 0xFFFF0000u);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          ad[j] = fmaf(a, gf[j], ad[j]);
-          ae[j] = fmaf(q, xf[j], ae[j]);
-        }
+        scatter_fma(csr_val[i], __ldg(go_v + static_cast<size_t>(t0) * nvec),
+                    __ldg(xc_v + static_cast<size_t>(t0) * nvec), ad, ae);
       }
-      const size_t o = static_cast<size_t>(f) * d + tid * 8;
+    }
+    if constexpr (G > 1) {
+      if (e - s > 1) {   // uniform across the block
+        if (g > 0 && has) {
+          float4* p = s_part + ((g - 1) * V + col) * 4;
+          p[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
+          p[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
+          p[2] = make_float4(ae[0], ae[1], ae[2], ae[3]);
+          p[3] = make_float4(ae[4], ae[5], ae[6], ae[7]);
+        }
+        __syncthreads();
+        if (g == 0 && has) {
+#pragma unroll
+          for (int h = 0; h < G - 1; ++h) {
+            const float4* p = s_part + (h * V + col) * 4;
+            const float4 a0 = p[0], a1 = p[1], b0 = p[2], b1 = p[3];
+            ad[0] += a0.x; ad[1] += a0.y; ad[2] += a0.z; ad[3] += a0.w;
+            ad[4] += a1.x; ad[5] += a1.y; ad[6] += a1.z; ad[7] += a1.w;
+            ae[0] += b0.x; ae[1] += b0.y; ae[2] += b0.z; ae[3] += b0.w;
+            ae[4] += b1.x; ae[5] += b1.y; ae[6] += b1.z; ae[7] += b1.w;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    if (g == 0 && has) {
+      const size_t o = static_cast<size_t>(f) * d + col * 8;
       if (g_wdec != nullptr) {
         float4* p = reinterpret_cast<float4*>(g_wdec + o);
         if (accumulate) {

@@ -310,6 +310,334 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------------
+// Paired-CTA version (tcgen05 cta_group::2). A cluster of two CTAs computes a
+// 256-feature x 256-token tile: CTA r holds feature rows [128 r, 128 r + 128)
+// of the A slab and token rows [128 r, 128 r + 128) of the B slab in its own
+// shared memory, and the leader (rank 0) issues one M=256, N=256 MMA per
+// K step that reads both CTAs' halves and writes each CTA's 128 x 256
+// accumulator into that CTA's TMEM. Per SM this moves 32 KiB per K slab
+// instead of 48 KiB, and the ring gets 5-6 stages. Each CTA's epilogue is
+// the same as in the single-CTA kernel (its own 128 features x 256 tokens).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (barriers other CTAs arrive on).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_cluster(a, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_device_status(SAE_ERR_DEVICE_TIMEOUT);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap,
+                                                 uint32_t leader_bar, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the barrier at this offset in both CTAs once the pair's MMAs are done.
+__device__ __forceinline__ void tc_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair_local(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+constexpr int TC2_A_BYTES = TILE_M * TILE_K * 2;      // 16 KiB: this CTA's 128 features
+constexpr int TC2_B_BYTES = (TILE_N / 2) * TILE_K * 2;  // 16 KiB: this CTA's 128 tokens
+constexpr int TC2_STAGE_BYTES = TC2_A_BYTES + TC2_B_BYTES;
+
+template <int AUX>
+struct Tc2Config {
+  static constexpr int STAGES = AUX == AUX_NONE ? 6 : 5;
+  static constexpr size_t SMEM = STAGES * TC2_STAGE_BYTES +
+                                 (AUX == AUX_NONE ? 0 : TC_AUX_BYTES) + TC_BARRIER_BYTES + 1024;
+};
+
+// Pair tile t -> (feature pair index, token tile), same grouping as tile_coord.
+template <class Epi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
+    tc2_tile_gemm(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_t,
+                  const __grid_constant__ CUtensorMap tm_aux, int m_pairs, int n_tiles,
+                  int k_blocks, const Epi epi) {
+  constexpr int AUX = Epi::kAux;
+  constexpr int STAGES = Tc2Config<AUX>::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + STAGES * TC2_A_BYTES;
+  bf16* s_aux = reinterpret_cast<bf16*>(smem + STAGES * TC2_STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * TC2_STAGE_BYTES +
+                                               (AUX == AUX_NONE ? 0 : TC_AUX_BYTES));
+  uint64_t* full = bars;                        // leader: both CTAs' TMA bytes
+  uint64_t* empty = bars + STAGES;              // each CTA: stage free (leader's commit)
+  uint64_t* acc_full = bars + 2 * STAGES;       // each CTA: accumulator ready
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // leader: 8 epilogue warps done
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint64_t* aux_full = bars + 2 * STAGES + 5;
+  uint64_t* aux_empty = bars + 2 * STAGES + 6;
+  uint64_t* epi_bar = bars + 2 * STAGES + 7;
+  uint64_t* done_bar = bars + 2 * STAGES + 8;   // end-of-kernel handshake of the pair
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t peer = rank ^ 1u;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);   // four epilogue warps in each CTA of the pair
+    }
+    mbar_init(drain, 1);
+    mbar_init(aux_full, 1);
+    mbar_init(aux_empty, 4);
+    mbar_init(epi_bar, 128);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, TC_TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_t);
+    if (AUX != AUX_NONE) prefetch_tmap(&tm_aux);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();   // both CTAs' barriers exist before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int pairs = gridDim.x >> 1;
+  const int pair = blockIdx.x >> 1;
+  const int total = m_pairs * n_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      uint32_t aux_parity = 0;
+      bool ok = true, aux_issued = false;
+      int kit = 0, it = 0;
+      for (int t = pair; t < total && ok; t += pairs, ++it) {
+        const TileCoord tc = tile_coord(t, m_pairs, n_tiles);
+        const int f0 = (2 * tc.m + static_cast<int>(rank)) * TILE_M;
+        const int t0 = tc.n * TILE_N + static_cast<int>(rank) * (TILE_N / 2);
+        for (int kb = 0; kb < k_blocks; ++kb, ++kit) {
+          const int s = kit % STAGES;
+          const uint32_t ph = (kit / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t lbar = mapa_shared(smem_u32(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * TC2_STAGE_BYTES);
+          tma_load_2d_pair(s_a + s * TC2_A_BYTES, &tm_w, lbar, kb * TILE_K, f0);
+          tma_load_2d_pair(s_b + s * TC2_B_BYTES, &tm_t, lbar, kb * TILE_K, t0);
+        }
+        if (AUX == AUX_LOAD && ok) {
+          const uint32_t ph = it & 1;
+          if (!mbar_wait(aux_empty, ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(aux_full, TC_AUX_BYTES);
+          tma_load_2d(s_aux, &tm_aux, aux_full, f0, tc.n * TILE_N);
+          aux_issued = true;
+          aux_parity = ph;
+        }
+      }
+      if (!ok && aux_issued) mbar_wait(aux_full, aux_parity, nullptr);
+      // Operand copies of an aborted pipeline complete on the leader's full
+      // barriers; the leader's MMA thread below drains them.
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // --------------------------------------------------------- MMA issue
+      constexpr uint32_t idesc = idesc_bf16_f32(2 * TILE_M, TILE_N);
+      bool ok = true, any_mma = false;
+      int kit = 0, it = 0;
+      for (int t = pair; t < total && ok; t += pairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_empty[acc], aph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TILE_N);
+        for (int kb = 0; kb < k_blocks; ++kb, ++kit) {
+          const int s = kit % STAGES;
+          const uint32_t ph = (kit / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = smem_desc_k_sw128(s_a + s * TC2_A_BYTES);
+          const uint64_t bdesc = smem_desc_k_sw128(s_b + s * TC2_B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < TILE_K / 16; ++kk)
+            tc_mma_bf16_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          any_mma = true;
+          tc_commit_pair_both(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit_pair_both(&acc_full[acc]);
+      }
+      if (!ok && any_mma) {
+        tc_commit_pair_local(drain);
+        mbar_wait(drain, 0, nullptr);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool issuer = (warp == 2 && lane == 0);
+    const uint32_t leader_acc_empty[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0),
+                                          mapa_shared(smem_u32(&acc_empty[1]), 0)};
+    uint32_t epi_phase = 0;
+    auto epi_sync = [&]() -> bool {
+      mbar_arrive(epi_bar);
+      const bool r = mbar_wait(epi_bar, epi_phase, abort_flag);
+      epi_phase ^= 1;
+      return r;
+    };
+    int it = 0;
+    for (int t = pair; t < total; t += pairs, ++it) {
+      const int acc = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      if (AUX == AUX_STORE) {
+        if (issuer) bulk_wait_read_all();
+        if (!epi_sync()) break;
+      }
+      if (!mbar_wait(&acc_full[acc], aph, abort_flag)) break;
+      if (AUX == AUX_LOAD && !mbar_wait(aux_full, it & 1, abort_flag)) break;
+      tc_fence_after();
+      const TileCoord tc = tile_coord(t, m_pairs, n_tiles);
+      const int m_tile = 2 * tc.m + static_cast<int>(rank);
+      Epi e = epi;
+      e.begin_tile(m_tile, tc.n, row, q, lane, AUX == AUX_NONE ? nullptr : s_aux);
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * TILE_N);
+#pragma unroll 1
+      for (int c = 0; c < TILE_N; c += 32) {
+        float v[32];
+        tmem_ld_32cols(t_row + c, v);
+        if (c == TILE_N - 32) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(leader_acc_empty[acc]);
+        }
+        e.chunk(c, v);
+      }
+      if (AUX == AUX_LOAD) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(aux_empty);
+      }
+      e.end_tile();
+      if (AUX == AUX_STORE) {
+        fence_proxy_async_smem();
+        if (!epi_sync()) break;
+        if (issuer) tma_store_2d(&tm_aux, s_aux, m_tile * TILE_M, tc.n * TILE_N);
+      }
+    }
+    if (AUX == AUX_STORE && issuer) bulk_wait_all();
+  }
+
+  // Teardown: the leader's MMAs write into both CTAs' TMEM, so neither CTA
+  // frees TMEM before both have finished (bounded handshake on done_bar).
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) {
+      mbar_arrive_remote(mapa_shared(smem_u32(done_bar), peer));
+      mbar_wait_cluster(done_bar, 0, nullptr);
+    }
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TC_TMEM_COLS);
+  }
+}
+
 // CUDA-core version of the same tile: one thread per feature row, 32 token
 // columns per pass, operands staged through shared memory in 32-wide K slabs.
 // T may be any of bf16 / fp32 through the loader functor below.
