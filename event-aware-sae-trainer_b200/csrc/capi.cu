@@ -83,6 +83,11 @@ struct Layout {
       thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part, counters, total;
 };
 
+// Row pitch (tokens) of the feature-major pre-activations: whole 64-token
+// boxes plus one, so that the pitch is never a power of two (a 2^k-byte pitch
+// puts the 128 rows of every TMA box on the same DRAM channels).
+inline int64_t pre_pitch(int64_t B) { return (B + 63) / 64 * 64 + 64; }
+
 Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   Layout L{};
   size_t off = 0;
@@ -95,7 +100,7 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   const size_t nT = static_cast<size_t>((B + TILE_N - 1) / TILE_N);
   L.theta = take(F * 4);
   L.xc = take(B * d * 2);
-  L.pre = take(B * F * 2);
+  L.pre = take(static_cast<size_t>(F) * pre_pitch(B) * 2);   // feature-major [F, ldp]
   L.mask = take(B * W * 4);
   L.tile_cnt = take(nT * F * 4);
   L.col_tot = take(F * 4);
@@ -186,13 +191,14 @@ EncodeTiledFn encode_tiled() {
 // Row-major bf16 [rows, cols] matrix in boxes of box_rows x box_cols.
 int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
               uint32_t box_cols = TILE_K,
-              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B, uint64_t pitch = 0) {
   EncodeTiledFn fn = encode_tiled();
   if (fn == nullptr) return fail(SAE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  if (!aligned16(base) || (cols * 2) % 16 != 0)
+  if (pitch == 0) pitch = cols;
+  if (!aligned16(base) || (pitch * 2) % 16 != 0)
     return fail(SAE_ERR_MISALIGNED, "TMA operand must be 16-byte aligned with 16-byte row pitch");
   const cuuint64_t gdim[2] = {cols, rows};
-  const cuuint64_t gstride[1] = {cols * 2};
+  const cuuint64_t gstride[1] = {pitch * 2};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estride[2] = {1, 1};
   const CUresult r =
@@ -219,8 +225,17 @@ bool tc_eligible(int64_t d, int64_t F, int force_simt) {
 }
 
 // Launch the feature x token tile GEMM W [F, d] . T [B, d]^T with epilogue e.
-// aux: the token-major [B, F] bf16 tensor the epilogue reads (AUX_LOAD) or
-// writes (AUX_STORE) through the 64 KiB side tile.
+// aux: the [B, F]-sized bf16 tensor the epilogue reads (AUX_LOAD) or writes
+// (AUX_STORE) through the 64 KiB side tile: token-major [B, F], or
+// feature-major [F, pre_pitch(B)] when Epi::kAuxFeatureMajor.
+template <class Epi>
+int aux_tmap(CUtensorMap* m, const bf16* aux, int64_t F, int64_t B, uint32_t box_tokens) {
+  if (Epi::kAuxFeatureMajor)
+    return make_tmap(m, aux, F, B, TILE_M, AUX_FM_BOX_TOKENS, CU_TENSOR_MAP_SWIZZLE_128B,
+                     pre_pitch(B));
+  return make_tmap(m, aux, B, F, box_tokens, TILE_M, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 template <class Epi>
 int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64_t d,
                      const Epi& e, bool use_tc, cudaStream_t stream, int timer = -1,
@@ -234,7 +249,7 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
     SAE_TRY(make_tmap(&tm_t, tok, B, d, TILE_N));
     if (Epi::kAux != AUX_NONE) {
       if (aux == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "tile GEMM side tensor is NULL");
-      SAE_TRY(make_tmap(&tm_aux, aux, B, F, TILE_N, TILE_M, CU_TENSOR_MAP_SWIZZLE_NONE));
+      SAE_TRY(aux_tmap<Epi>(&tm_aux, aux, F, B, TILE_N));
     } else {
       tm_aux = tm_w;
     }
@@ -248,7 +263,7 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
                              static_cast<int>(smem2));
         cudaLaunchConfig_t lc = {};
         lc.gridDim = dim3(2 * std::max(1, device_info().sm_count / 2));
-        lc.blockDim = dim3(TC_THREADS);
+        lc.blockDim = dim3(TC2_THREADS);
         lc.dynamicSmemBytes = smem2;
         cudaLaunchAttribute at;
         at.id = cudaLaunchAttributeClusterDimension;
@@ -264,14 +279,17 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
       });
       if (max_clusters > 0) {
         // Each CTA of the pair loads half of the 256-token slab.
-        CUtensorMap tm_t_half;
+        CUtensorMap tm_t_half, tm_aux2 = tm_aux;
         SAE_TRY(make_tmap(&tm_t_half, tok, B, d, TILE_N / 2));
+        // Side-tile stores go out in 128-token slabs.
+        if (Epi::kAux == AUX_STORE)
+          SAE_TRY(aux_tmap<Epi>(&tm_aux2, aux, F, B, TC2_STORE_ROWS));
         const int m_pairs = static_cast<int>(F / (2 * TILE_M));
         const int total_pairs = m_pairs * n_tiles;
         const int clusters = std::min(total_pairs, max_clusters);
         if (timer >= 0) timer_begin(timer, stream);
-        tc2_tile_gemm<Epi><<<2 * clusters, TC_THREADS, smem2, stream>>>(
-            tm_w, tm_t_half, tm_aux, m_pairs, n_tiles, static_cast<int>(d / TILE_K), e);
+        tc2_tile_gemm<Epi><<<2 * clusters, TC2_THREADS, smem2, stream>>>(
+            tm_w, tm_t_half, tm_aux2, m_pairs, n_tiles, static_cast<int>(d / TILE_K), e);
         const int rc = check_launch("tc2_tile_gemm");
         if (timer >= 0) timer_end(timer, stream);
         return rc;
@@ -360,6 +378,8 @@ extern "C" {
 int sae_b200_version(void) { return 1; }
 
 int64_t sae_b200_launch_count(void) { return g_launches.load(); }
+
+int64_t sae_b200_pre_pitch(int64_t n_tokens) { return pre_pitch(n_tokens); }
 
 int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event) {
   if (kernel != SAE_KERNEL_ENCODER_GEMM && kernel != SAE_KERNEL_GRAD_GEMM)
@@ -451,6 +471,7 @@ int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype
     e.n_tokens = static_cast<int>(B);
     e.n_features = static_cast<int>(F);
     e.mask_words = mask_words;
+    e.ldp = static_cast<int>(pre_pitch(B));
     SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), w.xc, F, B, d, e,
                              tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_ENCODER_GEMM,
                              w.pre));
@@ -473,7 +494,8 @@ int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype
   decode_kernel<XT, GG><<<DECODE_GRID, V * GG, dyn, stream>>>(                              \
       w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,             \
       static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), mask_words,   \
-      static_cast<float>(scale), w.go, x_hat_out, w.tok_sqerr, w.tok_cnt, w.gosum_part)
+      static_cast<int>(pre_pitch(B)), static_cast<float>(scale), w.go, x_hat_out,           \
+      w.tok_sqerr, w.tok_cnt, w.gosum_part)
     if (x_dtype == SAE_DTYPE_BF16) {
       if (G >= 4) SAE_DECODE(bf16, 4);
       else if (G == 2 || G == 3) SAE_DECODE(bf16, 2);
@@ -528,6 +550,7 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
     e.thr_part = w.thr_part;
     e.dbenc_part = w.dbenc_part;
     e.dense_dpre = dense_scratch;
+    e.ldp = static_cast<int>(pre_pitch(B));
     SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_dec_bf16), w.go, F, B, d, e,
                              tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_GRAD_GEMM,
                              w.pre));
@@ -566,16 +589,19 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
   // dense fallback: dW_enc = dpre^T xc, dW_dec = acts^T go
   {
     dim3 grid(static_cast<unsigned>((d + GG_T - 1) / GG_T), static_cast<unsigned>((F + GG_T - 1) / GG_T));
+    // dense_scratch holds [F, ldp] (feature-major, like pre)
+    const int64_t ldp = pre_pitch(B);
     gemm_generic_kernel<bf16, bf16, float><<<grid, 256, 0, stream>>>(
-        F, d, B, 1.f, dense_scratch, 1, F, w.xc, 1, d, acc ? 1.f : 0.f, grads->W_enc, d, 1,
+        F, d, B, 1.f, dense_scratch, ldp, 1, w.xc, 1, d, acc ? 1.f : 0.f, grads->W_enc, d, 1,
         nullptr);
     SAE_TRY(check_launch("gemm_generic_kernel(dW_enc)"));
     if (g_wdec != nullptr) {
-      gated_pre_kernel<<<grid_for(B * F, 256), 256, 0, stream>>>(w.pre, w.theta, B, F,
+      gated_pre_kernel<<<grid_for(B * F, 256), 256, 0, stream>>>(w.pre, w.theta, B, F, ldp,
                                                                  dense_scratch);
       SAE_TRY(check_launch("gated_pre_kernel"));
       gemm_generic_kernel<bf16, bf16, float><<<grid, 256, 0, stream>>>(
-          F, d, B, 1.f, dense_scratch, 1, F, w.go, 1, d, acc ? 1.f : 0.f, g_wdec, d, 1, nullptr);
+          F, d, B, 1.f, dense_scratch, ldp, 1, w.go, 1, d, acc ? 1.f : 0.f, g_wdec, d, 1,
+          nullptr);
       SAE_TRY(check_launch("gemm_generic_kernel(dW_dec)"));
     }
   }

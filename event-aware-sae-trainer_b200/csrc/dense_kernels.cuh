@@ -209,13 +209,17 @@ __global__ void to_bf16_kernel(const float* __restrict__ src, bf16* __restrict__
 }
 
 // Dense activations for the dense backward: acts = pre where pre > theta.
+// (feature-major [F, ldp] in and out)
 __global__ void gated_pre_kernel(const bf16* __restrict__ pre, const float* __restrict__ theta,
-                                 int64_t n_tokens, int64_t n_features, bf16* __restrict__ out) {
+                                 int64_t n_tokens, int64_t n_features, int64_t ldp,
+                                 bf16* __restrict__ out) {
   const int64_t n = n_tokens * n_features;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const float p = __bfloat162float(pre[i]);
-    out[i] = (p > theta[i % n_features]) ? pre[i] : __float2bfloat16_rn(0.f);
+    const int64_t f = i / n_tokens, t = i - f * n_tokens;
+    const size_t o = static_cast<size_t>(f) * ldp + t;
+    const float p = __bfloat162float(pre[o]);
+    out[o] = (p > theta[f]) ? pre[o] : __float2bfloat16_rn(0.f);
   }
 }
 

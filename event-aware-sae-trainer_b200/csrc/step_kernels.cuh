@@ -125,18 +125,31 @@ __global__ void prep_kernel(const XT* __restrict__ x, const float* __restrict__ 
   }
 }
 
+// ------------------------------------------------- side-tile helpers
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// The pre-activations of a microbatch are kept feature-major, [F, ldp] bf16
+// (ldp = n_tokens rounded up to 64): the tile epilogues, where a thread owns
+// one feature, then read and write 8 consecutive tokens per 16-byte access.
+
 // -------------------------------------------------- encoder tile epilogue
 // pre = bf16(acc + bf16(b_enc)) (cuBLAS addmm with a bf16 bias); gate bit =
 // float(pre) > theta. Stores pre, one 32-feature mask word per token per
 // warp, and the active-token count of each feature in this 256-token tile.
 struct EncodeEpi {
   static constexpr int kAux = AUX_STORE;   // pre goes out through a TMA store
+  static constexpr bool kAuxFeatureMajor = true;
   const float* theta;
   const float* b_enc;
-  bf16* pre;
+  bf16* pre;          // [F, ldp]
   uint32_t* mask;
   int* tile_cnt;
-  int n_tokens, n_features, mask_words;
+  int n_tokens, n_features, mask_words, ldp;
   // per-thread tile state
   int f, n0, lane, word, row;
   float th, bias;
@@ -158,22 +171,39 @@ struct EncodeEpi {
     cnt = 0;
   }
   __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
+    const int t0 = n0 + c;
+    const int nj = row_ok ? min(32, n_tokens - t0) : 0;
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 s = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), make_float2(bias, bias));
+      pk[i] = pack_bf2(s.x, s.y);
+    }
     uint32_t myword = 0;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const int t = n0 + c + j;
-      const bool ok = row_ok && t < n_tokens;
-      const bf16 p = __float2bfloat16_rn(v[j] + bias);
-      if (aux != nullptr)
-        aux[(c + j) * TILE_M + row] = p;   // rows past n_tokens are clipped by the store
-      else if (ok)
-        pre[static_cast<size_t>(t) * n_features + f] = p;
-      const bool act = ok && (__bfloat162float(p) > th);
+      const float p = (j & 1) ? bf_hi(pk[j >> 1]) : bf_lo(pk[j >> 1]);
+      const bool act = (j < nj) && (p > th);
       const uint32_t bal = __ballot_sync(0xffffffffu, act);
       if (lane == j) myword = bal;
       cnt += act ? 1 : 0;
     }
-    const int t = n0 + c + lane;
+    if (aux != nullptr) {
+      // tokens past n_tokens are clipped by the TMA store
+      uint8_t* base = reinterpret_cast<uint8_t*>(aux);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(base + aux_fm_offset(row, (c >> 3) + q)) =
+            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    } else if (row_ok) {
+      bf16* dst = pre + static_cast<size_t>(f) * ldp + t0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (8 * q < nj)   // ldp is a multiple of 64: whole 8-token groups stay in the row
+          *reinterpret_cast<uint4*>(dst + 8 * q) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    }
+    const int t = t0 + lane;
     if (t < n_tokens && word < mask_words)
       mask[static_cast<size_t>(t) * mask_words + word] = myword;
   }
@@ -182,9 +212,10 @@ struct EncodeEpi {
   }
 };
 
-// pre only (module API encode_pre in bf16 mode).
+// pre only, token-major [B, F] (module API encode_pre in bf16 mode).
 struct PreOnlyEpi {
   static constexpr int kAux = AUX_STORE;
+  static constexpr bool kAuxFeatureMajor = false;
   const float* b_enc;
   bf16* pre;
   int n_tokens, n_features;
@@ -225,19 +256,20 @@ struct PreOnlyEpi {
 // pairs are appended to the feature-major CSR (token, pre, dpre) at the
 // positions the scan assigned, in token order.
 struct GradEpi {
+  static constexpr int kAux = AUX_LOAD;   // the pre tile arrives in shared memory by TMA
+  static constexpr bool kAuxFeatureMajor = true;
   const float* theta;
-  const bf16* pre;
+  const bf16* pre;    // [F, ldp]
   const int* col_offs;
   const int* tile_base;
   const SaeB200StepStats* stats;
   float eps;
-  int n_tokens, n_features;
+  int n_tokens, n_features, ldp;
   int* csr_tok;
   uint32_t* csr_val;
   float* thr_part;
   float* dbenc_part;
-  bf16* dense_dpre;   // non-null: write the gated gradient densely instead of the CSR
-  static constexpr int kAux = AUX_LOAD;   // the pre tile arrives in shared memory by TMA
+  bf16* dense_dpre;   // non-null: write the gated gradient densely ([F, ldp]) instead of the CSR
   // per-thread tile state
   int f, n0, pos, row;
   float th, gate_grad, thr_sum, db_sum;
@@ -262,39 +294,71 @@ struct GradEpi {
   }
   __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
     if (!row_ok) return;
-    // All 32 pre-activation loads of the chunk are issued before any is used,
-    // so a warp keeps 32 loads (32 x 64 contiguous bytes) in flight.
     const int t0 = n0 + c;
     const int nj = min(32, n_tokens - t0);
-    float pv[32];
+    uint32_t pw[16];   // 32 bf16 pre-activations, two per word
     if (aux != nullptr) {
+      const uint8_t* base = reinterpret_cast<const uint8_t*>(aux);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) pv[j] = __bfloat162float(aux[(c + j) * TILE_M + row]);
-    } else {
-      const bf16* pcol = pre + static_cast<size_t>(t0) * n_features + f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        pv[j] = (j < nj) ? __bfloat162float(pcol[static_cast<size_t>(j) * n_features]) : 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j >= nj) break;
-      const int t = t0 + j;
-      const float gf = bf16_round(v[j]);
-      const float p = pv[j];
-      const float comb = __fadd_rn(__fmul_rn(p, gf), gate_grad);
-      if (fabsf(__fsub_rn(p, th)) < eps) thr_sum += comb;
-      const bool act = p > th;
-      if (dense_dpre != nullptr)
-        dense_dpre[static_cast<size_t>(t) * n_features + f] = __float2bfloat16_rn(act ? gf : 0.f);
-      if (act) {
-        db_sum += gf;
-        if (write_csr) {
-          csr_tok[pos] = t;
-          csr_val[pos] = pack2(p, gf);
-        }
-        ++pos;
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = *reinterpret_cast<const uint4*>(base + aux_fm_offset(row, (c >> 3) + q));
+        pw[4 * q] = u.x;
+        pw[4 * q + 1] = u.y;
+        pw[4 * q + 2] = u.z;
+        pw[4 * q + 3] = u.w;
       }
+    } else {
+      const bf16* src = pre + static_cast<size_t>(f) * ldp + t0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (8 * q < nj) u = *reinterpret_cast<const uint4*>(src + 8 * q);
+        pw[4 * q] = u.x;
+        pw[4 * q + 1] = u.y;
+        pw[4 * q + 2] = u.z;
+        pw[4 * q + 3] = u.w;
+      }
+    }
+    const float2 gg = make_float2(gate_grad, gate_grad);
+    uint32_t dw[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t gw = pack_bf2(v[2 * i], v[2 * i + 1]);   // grad_feat as bf16
+      const float2 p = make_float2(bf_lo(pw[i]), bf_hi(pw[i]));
+      const float2 g = make_float2(bf_lo(gw), bf_hi(gw));
+      const float2 comb = __fadd2_rn(__fmul2_rn(p, g), gg);
+      const int j = 2 * i;
+      if (j < nj && fabsf(__fsub_rn(p.x, th)) < eps) thr_sum += comb.x;
+      if (j + 1 < nj && fabsf(__fsub_rn(p.y, th)) < eps) thr_sum += comb.y;
+      const bool a0 = (j < nj) && p.x > th;
+      const bool a1 = (j + 1 < nj) && p.y > th;
+      dw[i] = (a0 ? (gw & 0xFFFFu) : 0u) | (a1 ? (gw & 0xFFFF0000u) : 0u);
+      if (a0 | a1) {   // rare: ~L0 / F of the entries
+        if (a0) {
+          db_sum += g.x;
+          if (write_csr) {
+            csr_tok[pos] = n0 + c + j;
+            csr_val[pos] = (pw[i] & 0xFFFFu) | (gw << 16);
+          }
+          ++pos;
+        }
+        if (a1) {
+          db_sum += g.y;
+          if (write_csr) {
+            csr_tok[pos] = n0 + c + j + 1;
+            csr_val[pos] = (pw[i] >> 16) | (gw & 0xFFFF0000u);
+          }
+          ++pos;
+        }
+      }
+    }
+    if (dense_dpre != nullptr) {
+      bf16* dst = dense_dpre + static_cast<size_t>(f) * ldp + t0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (8 * q < nj)
+          *reinterpret_cast<uint4*>(dst + 8 * q) =
+              make_uint4(dw[4 * q], dw[4 * q + 1], dw[4 * q + 2], dw[4 * q + 3]);
     }
   }
   __device__ __forceinline__ void end_tile() {
@@ -364,7 +428,7 @@ __global__ void __launch_bounds__(1024)
     decode_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
                   const bf16* __restrict__ w_dec, const float* __restrict__ b_dec,
                   const XT* __restrict__ x, int64_t n_tokens, int d, int n_features,
-                  int mask_words, float go_scale, bf16* __restrict__ go,
+                  int mask_words, int ldp, float go_scale, bf16* __restrict__ go,
                   float* __restrict__ x_hat, float* __restrict__ tok_sqerr,
                   int* __restrict__ tok_cnt, float* __restrict__ gosum_part) {
   __shared__ int s_f[DECODE_LIST_CAP];
@@ -409,7 +473,7 @@ __global__ void __launch_bounds__(1024)
             if (rank >= win && rank < win + DECODE_LIST_CAP) {
               const int f = w * 32 + bit;
               s_f[rank - win] = f;
-              s_v[rank - win] = __bfloat162float(pre[b * n_features + f]);
+              s_v[rank - win] = __bfloat162float(pre[static_cast<size_t>(f) * ldp + b]);
             }
             ++rank;
           }

@@ -41,12 +41,27 @@ constexpr int TC_GROUP_M = 16;    // feature tiles per rasterisation group
 constexpr int TC_BARRIER_BYTES = 256;
 constexpr uint32_t TC_TMEM_COLS = 2 * TILE_N;     // two fp32 accumulators
 
-// Auxiliary [TILE_N tokens][TILE_M features] bf16 tile (64 KiB) that rides
-// along with each output tile: loaded by TMA for epilogues that read a
-// token-major [B, F] tensor (AUX_LOAD), or written by the epilogue and stored
-// by TMA for epilogues that produce one (AUX_STORE).
+// Auxiliary 128-feature x 256-token bf16 tile (64 KiB) that rides along with
+// each output tile: loaded by TMA for epilogues that read a [B, F]-sized
+// tensor (AUX_LOAD), or written by the epilogue and stored by TMA for
+// epilogues that produce one (AUX_STORE). Two layouts:
+//  * token-major (Epi::kAuxFeatureMajor == false): one [256 tokens][128
+//    features] box, no swizzle, for a token-major [B, F] global tensor;
+//  * feature-major: four [128 features][64 tokens] boxes with 128-byte
+//    swizzle, for a feature-major [F, ldp] global tensor. A thread that owns
+//    one feature moves 8 tokens with one 16-byte shared-memory access, and
+//    the swizzle spreads the 8 threads of each access phase over all banks.
 enum AuxMode { AUX_NONE = 0, AUX_LOAD = 1, AUX_STORE = 2 };
 constexpr int TC_AUX_BYTES = TILE_N * TILE_M * 2;
+constexpr int AUX_FM_BOX_TOKENS = 64;
+constexpr int AUX_FM_BOX_BYTES = TILE_M * AUX_FM_BOX_TOKENS * 2;   // 16 KiB
+
+// Byte offset of the 16-byte group holding tokens [8 g, 8 g + 8) of feature
+// row `row` in a feature-major side tile (g = 0..31).
+__device__ __forceinline__ uint32_t aux_fm_offset(int row, int g) {
+  return static_cast<uint32_t>((g >> 3) * AUX_FM_BOX_BYTES + row * 128 +
+                               (((g & 7) ^ (row & 7)) << 4));
+}
 
 template <int AUX>
 struct TcConfig {
@@ -58,13 +73,44 @@ struct TcConfig {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t x,
-                                             int32_t y) {
+__device__ __forceinline__ void tma_store_2d_nocommit(const void* tmap, const void* smem_src,
+                                                      int32_t x, int32_t y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
       "r"(smem_u32(smem_src)), "r"(x), "r"(y)
       : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Side-tile TMA load of the tile at (first feature f0, first token t0).
+template <class Epi>
+__device__ __forceinline__ void aux_load_tile(bf16* s_aux, const CUtensorMap* tm, uint64_t* bar,
+                                              int f0, int t0) {
+  if constexpr (Epi::kAuxFeatureMajor) {
+#pragma unroll
+    for (int b = 0; b < TILE_N / AUX_FM_BOX_TOKENS; ++b)
+      tma_load_2d(reinterpret_cast<uint8_t*>(s_aux) + b * AUX_FM_BOX_BYTES, tm, bar,
+                  t0 + b * AUX_FM_BOX_TOKENS, f0);
+  } else {
+    tma_load_2d(s_aux, tm, bar, f0, t0);
+  }
+}
+
+// Side-tile TMA store of tokens [r0, r0 + n) of the tile (one bulk group).
+// Token-major tiles use a tensor map whose box is n tokens high.
+template <class Epi>
+__device__ __forceinline__ void aux_store_rows(const bf16* s_aux, const CUtensorMap* tm, int f0,
+                                               int t0, int r0, int n) {
+  if constexpr (Epi::kAuxFeatureMajor) {
+    for (int b = r0 / AUX_FM_BOX_TOKENS; b < (r0 + n) / AUX_FM_BOX_TOKENS; ++b)
+      tma_store_2d_nocommit(tm, reinterpret_cast<const uint8_t*>(s_aux) + b * AUX_FM_BOX_BYTES,
+                            t0 + b * AUX_FM_BOX_TOKENS, f0);
+  } else {
+    tma_store_2d_nocommit(tm, s_aux + r0 * TILE_M, f0, t0 + r0);
+  }
+  bulk_commit();
 }
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -191,7 +237,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(aux_full, TC_AUX_BYTES);
-          tma_load_2d(s_aux, &tm_aux, aux_full, tc.m * TILE_M, tc.n * TILE_N);
+          aux_load_tile<Epi>(s_aux, &tm_aux, aux_full, tc.m * TILE_M, tc.n * TILE_N);
           aux_issued = true;
           aux_parity = ph;
         }
@@ -296,7 +342,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (AUX == AUX_STORE) {
         fence_proxy_async_smem();
         if (!epi_sync()) break;
-        if (issuer) tma_store_2d(&tm_aux, s_aux, tc.m * TILE_M, tc.n * TILE_N);
+        if (issuer) aux_store_rows<Epi>(s_aux, &tm_aux, tc.m * TILE_M, tc.n * TILE_N, 0, TILE_N);
       }
     }
     if (AUX == AUX_STORE && issuer) bulk_wait_all();
@@ -410,6 +456,14 @@ __device__ __forceinline__ void tc_commit_pair_local(uint64_t* bar) {
       : "memory");
 }
 
+constexpr int TC2_THREADS = 224;   // warps 0 TMA, 1 MMA, 2..5 epilogue, 6 side-tile TMA
+constexpr int TC2_AUX_WARP = 6;
+constexpr int TC2_STORE_ROWS = 128;   // tokens per side-tile TMA store (two per tile)
+
+__device__ __forceinline__ void bulk_wait_read_le1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
 constexpr int TC2_A_BYTES = TILE_M * TILE_K * 2;      // 16 KiB: this CTA's 128 features
 constexpr int TC2_B_BYTES = (TILE_N / 2) * TILE_K * 2;  // 16 KiB: this CTA's 128 tokens
 constexpr int TC2_STAGE_BYTES = TC2_A_BYTES + TC2_B_BYTES;
@@ -423,7 +477,7 @@ struct Tc2Config {
 
 // Pair tile t -> (feature pair index, token tile), same grouping as tile_coord.
 template <class Epi>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
     tc2_tile_gemm(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_t,
                   const __grid_constant__ CUtensorMap tm_aux, int m_pairs, int n_tiles,
                   int k_blocks, const Epi epi) {
@@ -493,10 +547,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------- producer
-      uint32_t aux_parity = 0;
-      bool ok = true, aux_issued = false;
-      int kit = 0, it = 0;
-      for (int t = pair; t < total && ok; t += pairs, ++it) {
+      bool ok = true;
+      int kit = 0;
+      for (int t = pair; t < total && ok; t += pairs) {
         const TileCoord tc = tile_coord(t, m_pairs, n_tiles);
         const int f0 = (2 * tc.m + static_cast<int>(rank)) * TILE_M;
         const int t0 = tc.n * TILE_N + static_cast<int>(rank) * (TILE_N / 2);
@@ -512,21 +565,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
           tma_load_2d_pair(s_a + s * TC2_A_BYTES, &tm_w, lbar, kb * TILE_K, f0);
           tma_load_2d_pair(s_b + s * TC2_B_BYTES, &tm_t, lbar, kb * TILE_K, t0);
         }
-        if (AUX == AUX_LOAD && ok) {
-          const uint32_t ph = it & 1;
-          if (!mbar_wait(aux_empty, ph ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(aux_full, TC_AUX_BYTES);
-          tma_load_2d(s_aux, &tm_aux, aux_full, f0, tc.n * TILE_N);
-          aux_issued = true;
-          aux_parity = ph;
-        }
       }
-      if (!ok && aux_issued) mbar_wait(aux_full, aux_parity, nullptr);
       // Operand copies of an aborted pipeline complete on the leader's full
       // barriers; the leader's MMA thread below drains them.
+    }
+  } else if (warp == TC2_AUX_WARP) {
+    if (AUX == AUX_LOAD && lane == 0) {
+      // ------------------------------------------------- side-tile producer
+      // Its own thread, so waiting for the previous tile's epilogue to free
+      // the buffer never holds up the operand loads of warp 0.
+      uint32_t aux_parity = 0;
+      bool aux_issued = false;
+      int it = 0;
+      for (int t = pair; t < total; t += pairs, ++it) {
+        const TileCoord tc = tile_coord(t, m_pairs, n_tiles);
+        const int f0 = (2 * tc.m + static_cast<int>(rank)) * TILE_M;
+        const uint32_t ph = it & 1;
+        if (!mbar_wait(aux_empty, ph ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(aux_full, TC_AUX_BYTES);
+        aux_load_tile<Epi>(s_aux, &tm_aux, aux_full, f0, tc.n * TILE_N);
+        aux_issued = true;
+        aux_parity = ph;
+      }
+      if (aux_issued && *abort_flag) mbar_wait(aux_full, aux_parity, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
@@ -582,13 +643,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       return r;
     };
     int it = 0;
-    for (int t = pair; t < total; t += pairs, ++it) {
+    bool ok = true;
+    for (int t = pair; t < total && ok; t += pairs, ++it) {
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      if (AUX == AUX_STORE) {
-        if (issuer) bulk_wait_read_all();
-        if (!epi_sync()) break;
-      }
       if (!mbar_wait(&acc_full[acc], aph, abort_flag)) break;
       if (AUX == AUX_LOAD && !mbar_wait(aux_full, it & 1, abort_flag)) break;
       tc_fence_after();
@@ -600,6 +658,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * TILE_N);
 #pragma unroll 1
       for (int c = 0; c < TILE_N; c += 32) {
+        if (AUX == AUX_STORE && (c % TC2_STORE_ROWS) == 0) {
+          // This slab's rows are free once the store of the same slab of the
+          // previous tile has read them out (one later store may be pending).
+          if (issuer) bulk_wait_read_le1();
+          if (!epi_sync()) {
+            ok = false;
+            break;
+          }
+        }
         float v[32];
         tmem_ld_32cols(t_row + c, v);
         if (c == TILE_N - 32) {
@@ -608,17 +675,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
           if (lane == 0) mbar_arrive_remote(leader_acc_empty[acc]);
         }
         e.chunk(c, v);
+        if (AUX == AUX_STORE && (c % TC2_STORE_ROWS) == TC2_STORE_ROWS - 32) {
+          fence_proxy_async_smem();
+          if (!epi_sync()) {
+            ok = false;
+            break;
+          }
+          const int r0 = c - (TC2_STORE_ROWS - 32);
+          if (issuer)
+            aux_store_rows<Epi>(s_aux, &tm_aux, m_tile * TILE_M, tc.n * TILE_N, r0,
+                                TC2_STORE_ROWS);
+        }
       }
+      if (!ok) break;
       if (AUX == AUX_LOAD) {
         __syncwarp();
         if (lane == 0) mbar_arrive(aux_empty);
       }
       e.end_tile();
-      if (AUX == AUX_STORE) {
-        fence_proxy_async_smem();
-        if (!epi_sync()) break;
-        if (issuer) tma_store_2d(&tm_aux, s_aux, m_tile * TILE_M, tc.n * TILE_N);
-      }
     }
     if (AUX == AUX_STORE && issuer) bulk_wait_all();
   }

@@ -119,6 +119,7 @@ _SIGNATURES = {
     "sae_b200_last_error": ([], ctypes.c_char_p),
     "sae_b200_get_device_status": ([POINTER(c_int), c_int], c_int),
     "sae_b200_launch_count": ([], c_int64),
+    "sae_b200_pre_pitch": ([c_int64], c_int64),
     "sae_b200_set_kernel_timer": ([c_int, c_void_p, c_void_p], c_int),
     "sae_b200_workspace_bytes": ([c_int64, c_int64, c_int64, c_int64, POINTER(c_size_t)], c_int),
     "sae_b200_workspace_offsets": ([c_int64, c_int64, c_int64, c_int64, POINTER(c_size_t)], c_int),
@@ -191,6 +192,11 @@ def call(name: str, *args) -> None:
 
 KERNEL_ENCODER_GEMM = 0
 KERNEL_GRAD_GEMM = 1
+
+
+def pre_pitch(n_tokens: int) -> int:
+    """Row pitch (tokens) of the feature-major [F, ldp] pre-activation arrays."""
+    return int(load().sae_b200_pre_pitch(n_tokens))
 
 
 def launch_count() -> int:

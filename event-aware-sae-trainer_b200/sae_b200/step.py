@@ -257,7 +257,7 @@ class FusedStep:
         grads = self._grads_struct()
         if st["csr_overflow"]:
             self.dense_fallbacks += 1
-            need = n * sae.n_features
+            need = L.pre_pitch(n) * sae.n_features   # [F, ldp] feature-major
             if self._dense_scratch is None or self._dense_scratch.numel() < need:
                 self._dense_scratch = torch.empty(need, device=self.device, dtype=torch.bfloat16)
             L.call("sae_b200_train_backward_dense", ctypes.byref(model), ctypes.byref(grads),

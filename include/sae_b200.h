@@ -138,13 +138,17 @@ int sae_b200_workspace_bytes(int64_t max_tokens, int64_t d_in, int64_t n_feature
 
 /* Byte offsets, inside the workspace of a step over n_tokens tokens, of the
  * intermediates a caller may inspect after sae_b200_train_forward/backward:
- * [0] theta f32 [F]        [1] xc bf16 [B, d]      [2] pre bf16 [B, F]
+ * [0] theta f32 [F]        [1] xc bf16 [B, d]
+ * [2] pre bf16, feature-major [F, ldp], ldp = sae_b200_pre_pitch(B)
  * [3] mask u32 [B, ceil(F/32)] (bit f%32 of word f/32: feature f active)
  * [4] go bf16 [B, d]       [5] per-token active count i32 [B]
  * [6] per-token squared error f32 [B]   [7] CSR row offsets i32 [F + 1]
  * [8] CSR token ids i32 [nnz]           [9] CSR values u32 [nnz]
  *     (low half: bf16 pre-activation, high half: bf16 gated grad_feat) */
 #define SAE_WS_N_OFFSETS 10
+/* Row pitch, in tokens, of the feature-major [F, ldp] pre-activation arrays:
+ * n_tokens rounded up to a multiple of 64, plus 64 (never a power of two). */
+int64_t sae_b200_pre_pitch(int64_t n_tokens);
 int sae_b200_workspace_offsets(int64_t n_tokens, int64_t d_in, int64_t n_features,
                                int64_t csr_capacity, size_t* offsets_out /* [10] */);
 
@@ -174,8 +178,8 @@ int sae_b200_train_backward(const SaeB200Model* model, const SaeB200Grads* grads
                             size_t workspace_bytes, SaeB200StepStats* stats, void* stream);
 
 /* Same gradients without the capacity limit, for microbatches whose active
- * set overflowed csr_capacity. dense_scratch: bf16 [n_tokens, F] device
- * buffer owned by the caller. */
+ * set overflowed csr_capacity. dense_scratch: bf16 device buffer of
+ * n_features * sae_b200_pre_pitch(n_tokens) elements owned by the caller. */
 int sae_b200_train_backward_dense(const SaeB200Model* model, const SaeB200Grads* grads,
                                   const SaeB200StepConfig* cfg, void* workspace,
                                   size_t workspace_bytes, SaeB200StepStats* stats,

@@ -75,6 +75,7 @@ def workspace_views(fs, n_tokens):
     d, F = sae.d_in, sae.n_features
     off = L.workspace_offsets(n_tokens, d, F, fs.csr_capacity)
     W = (F + 31) // 32
+    ldp = L.pre_pitch(n_tokens)
 
     def view(name, dtype, count):
         o = off[name]
@@ -84,7 +85,8 @@ def workspace_views(fs, n_tokens):
     return {
         "theta": view("theta", torch.float32, F),
         "xc": view("xc", torch.bfloat16, n_tokens * d).view(n_tokens, d),
-        "pre": view("pre", torch.bfloat16, n_tokens * F).view(n_tokens, F),
+        # feature-major [F, ldp]; returned as the [B, F] view
+        "pre": view("pre", torch.bfloat16, F * ldp).view(F, ldp)[:, :n_tokens].t(),
         "mask": view("mask", torch.int32, n_tokens * W).view(n_tokens, W),
         "go": view("go", torch.bfloat16, n_tokens * d).view(n_tokens, d),
         "tok_cnt": view("tok_cnt", torch.int32, n_tokens),
