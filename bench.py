@@ -41,6 +41,10 @@ D_IN, N_FEAT, TOKENS, K_TARGET = 1536, 49152, 32768, 50
 LAMBDA, MU, LR = 1e-3, 1e-2, 2e-4
 NORM_MU, NORM_SIGMA = math.log(60.0), 0.4
 POOL_BATCHES = 4
+# DRAM bytes per launch of the two tile GEMMs at 32768 tokens: an ncu capture of a
+# 4096-token launch (read + write) scaled by 8 (their traffic grows with the tokens).
+TRAFFIC_ENCODER_GEMM = 8 * (0.198459e9 + 0.385634e9)
+TRAFFIC_GRAD_GEMM = 8 * (0.604495e9 + 0.014044e9)
 WORKLOAD = ("d_in=1536 F=49152 32768-token microbatch, L0~50, bf16 activations / "
             "fp32 master+Adam (Gemma-4-E2B residual shape)")
 
@@ -304,9 +308,11 @@ def run_b200(args):
         gemm_flop = 2.0 * TOKENS * D_IN * N_FEAT
         enc_tf = gemm_flop / (enc_ms / 1e3) / 1e12
         grad_tf = gemm_flop / (grad_ms / 1e3) / 1e12
-        dom_ms, dom_tf, dom_name = ((enc_ms, enc_tf, "encoder tile GEMM (tcgen05) + JumpReLU epilogue")
-                                    if enc_ms >= grad_ms else
-                                    (grad_ms, grad_tf, "grad_feat tile GEMM (tcgen05) + STE epilogue"))
+        dom_ms, dom_tf, dom_name, dom_traffic = (
+            (enc_ms, enc_tf, "encoder tile GEMM (tcgen05 cta_group::2) + JumpReLU epilogue",
+             TRAFFIC_ENCODER_GEMM) if enc_ms >= grad_ms else
+            (grad_ms, grad_tf, "grad_feat tile GEMM (tcgen05 cta_group::2) + STE epilogue",
+             TRAFFIC_GRAD_GEMM))
         peak = peaks["bf16_sustained"]
         last = stats[-1]
         step_flop = 4.0 * TOKENS * D_IN * N_FEAT
@@ -330,7 +336,9 @@ def run_b200(args):
                          "achieved": dom_tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": dom_tf / peak,
                          "peak_source": f"bf16_tflops_sustained ({peaks['src']})",
-                         "traffic": None,
+                         "traffic": dom_traffic,
+                         "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                                         "4096-token launch, x8 for 32768 tokens",
                          "per_launch_flop": gemm_flop, "launch_ms": dom_ms},
             "kernels": {"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
                         "grad_gemm_ms": grad_ms, "grad_gemm_tflops": grad_tf,
