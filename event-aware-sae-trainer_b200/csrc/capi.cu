@@ -86,7 +86,11 @@ struct Layout {
 // Row pitch (tokens) of the feature-major pre-activations: whole 64-token
 // boxes plus one, so that the pitch is never a power of two (a 2^k-byte pitch
 // puts the 128 rows of every TMA box on the same DRAM channels).
-inline int64_t pre_pitch(int64_t B) { return (B + 63) / 64 * 64 + 64; }
+inline int64_t pre_pitch(int64_t B) {
+  int64_t p = (B + 63) / 64 * 64 + 64;
+  if ((p & (p - 1)) == 0) p += 64;
+  return p;
+}
 
 Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   Layout L{};

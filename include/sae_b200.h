@@ -147,7 +147,9 @@ int sae_b200_workspace_bytes(int64_t max_tokens, int64_t d_in, int64_t n_feature
  *     (low half: bf16 pre-activation, high half: bf16 gated grad_feat) */
 #define SAE_WS_N_OFFSETS 10
 /* Row pitch, in tokens, of the feature-major [F, ldp] pre-activation arrays:
- * n_tokens rounded up to a multiple of 64, plus 64 (never a power of two). */
+ * n_tokens rounded up to a multiple of 64, plus 64, plus another 64 if that
+ * is a power of two (a 2^k-byte pitch concentrates TMA boxes on few DRAM
+ * channels). */
 int64_t sae_b200_pre_pitch(int64_t n_tokens);
 int sae_b200_workspace_offsets(int64_t n_tokens, int64_t d_in, int64_t n_features,
                                int64_t csr_capacity, size_t* offsets_out /* [10] */);

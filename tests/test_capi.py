@@ -1,0 +1,64 @@
+"""The C ABI surface, without a GPU: the library loads, exports every function
+include/sae_b200.h declares, and rejects bad arguments with status codes
+before touching the device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "sae_b200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sae_b200_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_function():
+    from sae_b200 import _lib as L
+    lib = L.load()
+    names = _declared()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in the header but not exported"
+    # and the Python binding knows every one of them
+    assert set(names) == set(L.exported_symbols())
+
+
+def test_workspace_queries():
+    from sae_b200 import _lib as L
+    small = L.workspace_bytes(256, 128, 512, 1024)
+    big = L.workspace_bytes(32768, 1536, 49152, 32768 * 512)
+    assert 0 < small < big
+    off = L.workspace_offsets(300, 128, 512, 1024)
+    total = L.workspace_bytes(300, 128, 512, 1024)
+    assert len(set(off.values())) == len(off)            # distinct regions
+    assert all(v % 256 == 0 and v < total for v in off.values())
+    for n in (1, 63, 64, 65, 32768):
+        p = L.pre_pitch(n)
+        assert p >= n and p % 64 == 0 and (p & (p - 1)) != 0
+
+
+def test_bad_arguments_are_rejected_without_a_device():
+    from sae_b200 import _lib as L
+    lib = L.load()
+    assert lib.sae_b200_version() >= 1
+    rc = lib.sae_b200_train_forward(None, None, 0, None, None, 0, None, None, None, None)
+    assert rc == L.SAE_ERR_INVALID_ARGUMENT
+    assert b"model" in lib.sae_b200_last_error()
+    m = L.Model(0, 10, 1, 1, 1, 1, 1, 1, 1)
+    assert lib.sae_b200_grad_norm(ctypes.byref(m), None, 1.0, None, 0, None, None) != L.SAE_OK
+    out = ctypes.c_size_t(0)
+    assert lib.sae_b200_workspace_bytes(-1, 4, 4, 0, ctypes.byref(out)) == L.SAE_ERR_INVALID_ARGUMENT
+    with pytest.raises(L.SaeB200Error) as e:
+        L.call("sae_b200_gemm", 0, 4, 4, 1.0, None, 0, 1, 1, None, 0, 1, 1, 0.0, None, 0, 1, 1,
+               None, None)
+    assert e.value.code == L.SAE_ERR_INVALID_ARGUMENT
+    cfg = L.StepConfig(16, 1024, 0.0, 0.0, 0.0, 0.0, 1, 0, 1, 0)   # ste_bandwidth 0 is invalid
+    m = L.Model(64, 128, 16, 16, 16, 16, 16, 16, 16)
+    rc = lib.sae_b200_train_forward(ctypes.byref(m), 16, 1, ctypes.byref(cfg), 256, 1 << 30, 16,
+                                    None, None, None)
+    assert rc == L.SAE_ERR_INVALID_ARGUMENT
+    assert b"ste_bandwidth" in lib.sae_b200_last_error()
