@@ -205,6 +205,7 @@ def run_b200(args):
 
     import sae_b200
     from sae_b200 import _lib as L
+    from sae_b200 import atlas
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -237,11 +238,7 @@ def run_b200(args):
         torch.cuda.synchronize()
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return atlas.max_over_ranks(v, device=dev)
 
     # ---------------- device-resident timing (value)
     for i in range(args.warmup):
@@ -353,7 +350,7 @@ def run_b200(args):
             "gpu_launches": int(launches),
             "device_status": status,
         }
-        if args.cpu_baseline:
+        if args.cpu_baseline and world == 1:
             t_mb, t_adam, _ = cpu_reference_step_time(2048)
             cpu_step = (TOKENS // 2048) * t_mb + t_adam
             line["cpu_baseline"] = {
