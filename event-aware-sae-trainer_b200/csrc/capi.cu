@@ -101,7 +101,8 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
     return o;
   };
   const size_t W = static_cast<size_t>((F + 31) / 32);
-  const size_t nT = static_cast<size_t>((B + TILE_N - 1) / TILE_N);
+  // per-feature counts and partial sums per 128-token half of each token tile
+  const size_t nT = 2 * static_cast<size_t>((B + TILE_N - 1) / TILE_N);
   L.theta = take(F * 4);
   L.xc = take(B * d * 2);
   L.pre = take(static_cast<size_t>(F) * pre_pitch(B) * 2);   // feature-major [F, ldp]
@@ -482,7 +483,7 @@ int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype
   }
   // 3. per-feature scans -> CSR offsets
   scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(w.tile_cnt, w.col_tot, fired,
-                                                            n_tiles, static_cast<int>(F));
+                                                            2 * n_tiles, static_cast<int>(F));
   SAE_TRY(check_launch("scan_columns_kernel"));
   scan_offsets_kernel<<<1, 1024, 0, stream>>>(w.col_tot, w.col_offs, static_cast<int>(F),
                                               cfg->csr_capacity, stats, w.counters);
@@ -561,7 +562,7 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
   }
   // 2. per-feature gradients (threshold STE, b_enc)
   feature_grads_kernel<<<grid_for(F, 256), 256, 0, stream>>>(
-      w.thr_part, w.dbenc_part, w.theta, n_tiles, static_cast<int>(F), cfg->ste_bandwidth, acc,
+      w.thr_part, w.dbenc_part, w.theta, 2 * n_tiles, static_cast<int>(F), cfg->ste_bandwidth, acc,
       grads->log_threshold, grads->b_enc, w.db_enc);
   SAE_TRY(check_launch("feature_grads_kernel"));
   // 3. b_dec gradient

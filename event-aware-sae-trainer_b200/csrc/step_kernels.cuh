@@ -140,7 +140,8 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
 // -------------------------------------------------- encoder tile epilogue
 // pre = bf16(acc + bf16(b_enc)) (cuBLAS addmm with a bf16 bias); gate bit =
 // float(pre) > theta. Stores pre, one 32-feature mask word per token per
-// warp, and the active-token count of each feature in this 256-token tile.
+// warp, and the active-token count of each feature in each 128-token half of
+// the tile (the unit the epilogue warps split a tile into).
 struct EncodeEpi {
   static constexpr int kAux = AUX_STORE;   // pre goes out through a TMA store
   static constexpr bool kAuxFeatureMajor = true;
@@ -168,8 +169,8 @@ struct EncodeEpi {
     th = row_ok ? theta[f] : __int_as_float(0x7f800000);
     bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
     word = (m_tile * TILE_M + q * 32) >> 5;
-    cnt = 0;
   }
+  __device__ __forceinline__ void begin_half(int) { cnt = 0; }
   __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
     const int t0 = n0 + c;
     const int nj = row_ok ? min(32, n_tokens - t0) : 0;
@@ -207,9 +208,10 @@ struct EncodeEpi {
     if (t < n_tokens && word < mask_words)
       mask[static_cast<size_t>(t) * mask_words + word] = myword;
   }
-  __device__ __forceinline__ void end_tile() {
-    if (row_ok) tile_cnt[static_cast<size_t>(n0 / TILE_N) * n_features + f] = cnt;
+  __device__ __forceinline__ void end_half(int h) {
+    if (row_ok) tile_cnt[static_cast<size_t>(n0 / HALF_N + h) * n_features + f] = cnt;
   }
+  __device__ __forceinline__ void end_tile() {}
 };
 
 // pre only, token-major [B, F] (module API encode_pre in bf16 mode).
@@ -232,6 +234,8 @@ struct PreOnlyEpi {
     row_ok = f < n_features;
     bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
   }
+  __device__ __forceinline__ void begin_half(int) {}
+  __device__ __forceinline__ void end_half(int) {}
   __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -252,7 +256,7 @@ struct PreOnlyEpi {
 //   combined = pre * grad_feat + gate_grad                   (hook, 805-817)
 //   STE sum  += combined   where |pre - theta| < eps          (818-825)
 //   dpre      = grad_feat  where pre > theta                   (grad_pre, gated)
-// The per-feature sums of this tile go to thr_part / dbenc_part; active
+// The per-feature sums of each 128-token half go to thr_part / dbenc_part; active
 // pairs are appended to the feature-major CSR (token, pre, dpre) at the
 // positions the scan assigned, in token order.
 struct GradEpi {
@@ -286,8 +290,10 @@ struct GradEpi {
     th = row_ok ? theta[f] : 0.f;
     gate_grad = stats->gate_grad;
     write_csr = (dense_dpre == nullptr) && (stats->csr_overflow == 0);
+  }
+  __device__ __forceinline__ void begin_half(int h) {
     pos = (row_ok && write_csr)
-              ? col_offs[f] + tile_base[static_cast<size_t>(n_tile) * n_features + f]
+              ? col_offs[f] + tile_base[static_cast<size_t>(n0 / HALF_N + h) * n_features + f]
               : 0;
     thr_sum = 0.f;
     db_sum = 0.f;
@@ -361,12 +367,13 @@ struct GradEpi {
               make_uint4(dw[4 * q], dw[4 * q + 1], dw[4 * q + 2], dw[4 * q + 3]);
     }
   }
-  __device__ __forceinline__ void end_tile() {
+  __device__ __forceinline__ void end_half(int h) {
     if (!row_ok) return;
-    const size_t i = static_cast<size_t>(n0 / TILE_N) * n_features + f;
+    const size_t i = static_cast<size_t>(n0 / HALF_N + h) * n_features + f;
     thr_part[i] = thr_sum;
     dbenc_part[i] = db_sum;
   }
+  __device__ __forceinline__ void end_tile() {}
 };
 
 // ------------------------------------------------------------------- scans

@@ -33,6 +33,7 @@ namespace sae {
 constexpr int TILE_M = 128;   // features per tile (TMEM lanes)
 constexpr int TILE_N = 256;   // tokens per tile (TMEM columns per accumulator)
 constexpr int TILE_K = 64;    // d per pipeline stage (one 128-byte swizzle row)
+constexpr int HALF_N = TILE_N / 2;   // tokens per epilogue half: unit of the per-feature counts
 constexpr int TC_A_BYTES = TILE_M * TILE_K * 2;   // 16 KiB
 constexpr int TC_B_BYTES = TILE_N * TILE_K * 2;   // 32 KiB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
@@ -143,6 +144,8 @@ __device__ __forceinline__ TileCoord tile_coord(int t, int m_tiles, int n_tiles)
 //   begin_tile(m_tile, n_tile, row, quarter, lane, aux)   row = feature in tile;
 //       aux = the tile's [TILE_N][TILE_M] bf16 shared-memory buffer, or nullptr
 //       (CUDA-core path: the epilogue then uses global memory directly)
+//   begin_half(h) / end_half(h)   around the chunks of tokens [128 h, 128 h + 128);
+//       the paired kernel runs the two halves on different warps
 //   chunk(col, v[32])   v[j] = D[row, col + j], col in {0, 32, ..., 224};
 //                       called by all 32 lanes of a warp together (ballots)
 //   end_tile()
@@ -325,6 +328,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * TILE_N);
 #pragma unroll 1
       for (int c = 0; c < TILE_N; c += 32) {
+        if (c % (TILE_N / 2) == 0) e.begin_half(c / (TILE_N / 2));
         float v[32];
         tmem_ld_32cols(t_row + c, v);
         if (c == TILE_N - 32) {
@@ -333,6 +337,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
         }
         e.chunk(c, v);
+        if (c % (TILE_N / 2) == TILE_N / 2 - 32) e.end_half(c / (TILE_N / 2));
       }
       if (AUX == AUX_LOAD) {
         __syncwarp();
@@ -456,8 +461,11 @@ __device__ __forceinline__ void tc_commit_pair_local(uint64_t* bar) {
       : "memory");
 }
 
-constexpr int TC2_THREADS = 224;   // warps 0 TMA, 1 MMA, 2..5 epilogue, 6 side-tile TMA
-constexpr int TC2_AUX_WARP = 6;
+// warps: 0 operand TMA, 1 MMA, 2 side-tile TMA, 3..10 epilogue (two groups of
+// four, one per 128-token half of the tile)
+constexpr int TC2_THREADS = 352;
+constexpr int TC2_AUX_WARP = 2;
+constexpr int TC2_EPI_WARP0 = 3;
 constexpr int TC2_STORE_ROWS = 128;   // tokens per side-tile TMA store (two per tile)
 
 __device__ __forceinline__ void bulk_wait_read_le1() {
@@ -494,13 +502,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
   uint64_t* full = bars;                        // leader: both CTAs' TMA bytes
   uint64_t* empty = bars + STAGES;              // each CTA: stage free (leader's commit)
   uint64_t* acc_full = bars + 2 * STAGES;       // each CTA: accumulator ready
-  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // leader: 8 epilogue warps done
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;  // leader: 16 epilogue warps done
   uint64_t* drain = bars + 2 * STAGES + 4;
   uint64_t* aux_full = bars + 2 * STAGES + 5;
   uint64_t* aux_empty = bars + 2 * STAGES + 6;
-  uint64_t* epi_bar = bars + 2 * STAGES + 7;
-  uint64_t* done_bar = bars + 2 * STAGES + 8;   // end-of-kernel handshake of the pair
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 9);
+  uint64_t* epi_bar = bars + 2 * STAGES + 7;    // [2]: one per epilogue half
+  uint64_t* done_bar = bars + 2 * STAGES + 9;   // end-of-kernel handshake of the pair
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -516,12 +524,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 8);   // four epilogue warps in each CTA of the pair
+      mbar_init(&acc_empty[a], 16);   // eight epilogue warps in each CTA of the pair
+      mbar_init(&epi_bar[a], 128);
     }
     mbar_init(drain, 1);
     mbar_init(aux_full, 1);
-    mbar_init(aux_empty, 4);
-    mbar_init(epi_bar, 128);
+    mbar_init(aux_empty, 8);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -628,25 +636,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
         mbar_wait(drain, 0, nullptr);
       }
     }
-  } else {
+  } else if (warp >= TC2_EPI_WARP0) {
     // ------------------------------------------------------------ epilogue
+    // Eight warps: half h = 0 handles tokens [0, 128) of the tile, h = 1
+    // tokens [128, 256); within a half, warp w reads TMEM lane quarter w % 4.
+    const int h = (warp - TC2_EPI_WARP0) >> 2;
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const bool issuer = (warp == 2 && lane == 0);
-    const uint32_t leader_acc_empty[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0),
-                                          mapa_shared(smem_u32(&acc_empty[1]), 0)};
+    const bool issuer = (warp == TC2_EPI_WARP0 + 4 * h) && lane == 0;
+    const uint32_t leader_acc_empty0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    const uint32_t leader_acc_empty1 = mapa_shared(smem_u32(&acc_empty[1]), 0);
     uint32_t epi_phase = 0;
-    auto epi_sync = [&]() -> bool {
-      mbar_arrive(epi_bar);
-      const bool r = mbar_wait(epi_bar, epi_phase, abort_flag);
+    auto epi_sync = [&]() -> bool {   // the 128 threads of this half
+      mbar_arrive(&epi_bar[h]);
+      const bool r = mbar_wait(&epi_bar[h], epi_phase, abort_flag);
       epi_phase ^= 1;
       return r;
     };
+    const int c_begin = h * (TILE_N / 2), c_end = c_begin + TILE_N / 2;
     int it = 0;
     bool ok = true;
     for (int t = pair; t < total && ok; t += pairs, ++it) {
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
+      if (AUX == AUX_STORE) {
+        // this half's slab is free once its previous store has read it out
+        if (issuer) bulk_wait_read_all();
+        if (!epi_sync()) break;
+      }
       if (!mbar_wait(&acc_full[acc], aph, abort_flag)) break;
       if (AUX == AUX_LOAD && !mbar_wait(aux_full, it & 1, abort_flag)) break;
       tc_fence_after();
@@ -654,45 +671,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
       const int m_tile = 2 * tc.m + static_cast<int>(rank);
       Epi e = epi;
       e.begin_tile(m_tile, tc.n, row, q, lane, AUX == AUX_NONE ? nullptr : s_aux);
+      e.begin_half(h);
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * TILE_N);
 #pragma unroll 1
-      for (int c = 0; c < TILE_N; c += 32) {
-        if (AUX == AUX_STORE && (c % TC2_STORE_ROWS) == 0) {
-          // This slab's rows are free once the store of the same slab of the
-          // previous tile has read them out (one later store may be pending).
-          if (issuer) bulk_wait_read_le1();
-          if (!epi_sync()) {
-            ok = false;
-            break;
-          }
-        }
+      for (int c = c_begin; c < c_end; c += 32) {
         float v[32];
         tmem_ld_32cols(t_row + c, v);
-        if (c == TILE_N - 32) {
+        if (c == c_end - 32) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_remote(leader_acc_empty[acc]);
+          if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
         }
         e.chunk(c, v);
-        if (AUX == AUX_STORE && (c % TC2_STORE_ROWS) == TC2_STORE_ROWS - 32) {
-          fence_proxy_async_smem();
-          if (!epi_sync()) {
-            ok = false;
-            break;
-          }
-          const int r0 = c - (TC2_STORE_ROWS - 32);
-          if (issuer)
-            aux_store_rows<Epi>(s_aux, &tm_aux, m_tile * TILE_M, tc.n * TILE_N, r0,
-                                TC2_STORE_ROWS);
-        }
       }
-      if (!ok) break;
+      e.end_half(h);
       if (AUX == AUX_LOAD) {
         __syncwarp();
         if (lane == 0) mbar_arrive(aux_empty);
       }
       e.end_tile();
+      if (AUX == AUX_STORE) {
+        fence_proxy_async_smem();
+        if (!epi_sync()) break;
+        if (issuer)
+          aux_store_rows<Epi>(s_aux, &tm_aux, m_tile * TILE_M, tc.n * TILE_N, c_begin,
+                              TILE_N / 2);
+      }
     }
     if (AUX == AUX_STORE && issuer) bulk_wait_all();
   }
@@ -732,6 +737,7 @@ __global__ void __launch_bounds__(TILE_M)
   Epi e = epi;
   e.begin_tile(m_tile, n_tile, row, q, lane, nullptr);
   for (int c = 0; c < TILE_N; c += 32) {
+    if (c % (TILE_N / 2) == 0) e.begin_half(c / (TILE_N / 2));
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = 0.f;
@@ -761,6 +767,7 @@ __global__ void __launch_bounds__(TILE_M)
     }
     (void)f;
     e.chunk(c, v);
+    if (c % (TILE_N / 2) == TILE_N / 2 - 32) e.end_half(c / (TILE_N / 2));
   }
   e.end_tile();
 }
