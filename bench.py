@@ -5,18 +5,24 @@ bf16 synthetic superposition activations (50 of 49152 unit directions per
 token, Exponential(1) magnitudes, N(0, 0.05^2) noise, per-token norm
 LogNormal(log 60, 0.4)), K = 50, lambda = 1e-3, mu = 1e-2, lr = 2e-4, fp32
 master weights and Adam state. Thresholds are calibrated once (untimed) so
-that the mean L0 is ~50, the trained-like state the metric is quoted at.
+that the mean L0 is ~50, the trained-like state the metric is quoted at, and
+a proportional threshold nudge after every step (the trainer's L0
+controller) keeps it there.
 
 A step is the reference loop body: forward, backward, global clip, Adam with
 the fused decoder/encoder renormalisation, with the loop's stats read-back
 before the optimizer step.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+                    [--workload atlas|sharded]
 
 Under torchrun every rank trains its own SAE (one layer per GPU, the atlas
 layout): no data-path collective, weak scaling; the timing is the max over
-ranks. `--impl reference` times the oracle's CPU restatement of the reference
-step on this host's cores (rank 0 only).
+ranks. `--workload sharded` instead trains one wide SAE (d_in = 4096,
+F = 131072, K = 64, LogNormal(log 80, 0.4) norms) with its dictionary split
+over the ranks and three all-reduces per step (strong scaling).
+`--impl reference` times the oracle's CPU restatement of the reference step on
+this host's cores (rank 0 only).
 """
 from __future__ import annotations
 
@@ -179,7 +185,157 @@ def run_reference(args):
 
 
 # -------------------------------------------------------------- GPU arm
-def calibrate(sae, pool, target_l0):
+WORKLOADS = {
+    # the metric's configuration; under torchrun one layer's SAE per GPU (atlas)
+    "atlas": dict(d=D_IN, F=N_FEAT, tokens=TOKENS, k=K_TARGET, norm_mu=NORM_MU,
+                  norm_sigma=NORM_SIGMA, lr=LR, description=WORKLOAD),
+    # one wide SAE, dictionary split over the GPUs (strong scaling)
+    "sharded": dict(d=4096, F=131072, tokens=32768, k=64, norm_mu=math.log(80.0),
+                    norm_sigma=0.4, lr=LR,
+                    description=("wide SAE d_in=4096 F=131072, 32768-token microbatch, K=64, "
+                                 "dictionary split evenly over the GPUs, all-reduce of the "
+                                 "partial x_hat + L0 counts, b_dec gradient and clip norm")),
+}
+
+
+INFER = dict(d=2304, F=65536, tokens=65536, k=80, norm_mu=math.log(60.0), norm_sigma=0.4,
+             description=("encode + gathered decode inference: d_in=2304 F=65536, 65536 bf16 "
+                          "tokens, per-feature log-thresholds ~ N(c, 0.3^2) with c set so the "
+                          "mean L0 is ~80 (80 active directions per token)"))
+
+
+def run_inference(args):
+    """Inference configuration: encoder GEMM + JumpReLU gate + gathered decode
+    (sae_b200_encode_decode), reported as tokens/s with the gathered decode's
+    HBM roofline. Under torchrun every rank runs its own replica."""
+    import torch
+    import torch.distributed as dist
+
+    import sae_b200
+    from sae_b200 import _lib as L
+    from sae_b200 import atlas
+
+    wl = INFER
+    d, F, tokens = wl["d"], wl["F"], wl["tokens"]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=300))
+    sae = sae_b200.make_shard_sae(d, F, 0, 1, seed=11 + rank, device=dev)
+    pool = [sae_b200.superposition_batch(tokens, d, F, wl["k"], wl["norm_mu"], wl["norm_sigma"],
+                                         seed=31 + 100 * rank + 7 * i, device=dev)
+            for i in range(2)]
+    with torch.no_grad():
+        sae.b_dec.copy_(pool[0].float().mean(0))
+        g = torch.Generator(device=dev).manual_seed(3)
+        z = 0.3 * torch.randn(F, generator=g, device=dev)
+        lo, hi = math.log(0.01), math.log(100.0)       # bisection on the common scale c
+        for _ in range(30):
+            c = 0.5 * (lo + hi)
+            sae.log_threshold.copy_(z + c)
+            _, cnt = sae.reconstruct(pool[0][:8192])
+            if cnt.float().mean().item() > wl["k"]:
+                lo = c
+            else:
+                hi = c
+        sae.log_threshold.copy_(z + hi)
+    x_hat = torch.empty(tokens, d, device=dev)
+    counts = torch.empty(tokens, device=dev, dtype=torch.int32)
+    model = sae._model_struct(need_shadows=True)
+    ws = torch.empty(L.workspace_bytes(tokens, d, F, 0), device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step(x):
+        L.call("sae_b200_encode_decode", model, L.ptr(x), L.DTYPE_BF16, tokens, L.ptr(ws),
+               ws.numel(), L.ptr(x_hat), L.ptr(counts), None, stream)
+
+    for i in range(args.warmup):
+        step(pool[i % 2])
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0s = []
+    launches0 = L.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0.record()
+        for i in range(args.steps):
+            L.set_kernel_timer(L.KERNEL_ENCODER_GEMM, ev[i][0], ev[i][1])
+            L.set_kernel_timer(L.KERNEL_DECODE, ev[i][2], ev[i][3])
+            step(pool[i % 2])
+        t1.record()
+        torch.cuda.synchronize()
+    L.set_kernel_timer(L.KERNEL_ENCODER_GEMM)
+    L.set_kernel_timer(L.KERNEL_DECODE)
+    launches = L.launch_count() - launches0
+    l0 = counts.float().mean().item()
+    ms = atlas.max_over_ranks(t0.elapsed_time(t1) / args.steps, device=dev)
+    enc_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    dec_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
+    clock = clocks.summary()
+    # end to end: pinned host batch in, x_hat (fp32) back, every step
+    host = [b.cpu().pin_memory() for b in pool]
+    out_host = torch.empty(tokens, d, dtype=torch.float32).pin_memory()
+    xb = torch.empty_like(pool[0])
+    e2e_steps = max(3, min(args.steps, 10))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        xb.copy_(host[i % 2], non_blocking=True)
+        step(xb)
+        out_host.copy_(x_hat, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = atlas.max_over_ranks(e0.elapsed_time(e1) / e2e_steps, device=dev)
+    if rank == 0:
+        peaks = _peaks()
+        rows = tokens * l0 * d * 2
+        dec_bytes = rows + tokens * d * 4 + tokens * ((F + 31) // 32) * 4 + tokens * l0 * 2
+        dec_gbs = dec_bytes / (dec_ms / 1e3) / 1e9
+        enc_tf = 2.0 * tokens * d * F / (enc_ms / 1e3) / 1e12
+        line = {
+            "metric": "SAE encode+sparse-decode tokens/s at d=2304x65536 L0~80; gather-decode "
+                      "HBM GB/s",
+            "value": world * tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic superposition activations (seeded, on device)",
+            "config": {"workload": wl["description"], "d_in": d, "n_features": F,
+                       "tokens_per_step": tokens, "l0_measured": l0,
+                       "parallelism": f"replicas only: {world} independent GPU(s)",
+                       "l2": "inputs alternate between two 302 MB batches; each step writes the "
+                             "8.6 GB pre-activation tensor"},
+            "roofline": {"bound": "hbm", "kernel": "gathered decode (decode_kernel)",
+                         "achieved": dec_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": dec_gbs / peaks["hbm_gbs"],
+                         "peak_source": f"hbm_gbs ({peaks['src']})", "traffic": None,
+                         "algorithmic_bytes": dec_bytes, "launch_ms": dec_ms,
+                         "bytes_note": "B*L0*d*2 gathered bf16 decoder rows + B*d*4 x_hat + "
+                                       "B*F/8 mask + B*L0*2 pre values"},
+            "kernels": {"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
+                        "decode_ms": dec_ms, "decode_row_gbs": rows / (dec_ms / 1e3) / 1e9},
+            "clocks": clock,
+            "e2e": {"value": world * tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": world * tokens * d * 2,
+                    "d2h_bytes_per_step": world * tokens * d * 4},
+            "gpu_launches": int(launches),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def calibrate(sae, pool, target_l0, n_features_total):
     """Untimed set-up that mirrors the trainer's preflight (2576-2640): b_dec =
     mean activation, then one uniform threshold at the pre-activation quantile
     that gives the target L0 (the metric is quoted at L0 ~ 50)."""
@@ -187,16 +343,27 @@ def calibrate(sae, pool, target_l0):
 
     with torch.no_grad():
         sae.b_dec.copy_(pool[0].float().mean(0))
-        probe = pool[0][:2048]
+        probe = pool[0][:4096]
         with torch.autocast("cuda", dtype=torch.bfloat16):
             pre = sae.encode_pre(probe)
         flat = pre.float().flatten()
-        idx = torch.randint(0, flat.numel(), (4_000_000,), device=flat.device,
+        idx = torch.randint(0, flat.numel(), (8_000_000,), device=flat.device,
                             generator=torch.Generator(device=flat.device).manual_seed(0))
-        q = torch.quantile(flat[idx], 1.0 - target_l0 / sae.n_features).item()
+        q = torch.quantile(flat[idx], 1.0 - target_l0 / n_features_total).item()
         sae.log_threshold.fill_(math.log(max(q, 1e-3)))
         sae.mark_weights_dirty()
     return q
+
+
+def threshold_nudge(sae, l0, target):
+    """The trainer's L0 controller writes log_threshold after every step
+    (compute_threshold_nudge, sae_scheduler.py:876-959, applied at
+    sae_trainer_rolling.py:3334-3338); here a plain proportional version keeps
+    the benchmark at the L0 its metric is quoted for."""
+    import torch
+    nudge = max(-0.05, min(0.05, 0.5 * math.log(max(l0, 1e-3) / target)))
+    with torch.no_grad():
+        sae.log_threshold.add_(nudge)
 
 
 def run_b200(args):
@@ -207,6 +374,8 @@ def run_b200(args):
     from sae_b200 import _lib as L
     from sae_b200 import atlas
 
+    wl = WORKLOADS[args.workload]
+    d, F_total, tokens, k_target = wl["d"], wl["F"], wl["tokens"], wl["k"]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -215,22 +384,34 @@ def run_b200(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev,
                                 timeout=__import__("datetime").timedelta(seconds=300))
-    layer = rank   # atlas layout: one layer's SAE per GPU
-    torch.manual_seed(1000 + layer)
-    pool = [sae_b200.superposition_batch(TOKENS, D_IN, N_FEAT, K_TARGET,
-                                         NORM_MU, NORM_SIGMA,
-                                         seed=17 + 100 * layer + 7 * i, device=dev)
+    sharded = args.workload == "sharded"
+    if sharded:
+        # every rank holds the same batches (replicated input), its slice of the dictionary
+        data_seed = 17
+        F = F_total // world
+        sae = sae_b200.make_shard_sae(d, F_total, rank, world, seed=5, device=dev)
+    else:
+        data_seed = 17 + 100 * rank      # atlas layout: one layer's SAE per GPU
+        F = F_total
+        torch.manual_seed(1000 + rank)
+        sae = sae_b200.make_sae(d, F, seed=rank).to(dev)
+    pool = [sae_b200.superposition_batch(tokens, d, F_total, k_target, wl["norm_mu"],
+                                         wl["norm_sigma"], seed=data_seed + 7 * i, device=dev)
             for i in range(POOL_BATCHES)]
-    sae = sae_b200.make_sae(D_IN, N_FEAT, seed=layer).to(dev)
     sae.ste_bandwidth = 0.2
-    thr = calibrate(sae, pool, K_TARGET)
-    opt = sae_b200.B200Adam(sae_b200.reference_param_groups(sae, LR), lr=LR, betas=(0.9, 0.999),
-                            sae=sae, renorm=True)
-    fs = sae_b200.FusedStep(sae, opt, max_tokens=TOKENS)
+    thr = calibrate(sae, pool, k_target, F_total)
+    opt = sae_b200.B200Adam(sae_b200.reference_param_groups(sae, wl["lr"]), lr=wl["lr"],
+                            betas=(0.9, 0.999), sae=sae, renorm=True)
+    if sharded:
+        fs = sae_b200.ShardedFusedStep(sae, opt, max_tokens=tokens)
+    else:
+        fs = sae_b200.FusedStep(sae, opt, max_tokens=tokens)
 
     def step(i, x):
-        return fs.step(x, lambda_l0=LAMBDA, al_mu=MU, target_l0=K_TARGET,
-                       wenc_dampen=lambda l0: 1.0)
+        out = fs.step(x, lambda_l0=LAMBDA, al_mu=MU, target_l0=k_target,
+                      wenc_dampen=lambda l0: 1.0)
+        threshold_nudge(sae, out["l0"], k_target)
+        return out
 
     def barrier():
         if world > 1:
@@ -270,7 +451,9 @@ def run_b200(args):
                               for i in range(n_ev))
     clock = clocks.summary()
     status = L.device_status()
-    value = world * TOKENS / (ms / 1e3)   # max-over-ranks time, all ranks' tokens
+    job_tokens = tokens if sharded else world * tokens
+    value = job_tokens / (ms / 1e3)   # max-over-ranks time, all ranks' tokens
+    l0_timed = statistics.mean(s["l0"] for s in stats)
 
     # ---------------- end to end from host memory (e2e)
     host = [b.cpu().pin_memory() for b in pool]
@@ -298,59 +481,68 @@ def run_b200(args):
     e1.record()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    e2e_value = world * TOKENS / (e2e_ms / 1e3)
+    e2e_value = job_tokens / (e2e_ms / 1e3)
 
     if rank == 0:
         peaks = _peaks()
-        gemm_flop = 2.0 * TOKENS * D_IN * N_FEAT
+        gemm_flop = 2.0 * tokens * d * F
         enc_tf = gemm_flop / (enc_ms / 1e3) / 1e12
         grad_tf = gemm_flop / (grad_ms / 1e3) / 1e12
+        traffic_scale = (d * F) / (D_IN * N_FEAT) * (tokens / TOKENS)
         dom_ms, dom_tf, dom_name, dom_traffic = (
             (enc_ms, enc_tf, "encoder tile GEMM (tcgen05 cta_group::2) + JumpReLU epilogue",
              TRAFFIC_ENCODER_GEMM) if enc_ms >= grad_ms else
             (grad_ms, grad_tf, "grad_feat tile GEMM (tcgen05 cta_group::2) + STE epilogue",
              TRAFFIC_GRAD_GEMM))
         peak = peaks["bf16_sustained"]
-        last = stats[-1]
-        step_flop = 4.0 * TOKENS * D_IN * N_FEAT
+        step_flop = 4.0 * tokens * d * F_total
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC if not sharded else
+            "wide-SAE fwd+bwd+Adam tokens/s at d=4096x131072 L0~64 (dictionary-sharded)",
+            "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+            "vs_baseline": None if sharded else value / PUBLISHED_TOK_S, "dtype": "bf16",
             "data": "synthetic superposition activations (seeded, on device)",
-            "config": {"workload": WORKLOAD, "model": "JumpReLU SAE d_in=1536 F=49152",
-                       "d_in": D_IN, "n_features": N_FEAT, "tokens_per_step": TOKENS,
-                       "global_batch": TOKENS * world, "seq_len": None,
-                       "parallelism": f"atlas: {world} independent SAE(s), one per GPU",
-                       "l0_target": K_TARGET, "l0_measured": last["l0"],
+            "config": {"workload": wl["description"],
+                       "model": f"JumpReLU SAE d_in={d} F={F_total}",
+                       "d_in": d, "n_features": F_total, "features_per_gpu": F,
+                       "tokens_per_step": tokens, "global_batch": job_tokens, "seq_len": None,
+                       "parallelism": (f"dictionary split over {world} GPU(s), NCCL all-reduce"
+                                       if sharded else
+                                       f"atlas: {world} independent SAE(s), one per GPU"),
+                       "l0_target": k_target, "l0_measured": l0_timed,
                        "threshold_calibrated": thr,
-                       "l2": "inputs rotate over a 4-batch pool (400 MB); every step writes "
-                             "3.2 GB of pre-activations, which flushes the 126 MB L2",
-                       "dense_gemm_flop_per_token": 4 * D_IN * N_FEAT,
+                       "threshold_control": "proportional log-threshold nudge after each step "
+                                            "(the trainer's L0 controller)",
+                       "l2": "inputs rotate over a 4-batch pool; every step writes the "
+                             f"{2 * tokens * F / 1e9:.1f} GB bf16 pre-activation tensor, which "
+                             "flushes the 126 MB L2",
+                       "dense_gemm_flop_per_token": 4 * d * F_total,
                        "weight_grads": "sparse (CSR gather) -- 4*d*F dense FLOP/token"},
             "roofline": {"bound": "tensor", "kernel": dom_name,
                          "achieved": dom_tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": dom_tf / peak,
                          "peak_source": f"bf16_tflops_sustained ({peaks['src']})",
-                         "traffic": dom_traffic,
+                         "traffic": dom_traffic * traffic_scale,
                          "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
-                                         "4096-token launch, x8 for 32768 tokens",
+                                         "4096-token d=1536 F=49152 launch, scaled by tokens "
+                                         "and by d*F",
                          "per_launch_flop": gemm_flop, "launch_ms": dom_ms},
             "kernels": {"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
                         "grad_gemm_ms": grad_ms, "grad_gemm_tflops": grad_tf,
                         "step_dense_tflops": step_flop / (ms / 1e3) / 1e12},
             "clocks": clock,
             "e2e": {"value": e2e_value, "unit": "tokens/s",
-                    "h2d_bytes_per_step": TOKENS * D_IN * 2,
-                    "d2h_bytes_per_step": 2 * 64,
-                    "note": "pinned host batches, H2D on a side stream overlapped with the "
-                            "previous step (as the trainer's double buffer), stats read back "
-                            "every step"},
+                    "h2d_bytes_per_step": world * tokens * d * 2,
+                    "d2h_bytes_per_step": world * 2 * 64,
+                    "note": "whole job: every rank copies its pinned host batch (H2D on a side "
+                            "stream overlapped with the previous step, as the trainer's double "
+                            "buffer) and reads its stats back every step"},
             "gpu_launches": int(launches),
             "device_status": status,
         }
-        if args.cpu_baseline and world == 1:
+        if args.cpu_baseline and world == 1 and not sharded:
             t_mb, t_adam, _ = cpu_reference_step_time(2048)
             cpu_step = (TOKENS // 2048) * t_mb + t_adam
             line["cpu_baseline"] = {
@@ -372,12 +564,18 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["inference"], default="atlas",
+                    help="atlas: the metric's d=1536 F=49152 SAE, one per GPU (default); "
+                         "sharded: one d=4096 F=131072 SAE split over the GPUs; inference: "
+                         "encode + gathered decode at d=2304 F=65536")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "inference":
+        return run_inference(args)
     return run_b200(args)
 
 

@@ -23,8 +23,8 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<int64_t> g_launches{0};
-cudaEvent_t g_timer_start[2] = {nullptr, nullptr};
-cudaEvent_t g_timer_stop[2] = {nullptr, nullptr};
+cudaEvent_t g_timer_start[3] = {nullptr, nullptr, nullptr};
+cudaEvent_t g_timer_stop[3] = {nullptr, nullptr, nullptr};
 
 void timer_begin(int which, cudaStream_t s) {
   if (g_timer_start[which] != nullptr) cudaEventRecord(g_timer_start[which], s);
@@ -387,7 +387,8 @@ int64_t sae_b200_launch_count(void) { return g_launches.load(); }
 int64_t sae_b200_pre_pitch(int64_t n_tokens) { return pre_pitch(n_tokens); }
 
 int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event) {
-  if (kernel != SAE_KERNEL_ENCODER_GEMM && kernel != SAE_KERNEL_GRAD_GEMM)
+  if (kernel != SAE_KERNEL_ENCODER_GEMM && kernel != SAE_KERNEL_GRAD_GEMM &&
+      kernel != SAE_KERNEL_DECODE)
     return fail(SAE_ERR_INVALID_ARGUMENT, "unknown kernel id %d", kernel);
   if ((start_event == nullptr) != (stop_event == nullptr))
     return fail(SAE_ERR_INVALID_ARGUMENT, "set both timer events or neither");
@@ -431,27 +432,52 @@ int sae_b200_workspace_offsets(int64_t n_tokens, int64_t d_in, int64_t n_feature
   return SAE_OK;
 }
 
-int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype,
-                           const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
-                           SaeB200StepStats* stats, float* x_hat_out, uint8_t* fired,
-                           void* stream_) {
+}  // extern "C"
+
+namespace {
+
+struct ForwardCtx {
+  int64_t B, d, F;
+  Layout L;
+  Ws w;
+  int mask_words, n_tiles;
+  float go_scale;
+};
+
+int forward_checks(const SaeB200Model* model, const void* x, int x_dtype,
+                   const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                   const SaeB200StepStats* stats, const float* x_hat_out, ForwardCtx* c,
+                   bool need_stats = true) {
   SAE_TRY(check_model(model, true));
   SAE_TRY(check_cfg(cfg));
   SAE_TRY(check_fused_shape(model));
-  if (x == nullptr || stats == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "x/stats is NULL");
+  if (x == nullptr || (stats == nullptr && need_stats))
+    return fail(SAE_ERR_INVALID_ARGUMENT, "x/stats is NULL");
   if (x_dtype != SAE_DTYPE_F32 && x_dtype != SAE_DTYPE_BF16)
     return fail(SAE_ERR_INVALID_ARGUMENT, "x_dtype must be F32 or BF16");
   if (!aligned16(x) || !aligned16(model->W_dec_bf16) || !aligned16(model->W_enc_bf16) ||
       (x_hat_out && !aligned16(x_hat_out)))
     return fail(SAE_ERR_MISALIGNED, "x, x_hat and bf16 weights must be 16-byte aligned");
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  const int64_t B = cfg->n_tokens, d = model->d_in, F = model->n_features;
-  const Layout L = make_layout(B, d, F, cfg->csr_capacity);
-  SAE_TRY(check_ws(L, workspace, workspace_bytes));
-  const Ws w = carve(workspace, L);
-  const int mask_words = static_cast<int>((F + 31) / 32);
-  const int n_tiles = static_cast<int>((B + TILE_N - 1) / TILE_N);
+  c->B = cfg->n_tokens;
+  c->d = model->d_in;
+  c->F = model->n_features;
+  c->L = make_layout(c->B, c->d, c->F, cfg->csr_capacity);
+  SAE_TRY(check_ws(c->L, workspace, workspace_bytes));
+  c->w = carve(workspace, c->L);
+  c->mask_words = static_cast<int>((c->F + 31) / 32);
+  c->n_tiles = static_cast<int>((c->B + TILE_N - 1) / TILE_N);
+  c->go_scale = static_cast<float>(
+      1.0 / (static_cast<double>(cfg->accum_steps) * static_cast<double>(c->B) *
+             static_cast<double>(c->d)));
+  return SAE_OK;
+}
 
+// theta, xc, encoder GEMM + JumpReLU epilogue, per-feature scans -> CSR offsets.
+int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
+                   const SaeB200StepConfig* cfg, const ForwardCtx& c, SaeB200StepStats* stats,
+                   uint8_t* fired, cudaStream_t stream) {
+  const int64_t B = c.B, d = c.d, F = c.F;
+  const Ws& w = c.w;
   // 1. theta, xc
   {
     const int g = grid_for(std::max<int64_t>(F, B * d / 8), 256);
@@ -475,7 +501,7 @@ int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype
     e.tile_cnt = w.tile_cnt;
     e.n_tokens = static_cast<int>(B);
     e.n_features = static_cast<int>(F);
-    e.mask_words = mask_words;
+    e.mask_words = c.mask_words;
     e.ldp = static_cast<int>(pre_pitch(B));
     SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), w.xc, F, B, d, e,
                              tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_ENCODER_GEMM,
@@ -483,46 +509,173 @@ int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype
   }
   // 3. per-feature scans -> CSR offsets
   scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(w.tile_cnt, w.col_tot, fired,
-                                                            2 * n_tiles, static_cast<int>(F));
+                                                            2 * c.n_tiles, static_cast<int>(F));
   SAE_TRY(check_launch("scan_columns_kernel"));
   scan_offsets_kernel<<<1, 1024, 0, stream>>>(w.col_tot, w.col_offs, static_cast<int>(F),
                                               cfg->csr_capacity, stats, w.counters);
-  SAE_TRY(check_launch("scan_offsets_kernel"));
-  // 4. gathered decode + residual
-  {
-    const double scale = 1.0 / (static_cast<double>(cfg->accum_steps) * static_cast<double>(B) *
-                                static_cast<double>(d));
-    const int V = vec_threads(d);
-    const int G = std::min(4, std::max(1, 512 / V));   // row groups per token
-    const size_t dyn = static_cast<size_t>(G - 1) * V * 2 * sizeof(float4);
+  return check_launch("scan_offsets_kernel");
+}
+
+// Gathered decode; partial != NULL writes the shard's decoder sums and counts
+// instead of the residual (dictionary-sharded step).
+int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const ForwardCtx& c,
+                   float* x_hat_out, float* partial, cudaStream_t stream) {
+  const int64_t B = c.B, d = c.d, F = c.F;
+  const Ws& w = c.w;
+  const int V = vec_threads(d);
+  const int G = std::min(4, std::max(1, 512 / V));   // row groups per token
+  const size_t dyn = static_cast<size_t>(G - 1) * V * 2 * sizeof(float4);
 #define SAE_DECODE(XT, GG)                                                                   \
   decode_kernel<XT, GG><<<DECODE_GRID, V * GG, dyn, stream>>>(                              \
       w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,             \
-      static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), mask_words,   \
-      static_cast<int>(pre_pitch(B)), static_cast<float>(scale), w.go, x_hat_out,           \
-      w.tok_sqerr, w.tok_cnt, w.gosum_part)
-    if (x_dtype == SAE_DTYPE_BF16) {
-      if (G >= 4) SAE_DECODE(bf16, 4);
-      else if (G == 2 || G == 3) SAE_DECODE(bf16, 2);
-      else SAE_DECODE(bf16, 1);
-    } else {
-      if (G >= 4) SAE_DECODE(float, 4);
-      else if (G == 2 || G == 3) SAE_DECODE(float, 2);
-      else SAE_DECODE(float, 1);
-    }
-#undef SAE_DECODE
-    SAE_TRY(check_launch("decode_kernel"));
+      static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), c.mask_words, \
+      static_cast<int>(pre_pitch(B)), c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt,  \
+      w.gosum_part, partial)
+  timer_begin(SAE_KERNEL_DECODE, stream);
+  if (x_dtype == SAE_DTYPE_BF16) {
+    if (G >= 4) SAE_DECODE(bf16, 4);
+    else if (G == 2 || G == 3) SAE_DECODE(bf16, 2);
+    else SAE_DECODE(bf16, 1);
+  } else {
+    if (G >= 4) SAE_DECODE(float, 4);
+    else if (G == 2 || G == 3) SAE_DECODE(float, 2);
+    else SAE_DECODE(float, 1);
   }
-  // 5. loss terms
-  forward_stats_kernel<<<1, 1024, 0, stream>>>(w.tok_sqerr, w.tok_cnt, B, static_cast<int>(d),
-                                               cfg->lambda_l0, cfg->al_mu, cfg->target_l0,
-                                               cfg->accum_steps, stats);
+#undef SAE_DECODE
+  const int rc = check_launch("decode_kernel");
+  timer_end(SAE_KERNEL_DECODE, stream);
+  return rc;
+}
+
+int forward_stats(const SaeB200StepConfig* cfg, const ForwardCtx& c, SaeB200StepStats* stats,
+                  cudaStream_t stream) {
+  forward_stats_kernel<<<1, 1024, 0, stream>>>(c.w.tok_sqerr, c.w.tok_cnt, c.B,
+                                               static_cast<int>(c.d), cfg->lambda_l0, cfg->al_mu,
+                                               cfg->target_l0, cfg->accum_steps, stats);
   return check_launch("forward_stats_kernel");
 }
 
+}  // namespace
+
+extern "C" {
+
+int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                           const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                           SaeB200StepStats* stats, float* x_hat_out, uint8_t* fired,
+                           void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ForwardCtx c;
+  SAE_TRY(forward_checks(model, x, x_dtype, cfg, workspace, workspace_bytes, stats, x_hat_out,
+                         &c));
+  SAE_TRY(forward_encode(model, x, x_dtype, cfg, c, stats, fired, stream));
+  SAE_TRY(forward_decode(model, x, x_dtype, c, x_hat_out, nullptr, stream));
+  return forward_stats(cfg, c, stats, stream);
+}
+
+int sae_b200_encode_decode(const SaeB200Model* model, const void* x, int x_dtype,
+                           int64_t n_tokens, void* workspace, size_t workspace_bytes,
+                           float* x_hat_out, int32_t* active_counts_out, uint8_t* fired,
+                           void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (x_hat_out == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "x_hat_out is NULL");
+  SaeB200StepConfig cfg{};
+  cfg.n_tokens = n_tokens;
+  cfg.csr_capacity = 0;
+  cfg.ste_bandwidth = 1.f;
+  cfg.accum_steps = 1;
+  ForwardCtx c;
+  SAE_TRY(forward_checks(model, x, x_dtype, &cfg, workspace, workspace_bytes, nullptr, x_hat_out,
+                         &c, /*need_stats=*/false));
+  // theta, xc, encoder GEMM + gate epilogue (pre, mask rows, per-tile counts)
+  const int64_t B = c.B, d = c.d, F = c.F;
+  const Ws& w = c.w;
+  {
+    const int g = grid_for(std::max<int64_t>(F, B * d / 8), 256);
+    if (x_dtype == SAE_DTYPE_BF16)
+      prep_kernel<bf16><<<g, 256, 0, stream>>>(static_cast<const bf16*>(x), model->b_dec,
+                                               model->log_threshold, w.theta, w.xc, B,
+                                               static_cast<int>(d), static_cast<int>(F));
+    else
+      prep_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(x), model->b_dec,
+                                                model->log_threshold, w.theta, w.xc, B,
+                                                static_cast<int>(d), static_cast<int>(F));
+    SAE_TRY(check_launch("prep_kernel"));
+    EncodeEpi e{};
+    e.theta = w.theta;
+    e.b_enc = model->b_enc;
+    e.pre = w.pre;
+    e.mask = w.mask;
+    e.tile_cnt = w.tile_cnt;
+    e.n_tokens = static_cast<int>(B);
+    e.n_features = static_cast<int>(F);
+    e.mask_words = c.mask_words;
+    e.ldp = static_cast<int>(pre_pitch(B));
+    SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), w.xc, F, B, d, e,
+                             tc_eligible(d, F, 0), stream, SAE_KERNEL_ENCODER_GEMM, w.pre));
+  }
+  if (fired != nullptr) {
+    scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(w.tile_cnt, w.col_tot, fired,
+                                                              2 * c.n_tiles, static_cast<int>(F));
+    SAE_TRY(check_launch("scan_columns_kernel"));
+  }
+  SAE_TRY(forward_decode(model, nullptr, x_dtype, c, x_hat_out, nullptr, stream));
+  if (active_counts_out != nullptr) {
+    const cudaError_t e = cudaMemcpyAsync(active_counts_out, w.tok_cnt, B * sizeof(int32_t),
+                                          cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return fail(SAE_ERR_CUDA, "counts copy: %s", cudaGetErrorString(e));
+  }
+  return SAE_OK;
+}
+
+int64_t sae_b200_shard_exchange_floats(int64_t n_tokens, int64_t d_in) {
+  if (n_tokens <= 0 || d_in <= 0) return 0;
+  return n_tokens * d_in + n_tokens;
+}
+
+int sae_b200_shard_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                           const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                           SaeB200StepStats* stats, uint8_t* fired, float* exchange,
+                           void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ForwardCtx c;
+  SAE_TRY(forward_checks(model, x, x_dtype, cfg, workspace, workspace_bytes, stats, nullptr, &c));
+  if (exchange == nullptr || !aligned16(exchange))
+    return fail(SAE_ERR_MISALIGNED, "exchange must be a 16-byte aligned device buffer");
+  SAE_TRY(forward_encode(model, x, x_dtype, cfg, c, stats, fired, stream));
+  return forward_decode(model, x, x_dtype, c, nullptr, exchange, stream);
+}
+
+int sae_b200_shard_finish_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                                  const SaeB200StepConfig* cfg, void* workspace,
+                                  size_t workspace_bytes, SaeB200StepStats* stats,
+                                  const float* exchange, float* x_hat_out, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ForwardCtx c;
+  SAE_TRY(forward_checks(model, x, x_dtype, cfg, workspace, workspace_bytes, stats, x_hat_out,
+                         &c));
+  if (exchange == nullptr || !aligned16(exchange))
+    return fail(SAE_ERR_MISALIGNED, "exchange must be a 16-byte aligned device buffer");
+  const int V = vec_threads(c.d);
+  const Ws& w = c.w;
+  if (x_dtype == SAE_DTYPE_BF16)
+    residual_kernel<bf16><<<DECODE_GRID, V, 0, stream>>>(
+        exchange, model->b_dec, static_cast<const bf16*>(x), c.B, static_cast<int>(c.d),
+        c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt, w.gosum_part);
+  else
+    residual_kernel<float><<<DECODE_GRID, V, 0, stream>>>(
+        exchange, model->b_dec, static_cast<const float*>(x), c.B, static_cast<int>(c.d),
+        c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt, w.gosum_part);
+  SAE_TRY(check_launch("residual_kernel"));
+  return forward_stats(cfg, c, stats, stream);
+}
+
+// bdec_owner = 0 (dictionary shards other than the first): the b_dec gradient
+// gets only this shard's encoder term, overwriting; the shards' values are then
+// summed across GPUs, with the go sum and the accumulated value counted once.
 static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
                            const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
-                           SaeB200StepStats* stats, bf16* dense_scratch, cudaStream_t stream) {
+                           SaeB200StepStats* stats, bf16* dense_scratch, cudaStream_t stream,
+                           int bdec_owner = 1) {
   SAE_TRY(check_model(model, true));
   SAE_TRY(check_cfg(cfg));
   SAE_TRY(check_fused_shape(model));
@@ -572,7 +725,8 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
                                                   w.gemv_part);
   SAE_TRY(check_launch("bdec_gemv_kernel"));
   bdec_grad_kernel<<<static_cast<unsigned>((d + 31) / 32), 1024, 0, stream>>>(
-      w.gosum_part, DECODE_GRID, w.gemv_part, GEMV_GRID, static_cast<int>(d), acc, grads->b_dec);
+      w.gosum_part, bdec_owner ? DECODE_GRID : 0, w.gemv_part, GEMV_GRID, static_cast<int>(d),
+      bdec_owner ? acc : 0, grads->b_dec);
   SAE_TRY(check_launch("bdec_grad_kernel"));
   // 4. weight gradients
   if (dense_scratch == nullptr) {
@@ -630,6 +784,18 @@ int sae_b200_train_backward_dense(const SaeB200Model* model, const SaeB200Grads*
                          static_cast<bf16*>(dense_scratch), static_cast<cudaStream_t>(stream));
 }
 
+int sae_b200_shard_backward(const SaeB200Model* model, const SaeB200Grads* grads,
+                            const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                            SaeB200StepStats* stats, int shard_rank, void* dense_scratch,
+                            void* stream) {
+  if (shard_rank < 0) return fail(SAE_ERR_INVALID_ARGUMENT, "shard_rank must be >= 0");
+  if (dense_scratch != nullptr && !aligned16(dense_scratch))
+    return fail(SAE_ERR_MISALIGNED, "dense_scratch must be 16-byte aligned");
+  return backward_common(model, grads, cfg, workspace, workspace_bytes, stats,
+                         static_cast<bf16*>(dense_scratch), static_cast<cudaStream_t>(stream),
+                         shard_rank == 0 ? 1 : 0);
+}
+
 int sae_b200_grad_norm(const SaeB200Model* model, const SaeB200Grads* grads, float max_norm,
                        void* workspace, size_t workspace_bytes, SaeB200StepStats* stats,
                        void* stream_) {
@@ -658,6 +824,41 @@ int sae_b200_grad_norm(const SaeB200Model* model, const SaeB200Grads* grads, flo
   grad_sumsq_kernel<<<NORM_GRID, 512, 0, stream>>>(gl, part);
   SAE_TRY(check_launch("grad_sumsq_kernel"));
   grad_norm_final_kernel<<<1, 1024, 0, stream>>>(part, NORM_GRID, max_norm, stats);
+  return check_launch("grad_norm_final_kernel");
+}
+
+int sae_b200_grad_sumsq(const SaeB200Model* model, const SaeB200Grads* grads, void* workspace,
+                        size_t workspace_bytes, float* sumsq_out, void* stream_) {
+  SAE_TRY(check_model(model, false));
+  if (grads == nullptr || sumsq_out == nullptr)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (workspace == nullptr || workspace_bytes < NORM_GRID * sizeof(float))
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "grad_sumsq needs %zu workspace bytes",
+                NORM_GRID * sizeof(float));
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int64_t d = model->d_in, F = model->n_features;
+  GradList gl;
+  const float* ps[5] = {grads->W_enc, grads->b_enc, grads->W_dec_fm, grads->b_dec,
+                        grads->log_threshold};
+  const int64_t ns[5] = {F * d, F, F * d, d, F};
+  for (int k = 0; k < 5; ++k) {
+    gl.p[k] = ps[k];
+    gl.n[k] = ns[k];
+    if (ps[k] != nullptr && !aligned16(ps[k]))
+      return fail(SAE_ERR_MISALIGNED, "gradient %d must be 16-byte aligned", k);
+  }
+  float* part = static_cast<float*>(workspace);
+  grad_sumsq_kernel<<<NORM_GRID, 512, 0, stream>>>(gl, part);
+  SAE_TRY(check_launch("grad_sumsq_kernel"));
+  sum_parts_kernel<<<1, 1024, 0, stream>>>(part, NORM_GRID, sumsq_out);
+  return check_launch("sum_parts_kernel");
+}
+
+int sae_b200_clip_from_sumsq(const float* sumsq, float max_norm, SaeB200StepStats* stats,
+                             void* stream_) {
+  if (sumsq == nullptr || stats == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "NULL argument");
+  grad_norm_final_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream_)>>>(sumsq, 1, max_norm,
+                                                                           stats);
   return check_launch("grad_norm_final_kernel");
 }
 

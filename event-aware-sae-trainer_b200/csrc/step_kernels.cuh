@@ -430,6 +430,49 @@ __global__ void __launch_bounds__(1024)
 // reference's bf16 GEMM output plus the fp32 bias, 924), r = x - x_hat,
 // squared error per token, and the loss gradient go = -(scale * 2r) stored as
 // bf16 (what the decoder GEMMs see).
+//
+// Residual of 8 columns of one token given the fp32 decoder sum acc:
+// x_hat = bf16(acc) + b_dec, r = x - x_hat, go = -(scale * 2r) (bf16), and the
+// running per-column go sums. Returns the 8 columns' squared error.
+template <typename XT>
+__device__ __forceinline__ float residual8(const float (&acc)[8], const XT* __restrict__ x,
+                                           const float* __restrict__ b_dec, size_t base, int c0,
+                                           float go_scale, bf16* __restrict__ go,
+                                           float* __restrict__ x_hat, float (&gsum)[8]) {
+  float xv[8];
+  if constexpr (sizeof(XT) == 2) {
+    unpack8(*reinterpret_cast<const uint4*>(x + base), xv);
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(x + base);
+    const float4 c = *reinterpret_cast<const float4*>(x + base + 4);
+    xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+    xv[4] = c.x; xv[5] = c.y; xv[6] = c.z; xv[7] = c.w;
+  }
+  float gv[8], xh[8];
+  float sq = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    xh[j] = __fadd_rn(bf16_round(acc[j]), b_dec[c0 + j]);
+    const float r = __fsub_rn(xv[j], xh[j]);
+    sq = fmaf(r, r, sq);
+    gv[j] = -__fmul_rn(go_scale, __fadd_rn(r, r));
+    gsum[j] += gv[j];
+  }
+  *reinterpret_cast<uint4*>(go + base) = pack8(gv);
+  if (x_hat != nullptr) {
+    *reinterpret_cast<float4*>(x_hat + base) = make_float4(xh[0], xh[1], xh[2], xh[3]);
+    *reinterpret_cast<float4*>(x_hat + base + 4) = make_float4(xh[4], xh[5], xh[6], xh[7]);
+  }
+  return sq;
+}
+
+// x == NULL (inference): the block writes x_hat (fp32, required) and the
+// token's active count only.
+// partial != NULL (dictionary-sharded step): instead of the residual, the
+// block writes the token's fp32 decoder sum over this shard's features to
+// partial[b * d + c] and its active count to partial[n_tokens * d + b] (as a
+// float); the shards' partials are summed across GPUs and residual_kernel
+// finishes the forward.
 template <typename XT, int G>
 __global__ void __launch_bounds__(1024)
     decode_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
@@ -437,7 +480,8 @@ __global__ void __launch_bounds__(1024)
                   const XT* __restrict__ x, int64_t n_tokens, int d, int n_features,
                   int mask_words, int ldp, float go_scale, bf16* __restrict__ go,
                   float* __restrict__ x_hat, float* __restrict__ tok_sqerr,
-                  int* __restrict__ tok_cnt, float* __restrict__ gosum_part) {
+                  int* __restrict__ tok_cnt, float* __restrict__ gosum_part,
+                  float* __restrict__ partial) {
   __shared__ int s_f[DECODE_LIST_CAP];
   __shared__ float s_v[DECODE_LIST_CAP];
   __shared__ int s_itmp[33];
@@ -532,40 +576,76 @@ __global__ void __launch_bounds__(1024)
       }
     }
 
-    float sq = 0.f;
-    if (g == 0 && has) {
-      float xv[8];
-      const size_t base = static_cast<size_t>(b) * d + col * 8;
-      if constexpr (sizeof(XT) == 2) {
-        unpack8(*reinterpret_cast<const uint4*>(x + base), xv);
-      } else {
-        const float4 a = *reinterpret_cast<const float4*>(x + base);
-        const float4 c = *reinterpret_cast<const float4*>(x + base + 4);
-        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
-        xv[4] = c.x; xv[5] = c.y; xv[6] = c.z; xv[7] = c.w;
+    const size_t base = static_cast<size_t>(b) * d + col * 8;
+    if (partial != nullptr) {   // uniform across the block
+      if (g == 0 && has) {
+        *reinterpret_cast<float4*>(partial + base) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(partial + base + 4) =
+            make_float4(acc[4], acc[5], acc[6], acc[7]);
       }
-      float gv[8], xh[8];
+      if (tid == 0) partial[n_tokens * d + b] = static_cast<float>(total);
+      continue;
+    }
+    if (x == nullptr) {         // inference: x_hat only (uniform across the block)
+      if (g == 0 && has) {
+        float xh[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        xh[j] = __fadd_rn(bf16_round(acc[j]), b_dec[col * 8 + j]);
-        const float r = __fsub_rn(xv[j], xh[j]);
-        sq = fmaf(r, r, sq);
-        gv[j] = -__fmul_rn(go_scale, __fadd_rn(r, r));
-        gsum[j] += gv[j];
-      }
-      *reinterpret_cast<uint4*>(go + base) = pack8(gv);
-      if (x_hat != nullptr) {
+        for (int j = 0; j < 8; ++j) xh[j] = __fadd_rn(bf16_round(acc[j]), b_dec[col * 8 + j]);
         *reinterpret_cast<float4*>(x_hat + base) = make_float4(xh[0], xh[1], xh[2], xh[3]);
         *reinterpret_cast<float4*>(x_hat + base + 4) = make_float4(xh[4], xh[5], xh[6], xh[7]);
       }
+      if (tid == 0) tok_cnt[b] = total;
+      continue;
     }
+    float sq = 0.f;
+    if (g == 0 && has) sq = residual8(acc, x, b_dec, base, col * 8, go_scale, go, x_hat, gsum);
     const float tot_sq = block_sum(sq, s_ftmp);
     if (tid == 0) {
       tok_sqerr[b] = tot_sq;
       tok_cnt[b] = total;
     }
   }
-  if (g == 0 && has) {
+  if (partial == nullptr && x != nullptr && g == 0 && has) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      gosum_part[static_cast<size_t>(blockIdx.x) * d + col * 8 + j] = gsum[j];
+  }
+}
+
+// Second half of the dictionary-sharded forward: xsum holds the decoder sums
+// and active counts of decode_kernel's partial mode, already summed over all
+// shards ([n_tokens * d] floats, then [n_tokens] counts). Same residual, loss
+// and go as decode_kernel, one block of d / 8 threads per token (grid-stride,
+// launched with DECODE_GRID blocks so that gosum_part has the same rows).
+template <typename XT>
+__global__ void __launch_bounds__(1024)
+    residual_kernel(const float* __restrict__ xsum, const float* __restrict__ b_dec,
+                    const XT* __restrict__ x, int64_t n_tokens, int d, float go_scale,
+                    bf16* __restrict__ go, float* __restrict__ x_hat,
+                    float* __restrict__ tok_sqerr, int* __restrict__ tok_cnt,
+                    float* __restrict__ gosum_part) {
+  __shared__ float s_ftmp[33];
+  const int col = threadIdx.x;
+  const bool has = col < d / 8;
+  float gsum[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) gsum[j] = 0.f;
+  for (int64_t b = blockIdx.x; b < n_tokens; b += gridDim.x) {
+    float sq = 0.f;
+    if (has) {
+      const size_t base = static_cast<size_t>(b) * d + col * 8;
+      const float4 a = *reinterpret_cast<const float4*>(xsum + base);
+      const float4 c = *reinterpret_cast<const float4*>(xsum + base + 4);
+      const float acc[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+      sq = residual8(acc, x, b_dec, base, col * 8, go_scale, go, x_hat, gsum);
+    }
+    const float tot_sq = block_sum(sq, s_ftmp);
+    if (threadIdx.x == 0) {
+      tok_sqerr[b] = tot_sq;
+      tok_cnt[b] = static_cast<int>(xsum[n_tokens * d + b]);
+    }
+  }
+  if (has) {
 #pragma unroll
     for (int j = 0; j < 8; ++j)
       gosum_part[static_cast<size_t>(blockIdx.x) * d + col * 8 + j] = gsum[j];
@@ -853,6 +933,17 @@ __global__ void grad_norm_final_kernel(const float* __restrict__ part, int n_par
     stats->grad_norm = norm;
     stats->clip_coef = fminf(coef, 1.0f);
   }
+}
+
+// out[0] = sum of the n_part per-block sums of squares (fixed order); the
+// dictionary-sharded step adds this partial over the shards before the norm.
+__global__ void sum_parts_kernel(const float* __restrict__ part, int n_part,
+                                 float* __restrict__ out) {
+  __shared__ float s_tmp[33];
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < n_part; i += blockDim.x) acc += part[i];
+  const float s = block_sum(acc, s_tmp);
+  if (threadIdx.x == 0) out[0] = s;
 }
 
 // -------------------------------------------------------------------- Adam

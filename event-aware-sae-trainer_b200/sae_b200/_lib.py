@@ -132,6 +132,22 @@ _SIGNATURES = {
     "sae_b200_train_backward_dense": (
         [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
          c_void_p, c_void_p], c_int),
+    "sae_b200_encode_decode": (
+        [POINTER(Model), c_void_p, c_int, c_int64, c_void_p, c_size_t, c_void_p, c_void_p,
+         c_void_p, c_void_p], c_int),
+    "sae_b200_shard_exchange_floats": ([c_int64, c_int64], c_int64),
+    "sae_b200_shard_forward": (
+        [POINTER(Model), c_void_p, c_int, POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
+         c_void_p, c_void_p, c_void_p], c_int),
+    "sae_b200_shard_finish_forward": (
+        [POINTER(Model), c_void_p, c_int, POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
+         c_void_p, c_void_p, c_void_p], c_int),
+    "sae_b200_shard_backward": (
+        [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_void_p, c_int,
+         c_void_p, c_void_p], c_int),
+    "sae_b200_grad_sumsq": (
+        [POINTER(Model), POINTER(Grads), c_void_p, c_size_t, c_void_p, c_void_p], c_int),
+    "sae_b200_clip_from_sumsq": ([c_void_p, c_float, c_void_p, c_void_p], c_int),
     "sae_b200_grad_norm": (
         [POINTER(Model), POINTER(Grads), c_float, c_void_p, c_size_t, c_void_p, c_void_p], c_int),
     "sae_b200_adam_step": (
@@ -192,6 +208,7 @@ def call(name: str, *args) -> None:
 
 KERNEL_ENCODER_GEMM = 0
 KERNEL_GRAD_GEMM = 1
+KERNEL_DECODE = 2
 
 
 def pre_pitch(n_tokens: int) -> int:

@@ -249,26 +249,33 @@ class _Decode(torch.autograd.Function):
 class B200JumpReLUSAE(nn.Module):
     """JumpReLU SAE on B200; see the module docstring for the contract."""
 
-    def __init__(self, d_in: int, n_features: int):
+    def __init__(self, d_in: int, n_features: int, *, _tensors=None):
         super().__init__()
         self.d_in = int(d_in)
         self.n_features = int(n_features)
-        # Same RNG draws as the reference constructor (772-800): two nn.Linear
-        # initialisations, then orthogonal_ on the [d, F] decoder, unit
-        # columns, W_enc = W_dec^T, b_enc = 0.
-        enc = nn.Linear(d_in, n_features, bias=True)
-        dec = nn.Linear(n_features, d_in, bias=False)
-        with torch.no_grad():
-            nn.init.orthogonal_(dec.weight)
-            norms = dec.weight.norm(dim=0, keepdim=True).clamp(min=1e-8)
-            dec.weight.div_(norms)
-            enc.weight.copy_(dec.weight.t())
-            enc.bias.zero_()
-        dec_fm = dec.weight.detach().t().contiguous()          # [F, d] feature-major
-        self.W_enc = _Linear(enc.weight.detach().clone(), enc.bias.detach().clone())
+        if _tensors is None:
+            # Same RNG draws as the reference constructor (772-800): two nn.Linear
+            # initialisations, then orthogonal_ on the [d, F] decoder, unit
+            # columns, W_enc = W_dec^T, b_enc = 0.
+            enc = nn.Linear(d_in, n_features, bias=True)
+            dec = nn.Linear(n_features, d_in, bias=False)
+            with torch.no_grad():
+                nn.init.orthogonal_(dec.weight)
+                norms = dec.weight.norm(dim=0, keepdim=True).clamp(min=1e-8)
+                dec.weight.div_(norms)
+                enc.weight.copy_(dec.weight.t())
+                enc.bias.zero_()
+            w_enc = enc.weight.detach().clone()
+            b_enc = enc.bias.detach().clone()
+            dec_fm = dec.weight.detach().t().contiguous()      # [F, d] feature-major
+            b_dec = torch.zeros(d_in)
+            log_thr = torch.full((n_features,), math.log(INIT_THRESHOLD))
+        else:
+            w_enc, b_enc, dec_fm, b_dec, log_thr = _tensors
+        self.W_enc = _Linear(w_enc, b_enc)
         self.W_dec = _Linear(dec_fm.t(), None)                 # [d, F] view
-        self.b_dec = nn.Parameter(torch.zeros(d_in))
-        self.log_threshold = nn.Parameter(torch.full((n_features,), math.log(INIT_THRESHOLD)))
+        self.b_dec = nn.Parameter(b_dec)
+        self.log_threshold = nn.Parameter(log_thr)
         self.ste_bandwidth = STE_BANDWIDTH
         self._sparse_decode_calls = 0
         self._sparse_decode_fallbacks = 0
@@ -405,6 +412,31 @@ class B200JumpReLUSAE(nn.Module):
         x_hat = self.decode(acts)
         return x_hat, acts
 
+    @torch.no_grad()
+    def reconstruct(self, x: torch.Tensor, fired: Optional[torch.Tensor] = None):
+        """Inference without the dense [B, F] activations: one library call runs
+        the encoder GEMM with the JumpReLU gate and the gathered decode
+        (bf16 operands and pre-activations, fp32 accumulation -- the autocast
+        forward). Returns (x_hat fp32 [B, d], per-token L0 int32 [B]);
+        ``fired`` (uint8 [F]) is OR-accumulated when given."""
+        _require_cuda(x)
+        if x.dim() != 2 or x.shape[1] != self.d_in:
+            raise ValueError(f"x must be [tokens, {self.d_in}]")
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            x = x.float()
+        x = x.contiguous()
+        B = x.shape[0]
+        model = self._model_struct(need_shadows=True)
+        need = L.workspace_bytes(B, self.d_in, self.n_features, 0)
+        ws = getattr(self, "_infer_ws", None)
+        if ws is None or ws.numel() < need or ws.device != x.device:
+            ws = self._infer_ws = torch.empty(need, device=x.device, dtype=torch.uint8)
+        x_hat = torch.empty(B, self.d_in, device=x.device, dtype=torch.float32)
+        counts = torch.empty(B, device=x.device, dtype=torch.int32)
+        L.call("sae_b200_encode_decode", model, L.ptr(x), _dt_code(x), B, L.ptr(ws), ws.numel(),
+               L.ptr(x_hat), L.ptr(counts), L.ptr(fired), _stream())
+        return x_hat, counts
+
 
 class _PlainLinear(torch.autograd.Function):
     """y = x W^T + b with gradients for x as well (the reference's fallback when
@@ -432,6 +464,20 @@ class _PlainLinear(torch.autograd.Function):
         gemm(F, d, B, g, 1, F, x2, 1, d, gw, d, 1)
         gb = column_sum(g, torch.empty(F, device=g.device, dtype=torch.float32))
         return gx, gw, gb
+
+
+def sae_from_tensors(W_enc: torch.Tensor, b_enc: torch.Tensor, W_dec_fm: torch.Tensor,
+                     b_dec: torch.Tensor, log_threshold: torch.Tensor) -> B200JumpReLUSAE:
+    """A module over existing float32 tensors (no initialisation, no RNG use):
+    W_enc [F, d], b_enc [F], the feature-major decoder W_dec_fm [F, d] (row f
+    is decoder column f), b_dec [d], log_threshold [F]."""
+    F, d = W_enc.shape
+    if W_dec_fm.shape != (F, d) or b_enc.shape != (F,) or b_dec.shape != (d,) \
+            or log_threshold.shape != (F,):
+        raise ValueError("inconsistent SAE tensor shapes")
+    ts = tuple(t.detach().float().contiguous().clone()
+               for t in (W_enc, b_enc, W_dec_fm, b_dec, log_threshold))
+    return B200JumpReLUSAE(d, F, _tensors=ts)
 
 
 def make_sae(d_in: int, n_features: int, seed: int = 0) -> B200JumpReLUSAE:

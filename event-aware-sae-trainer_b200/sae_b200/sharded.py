@@ -1,0 +1,162 @@
+"""One wide JumpReLU SAE with its dictionary split over the GPUs of a node.
+
+The reference trains a dictionary on one device (``train_sae_on_activations``,
+sae_trainer_rolling.py:2382-3672). For dictionaries too large or too slow for
+one GPU, rank r of N holds features [r F/N, (r+1) F/N): those rows of W_enc and
+b_enc, those columns of W_dec (rows of the feature-major storage), those
+entries of log_threshold, with their gradients and Adam state. The input batch
+and b_dec are replicated. Every per-feature computation is then local and the
+step needs exactly three sums over the ranks, all on the caller's stream
+through ``torch.distributed`` (NCCL over NVLink on a B200 node):
+
+1. forward: the shards' fp32 decoder outputs and per-token active counts,
+   one buffer of ``n_tokens * (d + 1)`` floats (the partial x_hat and the L0
+   counts); after it every rank forms the same residual, loss and go;
+2. backward: the b_dec gradient, whose encoder term -(Σ_b dpre) W_enc (601)
+   is a sum over features; rank 0 adds the go sum and the accumulated value;
+3. the global gradient-norm sum of squares of ``clip_grad_norm_`` (3049),
+   with the replicated b_dec gradient counted once.
+
+Adam, both renormalisations (each W_dec column / W_enc row lives on one rank)
+and the fired-feature mask are local; b_dec's Adam update sees identical
+gradients and state on every rank and so stays replicated.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from .sae import INIT_THRESHOLD, B200JumpReLUSAE, _stream, sae_from_tensors
+from .step import B200Adam, FusedStep
+
+
+def shard_range(n_features: int, rank: int, world: int) -> slice:
+    """Features held by ``rank``: an even, contiguous split of the dictionary."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("need 0 <= rank < world")
+    if n_features % world:
+        raise ValueError(f"n_features={n_features} does not split evenly over {world} ranks")
+    per = n_features // world
+    return slice(rank * per, (rank + 1) * per)
+
+
+@torch.no_grad()
+def shard_sae(full: B200JumpReLUSAE, rank: int, world: int,
+              device: Optional[torch.device] = None) -> B200JumpReLUSAE:
+    """Rank ``rank``'s slice of a whole SAE (same values, b_dec replicated)."""
+    s = shard_range(full.n_features, rank, world)
+    fm = full._dec_fm()
+    out = sae_from_tensors(full.W_enc.weight[s], full.W_enc.bias[s], fm[s], full.b_dec,
+                           full.log_threshold[s])
+    out.ste_bandwidth = full.ste_bandwidth
+    return out.to(device) if device is not None else out
+
+
+@torch.no_grad()
+def make_shard_sae(d_in: int, n_features: int, rank: int, world: int, seed: int = 0, *,
+                   device="cuda") -> B200JumpReLUSAE:
+    """A shard initialised on the device without building the whole dictionary:
+    unit-norm Gaussian decoder columns (the reference's orthogonal init is
+    impossible once F > d anyway; its columns are unit-norm), W_enc = W_dec^T,
+    b_enc = 0, threshold 0.1 -- the reference's init values apart from the
+    orthogonalisation. Feature f's column depends only on (seed, f's shard)."""
+    s = shard_range(n_features, rank, world)
+    per = s.stop - s.start
+    dev = torch.device(device)
+    g = torch.Generator(device=dev).manual_seed(int(seed) * 1_000_003 + rank)
+    fm = torch.randn(per, d_in, generator=g, device=dev)
+    fm /= fm.norm(dim=1, keepdim=True).clamp(min=1e-8)
+    return sae_from_tensors(fm, torch.zeros(per, device=dev), fm, torch.zeros(d_in, device=dev),
+                            torch.full((per,), math.log(INIT_THRESHOLD), device=dev))
+
+
+class ShardedFusedStep(FusedStep):
+    """FusedStep over one dictionary shard, with the three cross-rank sums.
+
+    ``group`` is the process group of the ranks sharing the dictionary
+    (default: the whole world). With one rank (or no process group) the
+    sequence reduces to the unsharded step. ``allreduce`` (with ``rank`` and
+    ``world``) replaces the torch.distributed sum by the caller's own in-place
+    sum over the ranks, called with each of the three buffers in order.
+    ``step()``, ``microbatch()``, ``grad_norm()`` and the returned statistics
+    have FusedStep's meaning; ``nnz`` and ``csr_overflow`` are this shard's."""
+
+    def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int, *,
+                 group=None, csr_capacity: Optional[int] = None, force_simt: bool = False,
+                 allreduce: Optional[Callable[[torch.Tensor], None]] = None,
+                 rank: Optional[int] = None, world: Optional[int] = None):
+        super().__init__(sae, optimizer, max_tokens, csr_capacity=csr_capacity,
+                         force_simt=force_simt)
+        self.group = group
+        if allreduce is not None:
+            if rank is None or world is None or not 0 <= rank < world:
+                raise ValueError("a custom allreduce needs rank and world (0 <= rank < world)")
+            self.rank, self.world = int(rank), int(world)
+        elif dist.is_available() and dist.is_initialized():
+            self.rank = dist.get_rank(group)
+            self.world = dist.get_world_size(group)
+        else:
+            self.rank, self.world = 0, 1
+        self._custom_allreduce = allreduce
+        n_ex = int(L.load().sae_b200_shard_exchange_floats(self.max_tokens, sae.d_in))
+        self.exchange = torch.empty(n_ex, device=self.device, dtype=torch.float32)
+        self.sumsq = torch.zeros(1, device=self.device, dtype=torch.float32)
+
+    def _allreduce(self, t: torch.Tensor) -> None:
+        if self._custom_allreduce is not None:
+            self._custom_allreduce(t)
+        elif self.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
+    def microbatch(self, x: torch.Tensor, *, accum_steps: int = 1, first: bool = True,
+                   lambda_l0: float = 0.0, al_mu: float = 0.0, target_l0: float = 0.0,
+                   x_hat_out: Optional[torch.Tensor] = None) -> dict:
+        sae = self.sae
+        x = self._check_input(x)
+        n = x.shape[0]
+        if first:
+            self.fired.zero_()
+        cfg = self._cfg(n, accum_steps, first, lambda_l0, al_mu, target_l0)
+        model = sae._model_struct(need_shadows=True)
+        stream = _stream()
+        dt = L.DTYPE_BF16 if x.dtype == torch.bfloat16 else L.DTYPE_F32
+        ex = self.exchange[:n * (sae.d_in + 1)]
+        L.call("sae_b200_shard_forward", ctypes.byref(model), L.ptr(x), dt, ctypes.byref(cfg),
+               L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), L.ptr(self.fired), L.ptr(ex),
+               stream)
+        self._allreduce(ex)                                    # partial x_hat + L0 counts
+        L.call("sae_b200_shard_finish_forward", ctypes.byref(model), L.ptr(x), dt,
+               ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), L.ptr(ex),
+               L.ptr(x_hat_out), stream)
+        st = self.read_stats()
+        self.nnz_last = st["nnz"]
+        grads = self._grads_struct()
+        scratch = None
+        if st["csr_overflow"]:
+            self.dense_fallbacks += 1
+            scratch = self._dense_scratch_for(n)
+        else:
+            sae._sparse_decode_calls += 1
+        L.call("sae_b200_shard_backward", ctypes.byref(model), ctypes.byref(grads),
+               ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), self.rank,
+               L.ptr(scratch), stream)
+        self._allreduce(self.g_b_dec)                          # b_dec gradient
+        self._bind_grads()
+        return st
+
+    def grad_norm(self, max_norm: float = 1.0) -> None:
+        model = self.sae._model_struct(need_shadows=False)
+        grads = self._grads_struct()
+        if self.rank != 0:
+            grads.b_dec = 0          # the replicated b_dec gradient counts once
+        stream = _stream()
+        L.call("sae_b200_grad_sumsq", ctypes.byref(model), ctypes.byref(grads),
+               L.ptr(self.norm_ws), self.norm_ws.numel(), L.ptr(self.sumsq), stream)
+        self._allreduce(self.sumsq)                            # clip_grad_norm_ sum
+        L.call("sae_b200_clip_from_sumsq", L.ptr(self.sumsq), float(max_norm),
+               L.ptr(self.stats), stream)

@@ -219,6 +219,25 @@ class FusedStep:
                             0 if first else 1, 1 if self.sae.W_dec.weight.requires_grad else 0,
                             1 if self.force_simt else 0)
 
+    def _check_input(self, x: torch.Tensor) -> torch.Tensor:
+        _require_cuda(x)
+        if x.dim() != 2 or x.shape[1] != self.sae.d_in:
+            raise ValueError(f"x must be [tokens, {self.sae.d_in}]")
+        if x.shape[0] > self.max_tokens:
+            raise ValueError(f"microbatch of {x.shape[0]} tokens exceeds "
+                             f"max_tokens={self.max_tokens}")
+        if x.dtype not in (torch.bfloat16, torch.float32):
+            x = x.float()
+        return x.contiguous()
+
+    def _dense_scratch_for(self, n_tokens: int) -> torch.Tensor:
+        """bf16 [F, ldp] buffer of the dense weight-gradient path (allocated on
+        the first microbatch whose active set overflows the CSR)."""
+        need = L.pre_pitch(n_tokens) * self.sae.n_features
+        if self._dense_scratch is None or self._dense_scratch.numel() < need:
+            self._dense_scratch = torch.empty(need, device=self.device, dtype=torch.bfloat16)
+        return self._dense_scratch
+
     def read_stats(self) -> dict:
         """One device->host copy of the StepStats (synchronises the stream)."""
         self._host_stats.copy_(self.stats, non_blocking=True)
@@ -234,15 +253,8 @@ class FusedStep:
         sparse or the dense weight-gradient path -- an active set larger than
         the workspace is never truncated) and returns them."""
         sae = self.sae
-        _require_cuda(x)
-        if x.dim() != 2 or x.shape[1] != sae.d_in:
-            raise ValueError(f"x must be [tokens, {sae.d_in}]")
+        x = self._check_input(x)
         n = x.shape[0]
-        if n > self.max_tokens:
-            raise ValueError(f"microbatch of {n} tokens exceeds max_tokens={self.max_tokens}")
-        if x.dtype not in (torch.bfloat16, torch.float32):
-            x = x.float()
-        x = x.contiguous()
         if first:
             self.fired.zero_()
         cfg = self._cfg(n, accum_steps, first, lambda_l0, al_mu, target_l0)
@@ -257,12 +269,9 @@ class FusedStep:
         grads = self._grads_struct()
         if st["csr_overflow"]:
             self.dense_fallbacks += 1
-            need = L.pre_pitch(n) * sae.n_features   # [F, ldp] feature-major
-            if self._dense_scratch is None or self._dense_scratch.numel() < need:
-                self._dense_scratch = torch.empty(need, device=self.device, dtype=torch.bfloat16)
             L.call("sae_b200_train_backward_dense", ctypes.byref(model), ctypes.byref(grads),
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
-                   L.ptr(self._dense_scratch), stream)
+                   L.ptr(self._dense_scratch_for(n)), stream)
         else:
             sae._sparse_decode_calls += 1
             L.call("sae_b200_train_backward", ctypes.byref(model), ctypes.byref(grads),

@@ -126,10 +126,12 @@ int64_t sae_b200_launch_count(void);
 /* Optional timing hook: while set, the library records start_event before and
  * stop_event after every launch of the chosen kernel on the launch stream
  * (cudaEvent_t handles owned by the caller; NULL, NULL clears it).
- * kernel: SAE_KERNEL_ENCODER_GEMM (tile GEMM of sae_b200_train_forward) or
- * SAE_KERNEL_GRAD_GEMM (tile GEMM of sae_b200_train_backward). */
+ * kernel: SAE_KERNEL_ENCODER_GEMM (tile GEMM of the forwards),
+ * SAE_KERNEL_GRAD_GEMM (tile GEMM of the backwards) or SAE_KERNEL_DECODE
+ * (gathered decode of the forwards). */
 #define SAE_KERNEL_ENCODER_GEMM 0
 #define SAE_KERNEL_GRAD_GEMM 1
+#define SAE_KERNEL_DECODE 2   /* the gathered decode of every forward */
 int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event);
 
 /* Bytes of scratch the training step needs for up to max_tokens tokens. */
@@ -196,6 +198,65 @@ int sae_b200_train_backward_dense(const SaeB200Model* model, const SaeB200Grads*
 int sae_b200_grad_norm(const SaeB200Model* model, const SaeB200Grads* grads, float max_norm,
                        void* workspace, size_t workspace_bytes, SaeB200StepStats* stats,
                        void* stream);
+
+/* Inference: encoder GEMM + JumpReLU gate + gathered decode, no loss and no
+ * backward state: x_hat_out [n_tokens, d] fp32 = bf16(gathered decoder sum) +
+ * b_dec, the forward of the module (encode 910-912 + decode 922-950; also the
+ * inference helper examples/use_trained_sae.py:58-75). active_counts_out
+ * (optional, int32 [n_tokens]) gets each token's L0; fired (optional, uint8
+ * [F]) is OR-accumulated. workspace: sae_b200_workspace_bytes(n_tokens, d, F, 0). */
+int sae_b200_encode_decode(const SaeB200Model* model, const void* x, int x_dtype,
+                           int64_t n_tokens, void* workspace, size_t workspace_bytes,
+                           float* x_hat_out, int32_t* active_counts_out, uint8_t* fired,
+                           void* stream);
+
+/* ------------------------------------------- dictionary-sharded wide SAE
+ * One wide SAE with its dictionary split over GPUs: each rank holds features
+ * [r*F/N, (r+1)*F/N) (W_enc rows, b_enc, W_dec columns, log_threshold, their
+ * gradients and Adam state); x and b_dec are replicated. The reference trains
+ * the whole dictionary on one device; these entry points split the same step
+ * (sae_trainer_rolling.py:2914-3090) at its three cross-feature sums, which the
+ * caller adds over the ranks (e.g. an NCCL all-reduce on the same stream):
+ *   1. sae_b200_shard_forward writes `exchange` = this shard's fp32 decoder
+ *      sums [n_tokens, d] followed by its per-token active counts [n_tokens]
+ *      (as floats); all-reduce(SUM) it, then sae_b200_shard_finish_forward
+ *      forms x_hat = bf16(sum) + b_dec, the residual, loss, L0 and go (the
+ *      same on every rank).
+ *   2. sae_b200_shard_backward (shard_rank 0 owns the replicated b_dec term):
+ *      all-reduce(SUM) grads->b_dec afterwards.
+ *   3. sae_b200_grad_sumsq (pass b_dec's gradient on rank 0 only, NULL
+ *      elsewhere): all-reduce(SUM) the float, then sae_b200_clip_from_sumsq.
+ * The Adam step is local (b_dec's update is identical on every rank). With
+ * N = 1 the sequence gives the same result as the unsharded entry points up
+ * to fp32 summation order. */
+int64_t sae_b200_shard_exchange_floats(int64_t n_tokens, int64_t d_in);
+/* Encoder GEMM + gate + CSR offsets + gathered decode of this shard's features
+ * (decode / _SparseDecode.forward 922-950 restricted to the shard). */
+int sae_b200_shard_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                           const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                           SaeB200StepStats* stats, uint8_t* fired, float* exchange,
+                           void* stream);
+/* Residual, reconstruction loss, sparsity term and go from the summed
+ * exchange (loss lines 2963-2974). */
+int sae_b200_shard_finish_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                                  const SaeB200StepConfig* cfg, void* workspace,
+                                  size_t workspace_bytes, SaeB200StepStats* stats,
+                                  const float* exchange, float* x_hat_out, void* stream);
+/* sae_b200_train_backward (dense_scratch NULL) or _dense (dense_scratch set)
+ * of this shard; on shard_rank != 0 the b_dec gradient is overwritten with the
+ * shard's encoder term -(sum_b dpre) W_enc_shard only (601), so that the sum
+ * over ranks is the full gradient, accumulated once. */
+int sae_b200_shard_backward(const SaeB200Model* model, const SaeB200Grads* grads,
+                            const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                            SaeB200StepStats* stats, int shard_rank, void* dense_scratch,
+                            void* stream);
+/* *sumsq_out (device float) = sum of squares of the non-NULL gradients. */
+int sae_b200_grad_sumsq(const SaeB200Model* model, const SaeB200Grads* grads, void* workspace,
+                        size_t workspace_bytes, float* sumsq_out, void* stream);
+/* stats->grad_norm = sqrt(*sumsq), stats->clip_coef = min(1, max_norm/(norm+1e-6))
+ * (clip_grad_norm_, 3049). */
+int sae_b200_clip_from_sumsq(const float* sumsq, float max_norm, SaeB200StepStats* stats,
+                             void* stream);
 
 /* L2-decay Adam (torch.optim.Adam, sae_trainer_rolling.py:2536-2541, 3076)
  * fused with the decoder-column / encoder-row renormalisation (778-782,

@@ -357,3 +357,120 @@ def superposition_batch(n_tokens: int, d: int, n_dirs: int, k_active: int, norm_
     norms = np.exp(norm_mu + norm_sigma * rng.standard_normal(n_tokens)).astype(np.float32)
     x *= (norms / np.maximum(np.linalg.norm(x, axis=1), 1e-8))[:, None]
     return x.astype(np.float32)
+
+
+# ------------------------------------------------ dictionary-sharded step
+# The reference trains one dictionary on one device. A wide SAE split over GPUs
+# along the dictionary (rank r holds features [r F/N, (r+1) F/N): rows of W_enc,
+# b_enc, log_threshold, columns of W_dec; x and b_dec replicated) computes the
+# same step if exactly three cross-feature sums are added over the ranks: the
+# decoder output and the per-token active counts (forward), the encoder term of
+# the b_dec gradient (601), and the sum of squares of the global clip (3049).
+# ``allreduce(a)`` is the caller's sum over ranks (identity for one rank).
+
+def shard_params(p: Params, rank: int, world: int) -> Params:
+    """Rank ``rank``'s slice of the dictionary (b_dec replicated)."""
+    F = p.W_enc.shape[0]
+    if F % world:
+        raise ValueError("n_features must divide evenly over the ranks")
+    s = slice(rank * F // world, (rank + 1) * F // world)
+    return Params(p.W_enc[s].copy(), p.b_enc[s].copy(), p.W_dec[:, s].copy(), p.b_dec.copy(),
+                  p.log_threshold[s].copy())
+
+
+def sharded_forward(x, p: Params, cfg: StepConfig, allreduce, precision: str = "fp32",
+                    theta=None) -> ForwardOut:
+    """forward() over one shard: the decoder sum and counts are all-reduced
+    before the bias, the residual and the loss terms."""
+    B = x.shape[0]
+    acc_dt = np.float64 if precision in ("fp64", "bf16") else np.float32
+    if precision == "bf16":
+        if theta is None:
+            theta = np.exp(p.log_threshold.astype(np.float32)).astype(np.float32)
+        theta = np.asarray(theta, np.float32)
+        xc = bf16(x.astype(np.float32) - p.b_dec.astype(np.float32))
+        pre = bf16((xc.astype(acc_dt) @ bf16(p.W_enc).astype(acc_dt).T
+                    + bf16(p.b_enc).astype(acc_dt)).astype(np.float32))
+        gate = (pre > theta).astype(np.float32)
+        feat = pre * gate
+        part = bf16(feat).astype(acc_dt) @ bf16(p.W_dec).astype(acc_dt).T
+    else:
+        dt = _dt(precision)
+        x = x.astype(dt)
+        theta = np.exp(p.log_threshold.astype(dt)) if theta is None else np.asarray(theta, dt)
+        xc = x - p.b_dec.astype(dt)
+        pre = xc @ p.W_enc.astype(dt).T + p.b_enc.astype(dt)
+        gate = (pre > theta).astype(dt)
+        feat = pre * gate
+        part = feat @ p.W_dec.astype(dt).T
+    exchange = np.concatenate([part.reshape(-1), gate.sum(axis=1).astype(part.dtype)])
+    exchange = allreduce(exchange)
+    dec = exchange[:B * x.shape[1]].reshape(B, -1)
+    counts = exchange[B * x.shape[1]:]
+    if precision == "bf16":
+        x_hat = bf16(dec.astype(np.float32)) + p.b_dec.astype(np.float32)
+        residual = x.astype(np.float32) - x_hat
+    else:
+        x_hat = (dec + p.b_dec.astype(dec.dtype)).astype(_dt(precision))
+        residual = x - x_hat
+    n = residual.size
+    recon = float(np.square(residual.astype(acc_dt)).sum() / n / cfg.accum_steps)
+    l0 = float(counts.astype(np.float64).mean())
+    diff = l0 - cfg.target_l0
+    slack = max(diff, 0.0)
+    sparsity = (cfg.lambda_l0 * slack + 0.5 * cfg.al_mu * slack * slack) / cfg.accum_steps
+    gate_grad = ((cfg.lambda_l0 + cfg.al_mu * slack) / cfg.accum_steps / B) if diff >= 0 else 0.0
+    return ForwardOut(theta, xc, pre, gate, feat, x_hat, residual, counts, recon, l0, sparsity,
+                      gate_grad, recon + sparsity)
+
+
+def sharded_backward(x, p: Params, fw: ForwardOut, cfg: StepConfig, rank: int, allreduce,
+                     precision: str = "fp32") -> Grads:
+    """backward() over one shard. Everything but the b_dec gradient is local;
+    rank 0 contributes Σ_b go, every rank its -(Σ_b dpre) W_enc term, and the
+    sum over ranks is the full b_dec gradient."""
+    g = backward(x, p, fw, cfg, precision)
+    go = g.extras["go"]
+    a = np.float64 if precision == "bf16" else _dt(precision)
+    gb_go = go.astype(np.float32 if precision == "bf16" else a)
+    if precision == "bf16":
+        go_sum = (-(np.float32(1.0 / (cfg.accum_steps * x.shape[0] * x.shape[1]))
+                    * (2.0 * fw.residual)).astype(np.float32)).astype(a).sum(axis=0)
+        enc_term = -(g.b_enc.astype(a) @ bf16(p.W_enc).astype(a))
+    else:
+        go_sum = gb_go.sum(axis=0)
+        enc_term = -(g.b_enc @ p.W_enc.astype(a))
+    mine = (go_sum if rank == 0 else 0.0) + enc_term
+    g.b_dec = allreduce(np.asarray(mine)).astype(g.b_dec.dtype)
+    return g
+
+
+def sharded_clip_coef(g: Grads, max_norm: float, rank: int, allreduce) -> tuple[float, float]:
+    """clip_coef() over shards: the replicated b_dec gradient counts once."""
+    tot = 0.0
+    for k in PARAM_NAMES:
+        v = getattr(g, k)
+        if v is None or (k == "b_dec" and rank != 0):
+            continue
+        tot += float(np.square(v.astype(np.float64)).sum())
+    tot = float(allreduce(np.array([tot]))[0])
+    norm = math.sqrt(tot)
+    return norm, min(1.0, max_norm / (norm + 1e-6))
+
+
+def sharded_train_step(xs, p: Params, st: AdamState, cfg: StepConfig, rank: int, allreduce,
+                       precision: str = "fp32", theta=None) -> StepResult:
+    """train_step() of one shard; Adam and the renormalisations are local (each
+    W_dec column and W_enc row lives on one rank)."""
+    g = None
+    fws = []
+    for x in xs:
+        fw = sharded_forward(x, p, cfg, allreduce, precision, theta)
+        gb = sharded_backward(x, p, fw, cfg, rank, allreduce, precision)
+        g = add_grads(g, gb)
+        fws.append(fw)
+    norm, clip = sharded_clip_coef(g, cfg.max_norm, rank, allreduce)
+    newp = adam_step(p, g, st, cfg, clip)
+    recon = sum(f.recon_loss for f in fws) * cfg.accum_steps / len(fws)
+    l0 = sum(f.l0 for f in fws) / len(fws)
+    return StepResult(newp, g, fws, norm, clip, recon, l0)
