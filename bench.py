@@ -217,6 +217,7 @@ def run_inference(args):
 
     wl = INFER
     d, F, tokens = wl["d"], wl["F"], wl["tokens"]
+    tokens = args.tokens or tokens
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -256,6 +257,8 @@ def run_inference(args):
     for i in range(args.warmup):
         step(pool[i % 2])
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for e in sum(ev, []):
+        e.record()    # creates the CUDA events before the library records them
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -376,6 +379,7 @@ def run_b200(args):
 
     wl = WORKLOADS[args.workload]
     d, F_total, tokens, k_target = wl["d"], wl["F"], wl["tokens"], wl["k"]
+    tokens = args.tokens or tokens
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -403,9 +407,9 @@ def run_b200(args):
     opt = sae_b200.B200Adam(sae_b200.reference_param_groups(sae, wl["lr"]), lr=wl["lr"],
                             betas=(0.9, 0.999), sae=sae, renorm=True)
     if sharded:
-        fs = sae_b200.ShardedFusedStep(sae, opt, max_tokens=tokens)
+        fs = sae_b200.ShardedFusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat)
     else:
-        fs = sae_b200.FusedStep(sae, opt, max_tokens=tokens)
+        fs = sae_b200.FusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat)
 
     def step(i, x):
         out = fs.step(x, lambda_l0=LAMBDA, al_mu=MU, target_l0=k_target,
@@ -489,13 +493,15 @@ def run_b200(args):
         enc_tf = gemm_flop / (enc_ms / 1e3) / 1e12
         grad_tf = gemm_flop / (grad_ms / 1e3) / 1e12
         traffic_scale = (d * F) / (D_IN * N_FEAT) * (tokens / TOKENS)
+        gemm_bwd = args.grad_feat == "gemm"
         dom_ms, dom_tf, dom_name, dom_traffic = (
             (enc_ms, enc_tf, "encoder tile GEMM (tcgen05 cta_group::2) + JumpReLU epilogue",
-             TRAFFIC_ENCODER_GEMM) if enc_ms >= grad_ms else
+             TRAFFIC_ENCODER_GEMM) if (enc_ms >= grad_ms or not gemm_bwd) else
             (grad_ms, grad_tf, "grad_feat tile GEMM (tcgen05 cta_group::2) + STE epilogue",
              TRAFFIC_GRAD_GEMM))
         peak = peaks["bf16_sustained"]
-        step_flop = 4.0 * tokens * d * F_total
+        dense_per_token = (4 if gemm_bwd else 2) * d * F_total
+        step_flop = float(dense_per_token) * tokens
         line = {
             "metric": METRIC if not sharded else
             "wide-SAE fwd+bwd+Adam tokens/s at d=4096x131072 L0~64 (dictionary-sharded)",
@@ -518,8 +524,12 @@ def run_b200(args):
                        "l2": "inputs rotate over a 4-batch pool; every step writes the "
                              f"{2 * tokens * F / 1e9:.1f} GB bf16 pre-activation tensor, which "
                              "flushes the 126 MB L2",
-                       "dense_gemm_flop_per_token": 4 * d * F_total,
-                       "weight_grads": "sparse (CSR gather) -- 4*d*F dense FLOP/token"},
+                       "dense_gemm_flop_per_token": dense_per_token,
+                       "backward": ("dense tcgen05 grad_feat GEMM + STE epilogue, sparse CSR "
+                                    "weight gradients: 4*d*F dense FLOP/token" if gemm_bwd else
+                                    "sampled: grad_feat dot products on the active and in-band "
+                                    "entries only, fused with the STE and the sparse weight "
+                                    "gradients: 2*d*F dense FLOP/token (the encoder)")},
             "roofline": {"bound": "tensor", "kernel": dom_name,
                          "achieved": dom_tf, "peak": peak, "unit": "TFLOP/s",
                          "frac": dom_tf / peak,
@@ -529,9 +539,11 @@ def run_b200(args):
                                          "4096-token d=1536 F=49152 launch, scaled by tokens "
                                          "and by d*F",
                          "per_launch_flop": gemm_flop, "launch_ms": dom_ms},
-            "kernels": {"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
-                        "grad_gemm_ms": grad_ms, "grad_gemm_tflops": grad_tf,
-                        "step_dense_tflops": step_flop / (ms / 1e3) / 1e12},
+            "kernels": ({"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
+                         "grad_gemm_ms": grad_ms, "grad_gemm_tflops": grad_tf} if gemm_bwd else
+                        {"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
+                         "sampled_backward_ms": grad_ms}) |
+                       {"step_dense_tflops": step_flop / (ms / 1e3) / 1e12},
             "clocks": clock,
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": world * tokens * d * 2,
@@ -569,6 +581,12 @@ def main():
                          "sharded: one d=4096 F=131072 SAE split over the GPUs; inference: "
                          "encode + gathered decode at d=2304 F=65536")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="tokens per step (default: the workload's); smaller values are for "
+                         "profiler captures, not for the reported metric")
+    ap.add_argument("--grad-feat", choices=["sampled", "gemm"], default="sampled",
+                    help="backward: grad_feat on the active + in-band entries only (default), "
+                         "or the dense tcgen05 grad_feat GEMM")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,0 +1,366 @@
+// Dead-feature aux loss of the training step (sae_trainer_rolling.py:2986-2998):
+//   pre_dead = relu(pre[:, dead]); (vals, idx) = topk(pre_dead, k) per token;
+//   x_aux = bf16(Σ vals · W_dec[:, dead[idx]]); aux = coeff · mean((r - x_aux)^2) / accum
+// with r = x - x_hat detached. Zero and negative pre-activations contribute
+// nothing (relu), so only the positive candidates are ever selected.
+//
+// Layout: the selected entries of token b sit at [b * k, b * k + cnt[b]) of
+// two arrays (dead-list index j, value), in increasing j; the backward works
+// on the same entries sorted by j (stable, so tokens ascend within a feature).
+#pragma once
+#include <cuda_bf16.h>
+#include <cstdint>
+#include "ptx.cuh"
+
+namespace sae {
+
+constexpr int AUX_TB = 32;   // tokens per selection block (one per lane)
+
+// bf16 bits of a positive value order like the value; everything else -> 0.
+__device__ __forceinline__ uint32_t aux_key(uint16_t bits) {
+  return (bits & 0x8000u) ? 0u : bits;
+}
+
+// Per block of 32 tokens: a two-round radix select (high byte, then low byte
+// of the bf16 key) finds each token's k-th largest positive key T and how
+// many of the keys equal to T to take (the lowest dead indices first); a
+// third pass over the dead rows writes the selected entries in dead order.
+// 256 threads; rows are read as 64-byte segments of the feature-major
+// pre-activations (one row = one dead feature's 32 tokens).
+__global__ void __launch_bounds__(256)
+    aux_select_kernel(const bf16* __restrict__ pre, int ldp, const int32_t* __restrict__ dead,
+                      int n_dead, int n_features, int k, int64_t n_tokens,
+                      int32_t* __restrict__ list_j,
+                      float* __restrict__ list_v, int32_t* __restrict__ cnt,
+                      int32_t* __restrict__ count_j) {
+  __shared__ uint32_t hist[AUX_TB][257];
+  __shared__ uint16_t tile[32][AUX_TB + 2];
+  __shared__ uint32_t s_hi[AUX_TB], s_above[AUX_TB], s_T[AUX_TB], s_m[AUX_TB];
+  __shared__ int s_base[AUX_TB], s_ties[AUX_TB];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * AUX_TB;
+  const bool tok_ok = t0 + lane < n_tokens;
+  const uint16_t* pre16 = reinterpret_cast<const uint16_t*>(pre);
+
+  auto key_at = [&](int j) -> uint32_t {
+    if (!tok_ok) return 0u;
+    const int f = min(max(dead[j], 0), n_features - 1);   // ids are checked by the caller
+    return aux_key(pre16[static_cast<size_t>(f) * ldp + t0 + lane]);
+  };
+
+  // round 1: histogram of the high byte of every positive key
+  for (int i = tid; i < AUX_TB * 257; i += blockDim.x) (&hist[0][0])[i] = 0u;
+  __syncthreads();
+  for (int j = warp; j < n_dead; j += 8) {
+    const uint32_t key = key_at(j);
+    if (key) atomicAdd(&hist[lane][key >> 8], 1u);
+  }
+  __syncthreads();
+  if (tid < AUX_TB) {
+    uint32_t cum = 0, hi = 0, total = 0;
+    for (int b = 255; b >= 0; --b) total += hist[tid][b];
+    if (total <= static_cast<uint32_t>(k)) {
+      s_hi[tid] = 0xFFFFFFFFu;   // take every positive key
+      s_above[tid] = 0;
+    } else {
+      for (int b = 255; b >= 0; --b) {
+        if (cum + hist[tid][b] >= static_cast<uint32_t>(k)) {
+          hi = b;
+          break;
+        }
+        cum += hist[tid][b];
+      }
+      s_hi[tid] = hi;
+      s_above[tid] = cum;
+    }
+  }
+  __syncthreads();
+  // round 2: low byte inside the chosen high-byte bin
+  for (int i = tid; i < AUX_TB * 257; i += blockDim.x) (&hist[0][0])[i] = 0u;
+  __syncthreads();
+  for (int j = warp; j < n_dead; j += 8) {
+    const uint32_t key = key_at(j);
+    if (key && (key >> 8) == s_hi[lane]) atomicAdd(&hist[lane][key & 0xFFu], 1u);
+  }
+  __syncthreads();
+  if (tid < AUX_TB) {
+    if (s_hi[tid] == 0xFFFFFFFFu) {
+      s_T[tid] = 1u;              // every positive key is > 0
+      s_m[tid] = 0xFFFFFFFFu;
+    } else {
+      uint32_t cum = s_above[tid];
+      uint32_t lo = 0;
+      for (int b = 255; b >= 0; --b) {
+        if (cum + hist[tid][b] >= static_cast<uint32_t>(k)) {
+          lo = b;
+          break;
+        }
+        cum += hist[tid][b];
+      }
+      s_T[tid] = (s_hi[tid] << 8) | lo;
+      s_m[tid] = static_cast<uint32_t>(k) - cum;   // keys equal to T still to take
+    }
+    s_base[tid] = 0;
+    s_ties[tid] = 0;
+  }
+  __syncthreads();
+  // round 3: rows in chunks of 32 through shared memory; warp w owns tokens
+  // w, w + 8, w + 16, w + 24 and walks the chunk's rows in order (lane = row)
+  for (int j0 = 0; j0 < n_dead; j0 += 32) {
+    for (int r = warp; r < 32; r += 8) {
+      const int j = j0 + r;
+      tile[r][lane] = (j < n_dead) ? static_cast<uint16_t>(key_at(j)) : 0;
+    }
+    __syncthreads();
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int q = warp; q < AUX_TB; q += 8) {
+      const int64_t b = t0 + q;
+      if (b >= n_tokens) continue;   // uniform per warp
+      const int j = j0 + lane;
+      const uint32_t key = (j < n_dead) ? tile[lane][q] : 0u;
+      const uint32_t T = s_T[q];
+      const bool eq = key != 0u && key == T;
+      const uint32_t eqb = __ballot_sync(0xffffffffu, eq);
+      const uint32_t rank = static_cast<uint32_t>(s_ties[q]) + __popc(eqb & lt);
+      const bool sel = key != 0u && (key > T || (eq && rank < s_m[q]));
+      const uint32_t sb = __ballot_sync(0xffffffffu, sel);
+      const int pos = s_base[q] + __popc(sb & lt);
+      if (sel && pos < k) {
+        list_j[b * k + pos] = j;
+        list_v[b * k + pos] = __uint_as_float(key << 16);
+        atomicAdd(&count_j[j], 1);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        s_base[q] += __popc(sb);
+        s_ties[q] += __popc(eqb);
+      }
+      __syncwarp();
+    }
+    __syncthreads();
+  }
+  if (tid < AUX_TB && t0 + tid < n_tokens) cnt[t0 + tid] = min(s_base[tid], k);
+}
+
+// Per token (grid-stride, d/8 threads): x_aux = bf16(Σ v · W_dec[dead[j]])
+// over the token's selected entries in dead order, e = (x - x_hat) - x_aux,
+// the token's Σ e² and g = bf16(-(2 coeff / (B d accum)) e), the gradient
+// reaching x_aux (what the bf16 aux matmul's backward sees).
+template <typename XT>
+__global__ void __launch_bounds__(1024)
+    aux_decode_kernel(const int32_t* __restrict__ list_j, const float* __restrict__ list_v,
+                      const int32_t* __restrict__ cnt, const int32_t* __restrict__ dead,
+                      int n_features, int k,
+                      const bf16* __restrict__ w_dec, const XT* __restrict__ x,
+                      const float* __restrict__ x_hat, int64_t n_tokens, int d, float g_scale,
+                      bf16* __restrict__ g_aux, float* __restrict__ aux_sq) {
+  __shared__ float s_tmp[33];
+  const int col = threadIdx.x;
+  const int nvec = d / 8;
+  const bool has = col < nvec;
+  const uint4* wcol = reinterpret_cast<const uint4*>(w_dec) + col;
+  for (int64_t b = blockIdx.x; b < n_tokens; b += gridDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    const int n = cnt[b];
+    float sq = 0.f;
+    if (has) {
+      int i = 0;
+      for (; i + 3 < n; i += 4) {
+        uint4 u[4];
+        float a[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int f = min(max(dead[list_j[b * k + i + r]], 0), n_features - 1);
+          a[r] = list_v[b * k + i + r];
+          u[r] = __ldg(wcol + static_cast<size_t>(f) * nvec);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float wf[8];
+          unpack8(u[r], wf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = fmaf(a[r], wf[j], acc[j]);
+        }
+      }
+      for (; i < n; ++i) {
+        const int f = min(max(dead[list_j[b * k + i]], 0), n_features - 1);
+        float wf[8];
+        unpack8(__ldg(wcol + static_cast<size_t>(f) * nvec), wf);
+        const float a = list_v[b * k + i];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+      }
+      const size_t base = static_cast<size_t>(b) * d + col * 8;
+      float xv[8];
+      if constexpr (sizeof(XT) == 2) {
+        unpack8(*reinterpret_cast<const uint4*>(x + base), xv);
+      } else {
+        const float4 a = *reinterpret_cast<const float4*>(x + base);
+        const float4 c = *reinterpret_cast<const float4*>(x + base + 4);
+        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+        xv[4] = c.x; xv[5] = c.y; xv[6] = c.z; xv[7] = c.w;
+      }
+      const float4 h0 = *reinterpret_cast<const float4*>(x_hat + base);
+      const float4 h1 = *reinterpret_cast<const float4*>(x_hat + base + 4);
+      const float xh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+      float gv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = __fsub_rn(xv[j], xh[j]);
+        const float e = __fsub_rn(r, bf16_round(acc[j]));
+        sq = fmaf(e, e, sq);
+        gv[j] = -__fmul_rn(g_scale, e);
+      }
+      *reinterpret_cast<uint4*>(g_aux + base) = pack8(gv);
+    }
+    const float tot = block_sum(sq, s_tmp);
+    if (threadIdx.x == 0) aux_sq[b] = tot;
+  }
+}
+
+// aux = coeff * Σ_b aux_sq[b] / (B d) / accum, added to the step's loss.
+__global__ void __launch_bounds__(1024)
+    aux_stats_kernel(const float* __restrict__ aux_sq, int64_t n_tokens, int d, float coeff,
+                     int accum, SaeB200StepStats* stats) {
+  __shared__ float s_tmp[33];
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n_tokens; i += blockDim.x) s += aux_sq[i];
+  const float tot = block_sum(s, s_tmp);
+  if (threadIdx.x == 0) {
+    const float aux = tot / static_cast<float>(static_cast<double>(n_tokens) * d) * coeff /
+                      static_cast<float>(accum);
+    stats->aux_loss = aux;
+    stats->loss += aux;
+  }
+}
+
+// Sort keys/values for the backward: key = dead-list index (n_dead for an
+// empty slot, sorted last), value = token << 32 | float bits of the value.
+__global__ void aux_pack_kernel(const int32_t* __restrict__ list_j,
+                                const float* __restrict__ list_v, const int32_t* __restrict__ cnt,
+                                int64_t n_tokens, int k, int n_dead, uint32_t* __restrict__ keys,
+                                uint64_t* __restrict__ vals) {
+  const int64_t total = n_tokens * k;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = i / k;
+    const int r = static_cast<int>(i - b * k);
+    const bool ok = r < cnt[b];
+    keys[i] = ok ? static_cast<uint32_t>(list_j[i]) : static_cast<uint32_t>(n_dead);
+    vals[i] = ok ? ((static_cast<uint64_t>(b) << 32) | __float_as_uint(list_v[i])) : 0ull;
+  }
+}
+
+// Per dead feature (blocks take them from a counter), over its entries in
+// token order: dpre = bf16(g_aux[b] . W_dec[f]) (the topk/relu backward of
+// the bf16 matmul), dW_enc[f] += dpre xc[b], db += dpre, dW_dec[f] += v g_aux[b].
+// Adds to the gradients of the main backward; db goes to db_full[f] for the
+// b_dec term. One row group of d/8 threads; 8 entries per chunk.
+template <int MAX_THREADS>
+__global__ void __launch_bounds__(MAX_THREADS)
+    aux_backward_kernel(const int32_t* __restrict__ offs, const uint64_t* __restrict__ vals,
+                        const int32_t* __restrict__ dead, int n_dead, int n_features,
+                        int64_t n_tokens,
+                        const bf16* __restrict__ g_aux, const bf16* __restrict__ xc,
+                        const bf16* __restrict__ w_dec, int d, float* __restrict__ g_wdec,
+                        float* __restrict__ g_wenc, float* __restrict__ g_benc,
+                        float* __restrict__ db_full, int* __restrict__ counter) {
+  __shared__ int s_f[2];
+  __shared__ float s_red[32][8];
+  __shared__ float s_gf[8];
+  const int tid = threadIdx.x, lane = tid & 31, wig = tid >> 5;
+  const int nwg = (blockDim.x + 31) >> 5;
+  const int nvec = d / 8;
+  const bool has = tid < nvec;
+  const uint4* ga_v = reinterpret_cast<const uint4*>(g_aux) + tid;
+  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + tid;
+  int it = 0;
+  while (true) {
+    if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
+    __syncthreads();
+    const int jd = s_f[it & 1];
+    ++it;
+    if (jd >= n_dead) break;
+    const int f = min(max(dead[jd], 0), n_features - 1);
+    const int s = offs[jd], e = offs[jd + 1];
+    float wf[8];
+    if (has) unpack8(__ldg(reinterpret_cast<const uint4*>(w_dec) + static_cast<size_t>(f) * nvec + tid), wf);
+    float ad[8], ae[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ad[j] = ae[j] = 0.f;
+    float db = 0.f;
+    for (int i0 = s; i0 < e; i0 += 8) {
+      const int n = min(8, e - i0);
+      int t[8];
+      float v[8], part[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const uint64_t pv = r < n ? vals[i0 + r] : 0ull;
+        const int64_t tv = static_cast<int64_t>(pv >> 32);
+        t[r] = static_cast<int>(tv < n_tokens ? tv : n_tokens - 1);
+        v[r] = __uint_as_float(static_cast<uint32_t>(pv));
+      }
+      uint4 gu[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        gu[r] = (has && r < n) ? __ldg(ga_v + static_cast<size_t>(t[r]) * nvec)
+                               : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        float g8[8];
+        unpack8(gu[r], g8);
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a = fmaf(g8[j], has ? wf[j] : 0.f, a);
+        part[r] = a;
+      }
+      const float q = warp_sum8(part, lane);
+      if ((lane & 3) == 0) s_red[wig][lane >> 2] = q;
+      __syncthreads();
+      if (tid < 8) {
+        float a = 0.f;
+        for (int w = 0; w < nwg; ++w) a += s_red[w][tid];
+        s_gf[tid] = bf16_round(a);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r < n) {
+          const float dp = s_gf[r];
+          db += dp;
+          if (has) {
+            float g8[8], x8[8];
+            unpack8(gu[r], g8);
+            unpack8(__ldg(xc_v + static_cast<size_t>(t[r]) * nvec), x8);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              ad[j] = fmaf(v[r], g8[j], ad[j]);
+              ae[j] = fmaf(dp, x8[j], ae[j]);
+            }
+          }
+        }
+      }
+    }
+    if (has && e > s) {
+      const size_t o = static_cast<size_t>(f) * d + tid * 8;
+      if (g_wdec != nullptr) {
+        float4* p = reinterpret_cast<float4*>(g_wdec + o);
+        const float4 u = p[0], w = p[1];
+        p[0] = make_float4(u.x + ad[0], u.y + ad[1], u.z + ad[2], u.w + ad[3]);
+        p[1] = make_float4(w.x + ad[4], w.y + ad[5], w.z + ad[6], w.w + ad[7]);
+      }
+      float4* p = reinterpret_cast<float4*>(g_wenc + o);
+      const float4 u = p[0], w = p[1];
+      p[0] = make_float4(u.x + ae[0], u.y + ae[1], u.z + ae[2], u.w + ae[3]);
+      p[1] = make_float4(w.x + ae[4], w.y + ae[5], w.z + ae[6], w.w + ae[7]);
+    }
+    if (tid == 0) {
+      if (e > s) g_benc[f] += db;
+      db_full[f] = db;
+    }
+  }
+}
+
+}  // namespace sae

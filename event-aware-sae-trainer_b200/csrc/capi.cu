@@ -12,9 +12,13 @@
 #include <mutex>
 #include <string>
 
+#include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
+
 #include "dense_kernels.cuh"
 #include "sae_b200.h"
 #include "step_kernels.cuh"
+#include "aux_kernels.cuh"
 #include "tile_gemm.cuh"
 
 using namespace sae;
@@ -79,8 +83,9 @@ DeviceInfo device_info() {
 
 // ------------------------------------------------------------ workspace
 struct Layout {
-  size_t theta, xc, pre, mask, tile_cnt, col_tot, col_offs, go, tok_sqerr, tok_cnt, gosum_part,
-      thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part, counters, total;
+  size_t theta, xc, pre, mask, tile_cnt, tile_band, col_tot, col_act, col_offs, go, tok_sqerr,
+      tok_cnt, gosum_part, thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part,
+      counters, total;
 };
 
 // Row pitch (tokens) of the feature-major pre-activations: whole 64-token
@@ -108,7 +113,9 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   L.pre = take(static_cast<size_t>(F) * pre_pitch(B) * 2);   // feature-major [F, ldp]
   L.mask = take(B * W * 4);
   L.tile_cnt = take(nT * F * 4);
+  L.tile_band = take(nT * F * 4);
   L.col_tot = take(F * 4);
+  L.col_act = take(F * 4);
   L.col_offs = take((F + 1) * 4);
   L.go = take(B * d * 2);
   L.tok_sqerr = take(B * 4);
@@ -132,7 +139,9 @@ struct Ws {
   bf16* pre;
   uint32_t* mask;
   int* tile_cnt;
+  int* tile_band;
   int* col_tot;
+  int* col_act;
   int* col_offs;
   bf16* go;
   float* tok_sqerr;
@@ -156,7 +165,9 @@ Ws carve(void* base, const Layout& L) {
   w.pre = reinterpret_cast<bf16*>(at(L.pre));
   w.mask = reinterpret_cast<uint32_t*>(at(L.mask));
   w.tile_cnt = reinterpret_cast<int*>(at(L.tile_cnt));
+  w.tile_band = reinterpret_cast<int*>(at(L.tile_band));
   w.col_tot = reinterpret_cast<int*>(at(L.col_tot));
+  w.col_act = reinterpret_cast<int*>(at(L.col_act));
   w.col_offs = reinterpret_cast<int*>(at(L.col_offs));
   w.go = reinterpret_cast<bf16*>(at(L.go));
   w.tok_sqerr = reinterpret_cast<float*>(at(L.tok_sqerr));
@@ -478,6 +489,7 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
                    uint8_t* fired, cudaStream_t stream) {
   const int64_t B = c.B, d = c.d, F = c.F;
   const Ws& w = c.w;
+  const bool sampled = cfg->grad_feat_gemm == 0;
   // 1. theta, xc
   {
     const int g = grid_for(std::max<int64_t>(F, B * d / 8), 256);
@@ -499,6 +511,8 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
     e.pre = w.pre;
     e.mask = w.mask;
     e.tile_cnt = w.tile_cnt;
+    e.tile_band = sampled ? w.tile_band : nullptr;
+    e.eps = cfg->ste_bandwidth;
     e.n_tokens = static_cast<int>(B);
     e.n_features = static_cast<int>(F);
     e.mask_words = c.mask_words;
@@ -507,12 +521,15 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
                              tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_ENCODER_GEMM,
                              w.pre));
   }
-  // 3. per-feature scans -> CSR offsets
-  scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(w.tile_cnt, w.col_tot, fired,
-                                                            2 * c.n_tiles, static_cast<int>(F));
+  // 3. per-feature scans -> CSR offsets (active entries, plus the inactive
+  //    in-band ones for the sampled backward)
+  scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(
+      w.tile_cnt, w.col_tot, fired, 2 * c.n_tiles, static_cast<int>(F),
+      sampled ? w.tile_band : nullptr, sampled ? w.col_act : nullptr);
   SAE_TRY(check_launch("scan_columns_kernel"));
   scan_offsets_kernel<<<1, 1024, 0, stream>>>(w.col_tot, w.col_offs, static_cast<int>(F),
-                                              cfg->csr_capacity, stats, w.counters);
+                                              cfg->csr_capacity, stats, w.counters,
+                                              sampled ? w.col_act : nullptr);
   return check_launch("scan_offsets_kernel");
 }
 
@@ -627,6 +644,205 @@ int sae_b200_encode_decode(const SaeB200Model* model, const void* x, int x_dtype
   return SAE_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+struct AuxLayout {
+  size_t list_j, list_v, cnt, g_aux, aux_sq, keys0, keys1, vals0, vals1, count_j, offs, db_full,
+      gemv_part, counter, cub_tmp, cub_bytes, total;
+};
+
+int aux_end_bit(int64_t n_dead) {
+  int b = 1;
+  while ((int64_t(1) << b) <= n_dead) ++b;
+  return b;
+}
+
+int make_aux_layout(int64_t B, int64_t d, int64_t F, int64_t n_dead, int64_t k, AuxLayout* A) {
+  *A = AuxLayout{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  const size_t items = static_cast<size_t>(B) * k;
+  A->list_j = take(items * 4);
+  A->list_v = take(items * 4);
+  A->cnt = take(B * 4);
+  A->g_aux = take(B * d * 2);
+  A->aux_sq = take(B * 4);
+  A->keys0 = take(items * 4);
+  A->keys1 = take(items * 4);
+  A->vals0 = take(items * 8);
+  A->vals1 = take(items * 8);
+  A->count_j = take((n_dead + 1) * 4);
+  A->offs = take((n_dead + 1) * 4);
+  A->db_full = take(F * 4);
+  A->gemv_part = take(static_cast<size_t>(GEMV_GRID) * d * 4);
+  A->counter = take(256);
+  size_t sort_bytes = 0, scan_bytes = 0;
+  if (cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, static_cast<uint32_t*>(nullptr),
+                                      static_cast<uint32_t*>(nullptr),
+                                      static_cast<uint64_t*>(nullptr),
+                                      static_cast<uint64_t*>(nullptr), static_cast<int>(items),
+                                      0, aux_end_bit(n_dead)) != cudaSuccess ||
+      cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int32_t*>(nullptr),
+                                    static_cast<int32_t*>(nullptr),
+                                    static_cast<int>(n_dead + 1)) != cudaSuccess)
+    return fail(SAE_ERR_CUDA, "temporary-storage query of the aux sort failed");
+  A->cub_bytes = std::max(sort_bytes, scan_bytes);
+  A->cub_tmp = take(A->cub_bytes);
+  A->total = off;
+  return SAE_OK;
+}
+
+int check_aux(const SaeB200Model* model, const SaeB200StepConfig* cfg, const SaeB200AuxConfig* a,
+              void* aux_ws, size_t aux_bytes, AuxLayout* A) {
+  if (a == nullptr || a->dead == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "aux config is NULL");
+  if (a->n_dead <= 0 || a->n_dead > model->n_features || a->k < 1 || a->k > a->n_dead ||
+      a->k > 4096)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "aux needs 1 <= k <= min(n_dead, 4096), n_dead <= F");
+  if (static_cast<int64_t>(cfg->n_tokens) * a->k > (int64_t(1) << 31) - 1)
+    return fail(SAE_ERR_UNSUPPORTED_SHAPE, "n_tokens * k must stay below 2^31");
+  SAE_TRY(make_aux_layout(cfg->n_tokens, model->d_in, model->n_features, a->n_dead, a->k, A));
+  if (aux_ws == nullptr || (reinterpret_cast<uintptr_t>(aux_ws) & 255u) != 0)
+    return fail(SAE_ERR_MISALIGNED, "aux workspace must be 256-byte aligned");
+  if (aux_bytes < A->total)
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "aux workspace has %zu bytes, needs %zu", aux_bytes,
+                A->total);
+  return SAE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sae_b200_aux_workspace_bytes(int64_t max_tokens, int64_t d_in, int64_t n_features,
+                                 int64_t max_dead, int32_t k, size_t* bytes_out) {
+  if (bytes_out == nullptr || max_tokens <= 0 || d_in <= 0 || n_features <= 0 || max_dead <= 0 ||
+      k < 1)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid aux workspace query");
+  AuxLayout A;
+  SAE_TRY(make_aux_layout(max_tokens, d_in, n_features, max_dead, k, &A));
+  *bytes_out = A.total;
+  return SAE_OK;
+}
+
+int sae_b200_aux_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                         const float* x_hat, const SaeB200StepConfig* cfg, void* workspace,
+                         size_t workspace_bytes, const SaeB200AuxConfig* aux, void* aux_ws,
+                         size_t aux_bytes, SaeB200StepStats* stats, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  ForwardCtx c;
+  SAE_TRY(forward_checks(model, x, x_dtype, cfg, workspace, workspace_bytes, stats, x_hat, &c));
+  if (x_hat == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "aux needs the forward's x_hat");
+  AuxLayout A;
+  SAE_TRY(check_aux(model, cfg, aux, aux_ws, aux_bytes, &A));
+  auto at = [&](size_t o) { return static_cast<uint8_t*>(aux_ws) + o; };
+  int32_t* list_j = reinterpret_cast<int32_t*>(at(A.list_j));
+  float* list_v = reinterpret_cast<float*>(at(A.list_v));
+  int32_t* cnt = reinterpret_cast<int32_t*>(at(A.cnt));
+  int32_t* count_j = reinterpret_cast<int32_t*>(at(A.count_j));
+  const int n_dead = static_cast<int>(aux->n_dead);
+  if (cudaMemsetAsync(count_j, 0, (n_dead + 1) * sizeof(int32_t), stream) != cudaSuccess)
+    return fail(SAE_ERR_CUDA, "aux count reset failed");
+  const unsigned blocks = static_cast<unsigned>((c.B + AUX_TB - 1) / AUX_TB);
+  aux_select_kernel<<<blocks, 256, 0, stream>>>(c.w.pre, static_cast<int>(pre_pitch(c.B)),
+                                                aux->dead, n_dead, static_cast<int>(c.F), aux->k,
+                                                c.B, list_j, list_v, cnt, count_j);
+  SAE_TRY(check_launch("aux_select_kernel"));
+  const float g_scale = static_cast<float>(
+      2.0 * aux->coeff / (static_cast<double>(c.B) * c.d * cfg->accum_steps));
+  const int V = vec_threads(c.d);
+  bf16* g_aux = reinterpret_cast<bf16*>(at(A.g_aux));
+  float* aux_sq = reinterpret_cast<float*>(at(A.aux_sq));
+  if (x_dtype == SAE_DTYPE_BF16)
+    aux_decode_kernel<bf16><<<DECODE_GRID, V, 0, stream>>>(
+        list_j, list_v, cnt, aux->dead, static_cast<int>(c.F), aux->k,
+        static_cast<const bf16*>(model->W_dec_bf16), static_cast<const bf16*>(x), x_hat, c.B,
+        static_cast<int>(c.d), g_scale, g_aux, aux_sq);
+  else
+    aux_decode_kernel<float><<<DECODE_GRID, V, 0, stream>>>(
+        list_j, list_v, cnt, aux->dead, static_cast<int>(c.F), aux->k,
+        static_cast<const bf16*>(model->W_dec_bf16), static_cast<const float*>(x), x_hat, c.B,
+        static_cast<int>(c.d), g_scale, g_aux, aux_sq);
+  SAE_TRY(check_launch("aux_decode_kernel"));
+  aux_stats_kernel<<<1, 1024, 0, stream>>>(aux_sq, c.B, static_cast<int>(c.d), aux->coeff,
+                                           cfg->accum_steps, stats);
+  return check_launch("aux_stats_kernel");
+}
+
+int sae_b200_aux_backward(const SaeB200Model* model, const SaeB200Grads* grads,
+                          const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                          const SaeB200AuxConfig* aux, void* aux_ws, size_t aux_bytes,
+                          void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  SAE_TRY(check_model(model, true));
+  SAE_TRY(check_cfg(cfg));
+  SAE_TRY(check_fused_shape(model));
+  if (grads == nullptr || !grads->W_enc || !grads->b_enc || !grads->b_dec)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "gradient pointer is NULL");
+  const int64_t B = cfg->n_tokens, d = model->d_in, F = model->n_features;
+  const Layout L = make_layout(B, d, F, cfg->csr_capacity);
+  SAE_TRY(check_ws(L, workspace, workspace_bytes));
+  const Ws w = carve(workspace, L);
+  AuxLayout A;
+  SAE_TRY(check_aux(model, cfg, aux, aux_ws, aux_bytes, &A));
+  auto at = [&](size_t o) { return static_cast<uint8_t*>(aux_ws) + o; };
+  const int n_dead = static_cast<int>(aux->n_dead);
+  const int items = static_cast<int>(B * aux->k);
+  uint32_t* keys0 = reinterpret_cast<uint32_t*>(at(A.keys0));
+  uint32_t* keys1 = reinterpret_cast<uint32_t*>(at(A.keys1));
+  uint64_t* vals0 = reinterpret_cast<uint64_t*>(at(A.vals0));
+  uint64_t* vals1 = reinterpret_cast<uint64_t*>(at(A.vals1));
+  int32_t* count_j = reinterpret_cast<int32_t*>(at(A.count_j));
+  int32_t* offs = reinterpret_cast<int32_t*>(at(A.offs));
+  float* db_full = reinterpret_cast<float*>(at(A.db_full));
+  int* counter = reinterpret_cast<int*>(at(A.counter));
+  // 1. entries sorted by dead index (stable: tokens ascend within a feature)
+  aux_pack_kernel<<<grid_for(items, 256), 256, 0, stream>>>(
+      reinterpret_cast<const int32_t*>(at(A.list_j)), reinterpret_cast<const float*>(at(A.list_v)),
+      reinterpret_cast<const int32_t*>(at(A.cnt)), B, aux->k, n_dead, keys0, vals0);
+  SAE_TRY(check_launch("aux_pack_kernel"));
+  size_t tmp = A.cub_bytes;
+  if (cub::DeviceRadixSort::SortPairs(at(A.cub_tmp), tmp, keys0, keys1, vals0, vals1, items, 0,
+                                      aux_end_bit(n_dead), stream) != cudaSuccess)
+    return fail(SAE_ERR_CUDA, "aux sort failed");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  tmp = A.cub_bytes;
+  if (cub::DeviceScan::ExclusiveSum(at(A.cub_tmp), tmp, count_j, offs, n_dead + 1, stream) !=
+      cudaSuccess)
+    return fail(SAE_ERR_CUDA, "aux scan failed");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  // 2. per dead feature: dpre, dW_enc, dW_dec, b_enc
+  if (cudaMemsetAsync(db_full, 0, F * sizeof(float), stream) != cudaSuccess ||
+      cudaMemsetAsync(counter, 0, sizeof(int), stream) != cudaSuccess)
+    return fail(SAE_ERR_CUDA, "aux reset failed");
+  const int V = vec_threads(d);
+#define SAE_AUX_BWD(MT)                                                                        \
+  aux_backward_kernel<MT><<<device_info().sm_count * std::max(1, 2048 / V), V, 0, stream>>>(   \
+      offs, vals1, aux->dead, n_dead, static_cast<int>(F), B,                                   \
+      reinterpret_cast<const bf16*>(at(A.g_aux)), w.xc,                                         \
+      static_cast<const bf16*>(model->W_dec_bf16), static_cast<int>(d),                         \
+      cfg->train_decoder ? grads->W_dec_fm : nullptr, grads->W_enc, grads->b_enc, db_full,      \
+      counter)
+  if (V <= 512) SAE_AUX_BWD(512);
+  else SAE_AUX_BWD(1024);
+#undef SAE_AUX_BWD
+  SAE_TRY(check_launch("aux_backward_kernel"));
+  // 3. b_dec: minus the aux encoder term -(sum dpre_aux) W_enc
+  float* gemv_part = reinterpret_cast<float*>(at(A.gemv_part));
+  bdec_gemv_kernel<<<GEMV_GRID, V, 0, stream>>>(
+      db_full, static_cast<const bf16*>(model->W_enc_bf16), static_cast<int>(F),
+      static_cast<int>(d), gemv_part);
+  SAE_TRY(check_launch("bdec_gemv_kernel"));
+  bdec_grad_kernel<<<static_cast<unsigned>((d + 31) / 32), 1024, 0, stream>>>(
+      w.gosum_part, 0, gemv_part, GEMV_GRID, static_cast<int>(d), 1, grads->b_dec);
+  return check_launch("bdec_grad_kernel");
+}
+
 int64_t sae_b200_shard_exchange_floats(int64_t n_tokens, int64_t d_in) {
   if (n_tokens <= 0 || d_in <= 0) return 0;
   return n_tokens * d_in + n_tokens;
@@ -691,6 +907,46 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
   const int n_tiles = static_cast<int>((B + TILE_N - 1) / TILE_N);
   const int acc = cfg->accumulate ? 1 : 0;
   float* g_wdec = cfg->train_decoder ? grads->W_dec_fm : nullptr;
+  const int thr = vec_threads(d);
+
+  // Sampled backward (cfg->grad_feat_gemm == 0): grad_feat only on the active
+  // and in-band entries; otherwise the dense tcgen05 grad_feat GEMM with the
+  // STE epilogue, then the CSR weight-gradient gather. Same gradients.
+  if (dense_scratch == nullptr && cfg->grad_feat_gemm == 0) {
+    // 1. CSR of the active and in-band entries, feature-major, token order
+    csr_fill_kernel<<<grid_for(F * 32, 256, 16), 256, 0, stream>>>(
+        w.pre, w.theta, w.col_offs, static_cast<int>(F), B, static_cast<int>(pre_pitch(B)),
+        cfg->ste_bandwidth, stats, w.csr_tok, w.csr_val);
+    SAE_TRY(check_launch("csr_fill_kernel"));
+    // 2. sampled grad_feat + STE + weight gradients, one feature at a time
+    const int G = std::max(1, std::min(2, 512 / thr));
+    const size_t dyn = static_cast<size_t>(G - 1) * thr * 4 * sizeof(float4);
+    const int grid = device_info().sm_count * std::max(1, 2048 / (thr * G));
+    timer_begin(SAE_KERNEL_GRAD_GEMM, stream);
+#define SAE_SAMPLED(GG, MT)                                                                    \
+  sampled_backward_kernel<GG, MT><<<grid, thr * GG, dyn, stream>>>(                           \
+      w.col_offs, w.csr_tok, w.csr_val, w.go, w.xc,                                           \
+      static_cast<const bf16*>(model->W_dec_bf16), w.theta, static_cast<int>(F),               \
+      static_cast<int>(B), static_cast<int>(d), cfg->ste_bandwidth, acc, g_wdec, grads->W_enc,  \
+      grads->log_threshold,                                                                    \
+      grads->b_enc, w.db_enc, w.counters, stats)
+    if (G >= 2) SAE_SAMPLED(2, 512);
+    else if (thr <= 512) SAE_SAMPLED(1, 512);
+    else SAE_SAMPLED(1, 1024);
+#undef SAE_SAMPLED
+    const int rc = check_launch("sampled_backward_kernel");
+    timer_end(SAE_KERNEL_GRAD_GEMM, stream);
+    SAE_TRY(rc);
+    // 3. b_dec gradient
+    bdec_gemv_kernel<<<GEMV_GRID, thr, 0, stream>>>(
+        w.db_enc, static_cast<const bf16*>(model->W_enc_bf16), static_cast<int>(F),
+        static_cast<int>(d), w.gemv_part);
+    SAE_TRY(check_launch("bdec_gemv_kernel"));
+    bdec_grad_kernel<<<static_cast<unsigned>((d + 31) / 32), 1024, 0, stream>>>(
+        w.gosum_part, bdec_owner ? DECODE_GRID : 0, w.gemv_part, GEMV_GRID, static_cast<int>(d),
+        bdec_owner ? acc : 0, grads->b_dec);
+    return check_launch("bdec_grad_kernel");
+  }
 
   // 1. dense grad_feat GEMM with the STE epilogue (+ CSR fill)
   {
@@ -719,7 +975,6 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
       grads->log_threshold, grads->b_enc, w.db_enc);
   SAE_TRY(check_launch("feature_grads_kernel"));
   // 3. b_dec gradient
-  const int thr = vec_threads(d);
   bdec_gemv_kernel<<<GEMV_GRID, thr, 0, stream>>>(w.db_enc, static_cast<const bf16*>(model->W_enc_bf16),
                                                   static_cast<int>(F), static_cast<int>(d),
                                                   w.gemv_part);
@@ -903,7 +1158,42 @@ int sae_b200_adam_step(const SaeB200Model* model, const SaeB200Grads* grads,
                             aligned16(params[k]) && aligned16(gs[k]) &&
                             aligned16(state->exp_avg[k]) && aligned16(state->exp_avg_sq[k]) &&
                             (shadows[k] == nullptr || (reinterpret_cast<uintptr_t>(shadows[k]) & 7u) == 0);
+    // wide-row kernel: VPT float4 per thread, threads per row a multiple of 32
+    int vpt = 0, tpr = 0;
     if (row_kernel) {
+      const int64_t nv = cols[k] / 4;
+      for (const int cand : {2, 4, 1, 3, 6, 8}) {
+        if (nv % cand == 0 && (nv / cand) % 32 == 0 && nv / cand <= 512) {
+          vpt = cand;
+          tpr = static_cast<int>(nv / cand);
+          break;
+        }
+      }
+    }
+    if (row_kernel && vpt > 0) {
+      const int rpb = std::max(1, 512 / tpr);
+      const int threads = rpb * tpr;
+      const int64_t blocks_needed = (rows[k] + rpb - 1) / rpb;
+      const int per_sm = std::max(1, 2048 / threads);
+      const int g = static_cast<int>(
+          std::min<int64_t>(blocks_needed, static_cast<int64_t>(device_info().sm_count) * per_sm));
+      const int rn = h.renorm_rows ? 1 : 0;
+#define SAE_ADAM_WIDE(V)                                                                    \
+  adam_rows_wide_kernel<V><<<g, threads, 0, stream>>>(params[k], gs[k], state->exp_avg[k],   \
+                                                      state->exp_avg_sq[k], shadows[k],     \
+                                                      rows[k], static_cast<int>(cols[k]),   \
+                                                      tpr, s, stats, rn)
+      switch (vpt) {
+        case 1: SAE_ADAM_WIDE(1); break;
+        case 2: SAE_ADAM_WIDE(2); break;
+        case 3: SAE_ADAM_WIDE(3); break;
+        case 4: SAE_ADAM_WIDE(4); break;
+        case 6: SAE_ADAM_WIDE(6); break;
+        default: SAE_ADAM_WIDE(8); break;
+      }
+#undef SAE_ADAM_WIDE
+      SAE_TRY(check_launch("adam_rows_wide_kernel"));
+    } else if (row_kernel) {
       const int nv_lane = static_cast<int>((cols[k] / 4 + 31) / 32);
       const int g = grid_for(rows[k] * 32, 256);
       const int rn = h.renorm_rows ? 1 : 0;

@@ -150,11 +150,13 @@ struct EncodeEpi {
   bf16* pre;          // [F, ldp]
   uint32_t* mask;
   int* tile_cnt;
+  int* tile_band;     // optional: inactive entries inside the STE band, |pre - theta| < eps
+  float eps;
   int n_tokens, n_features, mask_words, ldp;
   // per-thread tile state
   int f, n0, lane, word, row;
   float th, bias;
-  int cnt;
+  int cnt, bcnt;
   bool row_ok;
   bf16* aux;
 
@@ -170,7 +172,7 @@ struct EncodeEpi {
     bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
     word = (m_tile * TILE_M + q * 32) >> 5;
   }
-  __device__ __forceinline__ void begin_half(int) { cnt = 0; }
+  __device__ __forceinline__ void begin_half(int) { cnt = 0; bcnt = 0; }
   __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
     const int t0 = n0 + c;
     const int nj = row_ok ? min(32, n_tokens - t0) : 0;
@@ -188,6 +190,7 @@ struct EncodeEpi {
       const uint32_t bal = __ballot_sync(0xffffffffu, act);
       if (lane == j) myword = bal;
       cnt += act ? 1 : 0;
+      bcnt += ((j < nj) && !act && fabsf(__fsub_rn(p, th)) < eps) ? 1 : 0;
     }
     if (aux != nullptr) {
       // tokens past n_tokens are clipped by the TMA store
@@ -209,7 +212,11 @@ struct EncodeEpi {
       mask[static_cast<size_t>(t) * mask_words + word] = myword;
   }
   __device__ __forceinline__ void end_half(int h) {
-    if (row_ok) tile_cnt[static_cast<size_t>(n0 / HALF_N + h) * n_features + f] = cnt;
+    if (row_ok) {
+      const size_t i = static_cast<size_t>(n0 / HALF_N + h) * n_features + f;
+      tile_cnt[i] = cnt;
+      if (tile_band != nullptr) tile_band[i] = bcnt;
+    }
   }
   __device__ __forceinline__ void end_tile() {}
 };
@@ -379,18 +386,24 @@ struct GradEpi {
 // ------------------------------------------------------------------- scans
 // Per feature: exclusive prefix of the per-tile active counts (in place),
 // the feature's total, and the OR-accumulated fired flag.
+// With tile_band (sampled backward): col_tot counts the feature's CSR entries
+// -- active plus inactive in-band -- and col_act its active entries.
 __global__ void scan_columns_kernel(int* __restrict__ tile_cnt, int* __restrict__ col_tot,
-                                    uint8_t* __restrict__ fired, int n_tiles, int n_features) {
+                                    uint8_t* __restrict__ fired, int n_tiles, int n_features,
+                                    const int* __restrict__ tile_band = nullptr,
+                                    int* __restrict__ col_act = nullptr) {
   for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < n_features;
        f += gridDim.x * blockDim.x) {
-    int run = 0;
+    int run = 0, band = 0;
     for (int t = 0; t < n_tiles; ++t) {
       const size_t i = static_cast<size_t>(t) * n_features + f;
       const int v = tile_cnt[i];
       tile_cnt[i] = run;
       run += v;
+      if (tile_band != nullptr) band += tile_band[i];
     }
-    col_tot[f] = run;
+    col_tot[f] = run + band;
+    if (col_act != nullptr) col_act[f] = run;
     if (fired != nullptr && run > 0) fired[f] = 1;
   }
 }
@@ -398,24 +411,311 @@ __global__ void scan_columns_kernel(int* __restrict__ tile_cnt, int* __restrict_
 // Exclusive scan of the per-feature totals into CSR row offsets (one block).
 __global__ void __launch_bounds__(1024)
     scan_offsets_kernel(const int* __restrict__ col_tot, int* __restrict__ col_offs, int n_features,
-                        int64_t capacity, SaeB200StepStats* stats, int* counters) {
+                        int64_t capacity, SaeB200StepStats* stats, int* counters,
+                        const int* __restrict__ col_act = nullptr) {
   __shared__ int s_tmp[33];
   const int per = (n_features + blockDim.x - 1) / blockDim.x;
   const int b = threadIdx.x * per;
   const int e = min(n_features, b + per);
-  int local = 0;
-  for (int i = b; i < e; ++i) local += col_tot[i];
+  int local = 0, act = 0;
+  for (int i = b; i < e; ++i) {
+    local += col_tot[i];
+    if (col_act != nullptr) act += col_act[i];
+  }
   int total = 0;
   int run = block_excl_scan(local, s_tmp, total);
   for (int i = b; i < e; ++i) {
     col_offs[i] = run;
     run += col_tot[i];
   }
+  int act_total = total;   // without col_act every CSR entry is active
+  if (col_act != nullptr) block_excl_scan(act, s_tmp, act_total);
   if (threadIdx.x == 0) {
     col_offs[n_features] = total;
-    stats->nnz = total;
+    stats->nnz = act_total;
+    stats->csr_pairs = total;
     stats->csr_overflow = (static_cast<int64_t>(total) > capacity) ? 1 : 0;
     counters[0] = 0;
+  }
+}
+
+// ----------------------------------------------------- sampled backward
+// The straight-through backward needs grad_feat = go . W_dec[f] only where
+// it is used: on active entries (grad_pre, db_enc, dW_enc) and on entries
+// inside the STE band |pre - theta| < eps (the threshold gradient); the rest of
+// the dense [B, F] product is multiplied by zero. The sampled path builds a
+// feature-major CSR of exactly those entries and computes each one as a dot
+// product of two bf16 rows.
+//
+// CSR fill: one warp per feature row of the feature-major pre-activations;
+// lane l covers tokens [t0 + 8l, t0 + 8l + 8) of each 256-token window, and a
+// warp scan places the entries in token order after the feature's offset.
+// Entry value: low 16 bits bf16 pre, bit 16 active (pre > theta), bit 17 in
+// band (|pre - theta| < eps).
+constexpr uint32_t CSR_ACTIVE = 1u << 16;
+constexpr uint32_t CSR_BAND = 1u << 17;
+
+__global__ void __launch_bounds__(256)
+    csr_fill_kernel(const bf16* __restrict__ pre, const float* __restrict__ theta,
+                    const int* __restrict__ col_offs, int n_features, int64_t n_tokens, int ldp,
+                    float eps, const SaeB200StepStats* stats, int* __restrict__ csr_tok,
+                    uint32_t* __restrict__ csr_val) {
+  if (stats->csr_overflow) return;
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int f = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; f < n_features; f += warps) {
+    const float th = theta[f];
+    const uint4* row = reinterpret_cast<const uint4*>(pre + static_cast<size_t>(f) * ldp);
+    int pos = col_offs[f];
+    const int end = col_offs[f + 1];   // the encoder counted exactly these entries
+    for (int64_t t0 = 0; t0 < n_tokens; t0 += 256) {
+      const int64_t tl = t0 + 8 * lane;
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (tl < n_tokens) u = __ldg(row + (tl >> 3));   // ldp % 64 == 0: the 8 stay in the row
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      uint32_t flags = 0;   // 2 bits per token
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float p = (j & 1) ? bf_hi(w[j >> 1]) : bf_lo(w[j >> 1]);
+        const bool ok = tl + j < n_tokens;
+        const uint32_t a = (ok && p > th) ? 1u : 0u;
+        const uint32_t bnd = (ok && fabsf(__fsub_rn(p, th)) < eps) ? 2u : 0u;
+        flags |= (a | bnd) << (2 * j);
+      }
+      int mine = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mine += ((flags >> (2 * j)) & 3u) ? 1 : 0;
+      int incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int tot = __shfl_sync(0xffffffffu, incl, 31);
+      if (mine) {
+        int q = pos + incl - mine;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t fl = (flags >> (2 * j)) & 3u;
+          if (fl) {
+            if (q < end) {
+              csr_tok[q] = static_cast<int>(tl + j);
+              csr_val[q] = ((w[j >> 1] >> (16 * (j & 1))) & 0xFFFFu) | (fl << 16);
+            }
+            ++q;
+          }
+        }
+      }
+      pos += tot;
+    }
+  }
+}
+
+// Sum over the 32 lanes of each of 8 values: after the call, lane l with
+// (l & 3) == 0 holds the total of value ((l >> 2) & 7) (a transpose-style
+// butterfly: 4 + 2 + 1 exchanges halve the live values, 2 more finish).
+__device__ __forceinline__ float warp_sum8(float (&p)[8], int lane) {
+  float q4[4], q2[2];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const bool hi = lane & 16;
+    const float keep = hi ? p[k + 4] : p[k];
+    const float send = hi ? p[k] : p[k + 4];
+    q4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const bool hi = lane & 8;
+    const float keep = hi ? q4[k + 2] : q4[k];
+    const float send = hi ? q4[k] : q4[k + 2];
+    q2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  const bool hi = lane & 4;
+  float q = (hi ? q2[1] : q2[0]) + __shfl_xor_sync(0xffffffffu, hi ? q2[0] : q2[1], 4);
+  q += __shfl_xor_sync(0xffffffffu, q, 2);
+  q += __shfl_xor_sync(0xffffffffu, q, 1);
+  return q;
+}
+
+// Per feature (blocks take features from a global counter): for its CSR
+// entries, in chunks of 8, grad_feat = bf16(go[t] . W_dec[f]) (fp32
+// accumulation, the bf16 GEMM output of 643), then
+//   active:  dpre = grad_feat; db_enc += dpre; dW_enc[f] += dpre * xc[t];
+//            dW_dec[f] += pre * go[t]
+//   in band: STE sum += pre * grad_feat + gate_grad
+// and at the end the threshold gradient -(sum / 2 eps) * theta. A block is G
+// row groups of V = d/8 threads; group g takes chunks g, g + G, ... and the
+// group sums are combined in a fixed order: the result does not depend on
+// timing.
+template <int G, int MAX_THREADS>
+__global__ void __launch_bounds__(MAX_THREADS)
+    sampled_backward_kernel(const int* __restrict__ col_offs, const int* __restrict__ csr_tok,
+                            const uint32_t* __restrict__ csr_val, const bf16* __restrict__ go,
+                            const bf16* __restrict__ xc, const bf16* __restrict__ w_dec,
+                            const float* __restrict__ theta, int n_features, int n_tokens,
+                            int d, float eps, int accumulate, float* __restrict__ g_wdec,
+                            float* __restrict__ g_wenc, float* __restrict__ g_logthr,
+                            float* __restrict__ g_benc, float* __restrict__ db_enc,
+                            int* __restrict__ counter, const SaeB200StepStats* stats) {
+  if (stats->csr_overflow) return;
+  __shared__ int s_f[2];
+  __shared__ float s_red[G][32][8];   // per group, per warp, 8 partial dots
+  __shared__ float s_gf[G][8];
+  __shared__ float s_sc[G][2];
+  extern __shared__ float4 s_part[];   // (G - 1) x V x 4 float4
+  const int tid = threadIdx.x;
+  const int V = blockDim.x / G;
+  const int g = tid / V;
+  const int col = tid - g * V;
+  const int lane = tid & 31;
+  const int wig = col >> 5;              // warp index inside the group
+  const int nwg = (V + 31) >> 5;
+  const int nvec = d / 8;
+  const bool has = col < nvec;
+  const float gate_grad = stats->gate_grad;
+  const uint4* go_v = reinterpret_cast<const uint4*>(go) + col;
+  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + col;
+  int it = 0;
+  while (true) {
+    if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
+    __syncthreads();
+    const int f = s_f[it & 1];
+    ++it;
+    if (f >= n_features) break;
+    const int s = col_offs[f], e = col_offs[f + 1];
+    float wf[8];
+    if (has) unpack8(__ldg(reinterpret_cast<const uint4*>(w_dec) + static_cast<size_t>(f) * nvec + col), wf);
+    float ad[8], ae[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ad[j] = ae[j] = 0.f;
+    float thr = 0.f, db = 0.f;
+    const int n_chunks = (e - s + 7) >> 3;
+    for (int kb = 0; kb < n_chunks; kb += G) {   // same trip count in every group
+      const int i0 = s + 8 * (kb + g);
+      const int n = max(0, min(8, e - i0));
+      int t[8];
+      uint32_t v[8];
+      float part[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        // (the clamp only guards the row reads; the fill writes tokens < n_tokens)
+        t[r] = r < n ? min(max(csr_tok[i0 + r], 0), n_tokens - 1) : 0;
+        v[r] = r < n ? csr_val[i0 + r] : 0u;
+      }
+      {
+        uint4 gu[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+          gu[r] = (has && r < n) ? __ldg(go_v + static_cast<size_t>(t[r]) * nvec)
+                                 : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          float gf8[8];
+          unpack8(gu[r], gf8);
+          float a = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a = fmaf(gf8[j], has ? wf[j] : 0.f, a);
+          part[r] = a;
+        }
+      }
+      const float q = warp_sum8(part, lane);
+      if ((lane & 3) == 0) s_red[g][wig][lane >> 2] = q;
+      __syncthreads();
+      if (col < 8) {
+        float a = 0.f;
+        for (int w = 0; w < nwg; ++w) a += s_red[g][w][col];
+        s_gf[g][col] = bf16_round(a);
+      }
+      __syncthreads();
+      // active entries: go rows again (just read, L1/L2-resident) and xc rows
+      uint4 gu[8], xu[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const bool a = has && r < n && (v[r] & CSR_ACTIVE);
+        gu[r] = a ? __ldg(go_v + static_cast<size_t>(t[r]) * nvec) : make_uint4(0, 0, 0, 0);
+        xu[r] = a ? __ldg(xc_v + static_cast<size_t>(t[r]) * nvec) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r < n) {
+          const float p = __uint_as_float(v[r] << 16);
+          const float gfv = s_gf[g][r];
+          if (v[r] & CSR_ACTIVE) {
+            float gf8[8], xf[8];
+            unpack8(gu[r], gf8);
+            unpack8(xu[r], xf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              ad[j] = fmaf(p, gf8[j], ad[j]);
+              ae[j] = fmaf(gfv, xf[j], ae[j]);
+            }
+            db += gfv;
+          }
+          if (v[r] & CSR_BAND) thr += __fadd_rn(__fmul_rn(p, gfv), gate_grad);
+        }
+      }
+    }
+    if constexpr (G > 1) {
+      if (n_chunks > 1) {   // uniform across the block
+        if (g > 0 && has) {
+          float4* p = s_part + ((g - 1) * V + col) * 4;
+          p[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
+          p[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
+          p[2] = make_float4(ae[0], ae[1], ae[2], ae[3]);
+          p[3] = make_float4(ae[4], ae[5], ae[6], ae[7]);
+        }
+        if (col == 0) {
+          s_sc[g][0] = thr;
+          s_sc[g][1] = db;
+        }
+        __syncthreads();
+        if (g == 0 && has) {
+#pragma unroll
+          for (int h = 0; h < G - 1; ++h) {
+            const float4* p = s_part + (h * V + col) * 4;
+            const float4 a0 = p[0], a1 = p[1], b0 = p[2], b1 = p[3];
+            ad[0] += a0.x; ad[1] += a0.y; ad[2] += a0.z; ad[3] += a0.w;
+            ad[4] += a1.x; ad[5] += a1.y; ad[6] += a1.z; ad[7] += a1.w;
+            ae[0] += b0.x; ae[1] += b0.y; ae[2] += b0.z; ae[3] += b0.w;
+            ae[4] += b1.x; ae[5] += b1.y; ae[6] += b1.z; ae[7] += b1.w;
+          }
+        }
+        if (tid == 0) {
+          for (int h = 1; h < G; ++h) {
+            thr += s_sc[h][0];
+            db += s_sc[h][1];
+          }
+        }
+        __syncthreads();
+      }
+    }
+    if (g == 0 && has) {
+      const size_t o = static_cast<size_t>(f) * d + col * 8;
+      if (g_wdec != nullptr) {
+        float4* p = reinterpret_cast<float4*>(g_wdec + o);
+        if (accumulate) {
+          const float4 u = p[0], w = p[1];
+          ad[0] += u.x; ad[1] += u.y; ad[2] += u.z; ad[3] += u.w;
+          ad[4] += w.x; ad[5] += w.y; ad[6] += w.z; ad[7] += w.w;
+        }
+        p[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
+        p[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
+      }
+      float4* p = reinterpret_cast<float4*>(g_wenc + o);
+      if (accumulate) {
+        const float4 u = p[0], w = p[1];
+        ae[0] += u.x; ae[1] += u.y; ae[2] += u.z; ae[3] += u.w;
+        ae[4] += w.x; ae[5] += w.y; ae[6] += w.z; ae[7] += w.w;
+      }
+      p[0] = make_float4(ae[0], ae[1], ae[2], ae[3]);
+      p[1] = make_float4(ae[4], ae[5], ae[6], ae[7]);
+    }
+    if (tid == 0) {
+      const float gl = -(thr / (eps + eps)) * theta[f];
+      g_logthr[f] = accumulate ? g_logthr[f] + gl : gl;
+      g_benc[f] = accumulate ? g_benc[f] + db : db;
+      db_enc[f] = db;
+    }
   }
 }
 
@@ -682,6 +982,7 @@ __global__ void __launch_bounds__(1024)
     const float ggrad =
         diff >= 0.f ? ((lambda_l0 + al_mu * slack) * inv_accum) / static_cast<float>(n_tokens) : 0.f;
     stats->recon_loss = recon;
+    stats->aux_loss = 0.f;   // sae_b200_aux_forward sets it when the aux loss is on
     stats->l0 = l0;
     stats->sparsity_loss = sparsity;
     stats->gate_grad = ggrad;
@@ -1019,6 +1320,97 @@ __global__ void __launch_bounds__(256)
           u.x = pack2(pp.x, pp.y);
           u.y = pack2(pp.z, pp.w);
           reinterpret_cast<uint2*>(shadow + r * cols)[idx] = u;
+        }
+      }
+    }
+  }
+}
+
+// Wide rows: TPR = cols / (4 VPT) threads (a multiple of 32) share a row, each
+// holding VPT float4 of it in registers; a block holds RPB rows, and the row
+// norm is a warp sum plus a fixed-order sum over the row's warps. All loads of
+// a thread are issued before the first use, so a warp keeps 4 VPT 16-byte
+// loads in flight -- the wide-row replacement of the warp-per-row kernel, whose
+// per-lane register array grows with the row width.
+template <int VPT>
+__global__ void __launch_bounds__(512)
+    adam_rows_wide_kernel(float* __restrict__ p, const float* __restrict__ g,
+                          float* __restrict__ m, float* __restrict__ v, bf16* __restrict__ shadow,
+                          int64_t rows, int cols, int tpr, AdamScalars h,
+                          const SaeB200StepStats* stats, int renorm) {
+  __shared__ float s_ss[32];
+  const int rpb = blockDim.x / tpr;
+  const int rl = threadIdx.x / tpr;            // row slot in the block
+  const int c = threadIdx.x - rl * tpr;        // thread within the row
+  const int wir = c >> 5, lane = threadIdx.x & 31;
+  const int wpr = tpr >> 5;                    // warps per row
+  const float clip = (h.use_clip && stats != nullptr) ? stats->clip_coef : 1.f;
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpb; r0 < rows;
+       r0 += static_cast<int64_t>(gridDim.x) * rpb) {
+    const int64_t r = r0 + rl;
+    const bool ok = rl < rpb && r < rows;
+    float4 pr[VPT], gr[VPT], mr[VPT], vr[VPT];
+    const size_t base = static_cast<size_t>(ok ? r : 0) * cols;
+    float4* p4 = reinterpret_cast<float4*>(p + base);
+    float4* m4 = reinterpret_cast<float4*>(m + base);
+    float4* v4 = reinterpret_cast<float4*>(v + base);
+    const float4* g4 = reinterpret_cast<const float4*>(g + base);
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = c + tpr * i;
+        pr[i] = p4[idx];
+        gr[i] = g4[idx];
+        mr[i] = m4[idx];
+        vr[i] = v4[idx];
+      }
+    }
+    float ss = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = c + tpr * i;
+        float4 pp = pr[i], mm = mr[i], vv = vr[i];
+        const float4 gg = gr[i];
+        pp.x = adam_update(pp.x, gg.x, mm.x, vv.x, h, clip);
+        pp.y = adam_update(pp.y, gg.y, mm.y, vv.y, h, clip);
+        pp.z = adam_update(pp.z, gg.z, mm.z, vv.z, h, clip);
+        pp.w = adam_update(pp.w, gg.w, mm.w, vv.w, h, clip);
+        m4[idx] = mm;
+        v4[idx] = vv;
+        pr[i] = pp;
+        ss += pp.x * pp.x + pp.y * pp.y + pp.z * pp.z + pp.w * pp.w;
+      }
+    }
+    float nrm = 1.f;
+    if (renorm) {
+      ss = warp_sum(ss);
+      __syncthreads();
+      if (lane == 0 && rl < rpb) s_ss[rl * wpr + wir] = ss;
+      __syncthreads();
+      if (ok) {
+        float t = 0.f;
+        for (int w = 0; w < wpr; ++w) t += s_ss[rl * wpr + w];
+        nrm = fmaxf(sqrtf(t), 1e-8f);
+      }
+    }
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int idx = c + tpr * i;
+        float4 pp = pr[i];
+        if (renorm) {
+          pp.x = __fdiv_rn(pp.x, nrm);
+          pp.y = __fdiv_rn(pp.y, nrm);
+          pp.z = __fdiv_rn(pp.z, nrm);
+          pp.w = __fdiv_rn(pp.w, nrm);
+        }
+        p4[idx] = pp;
+        if (shadow != nullptr) {
+          uint2 u;
+          u.x = pack2(pp.x, pp.y);
+          u.y = pack2(pp.z, pp.w);
+          reinterpret_cast<uint2*>(shadow + base)[idx] = u;
         }
       }
     }

@@ -73,6 +73,7 @@ class StepConfig(ctypes.Structure):
         ("accumulate", c_int32),
         ("train_decoder", c_int32),
         ("force_simt", c_int32),
+        ("grad_feat_gemm", c_int32),
     ]
 
 
@@ -87,12 +88,23 @@ class StepStats(ctypes.Structure):
         ("clip_coef", c_float),
         ("nnz", c_int32),
         ("csr_overflow", c_int32),
-        ("reserved", c_int32 * 7),
+        ("csr_pairs", c_int32),
+        ("aux_loss", c_float),
+        ("reserved", c_int32 * 5),
     ]
 
 
 STATS_FLOATS = ctypes.sizeof(StepStats) // 4
 STATS_FIELDS = [name for name, _ in StepStats._fields_ if name != "reserved"]
+
+
+class AuxConfig(ctypes.Structure):
+    _fields_ = [
+        ("dead", c_void_p),
+        ("n_dead", c_int64),
+        ("k", c_int32),
+        ("coeff", c_float),
+    ]
 
 
 class AdamTensor(ctypes.Structure):
@@ -135,6 +147,14 @@ _SIGNATURES = {
     "sae_b200_encode_decode": (
         [POINTER(Model), c_void_p, c_int, c_int64, c_void_p, c_size_t, c_void_p, c_void_p,
          c_void_p, c_void_p], c_int),
+    "sae_b200_aux_workspace_bytes": (
+        [c_int64, c_int64, c_int64, c_int64, c_int32, POINTER(c_size_t)], c_int),
+    "sae_b200_aux_forward": (
+        [POINTER(Model), c_void_p, c_int, c_void_p, POINTER(StepConfig), c_void_p, c_size_t,
+         POINTER(AuxConfig), c_void_p, c_size_t, c_void_p, c_void_p], c_int),
+    "sae_b200_aux_backward": (
+        [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t,
+         POINTER(AuxConfig), c_void_p, c_size_t, c_void_p], c_int),
     "sae_b200_shard_exchange_floats": ([c_int64, c_int64], c_int64),
     "sae_b200_shard_forward": (
         [POINTER(Model), c_void_p, c_int, POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
@@ -231,6 +251,14 @@ def device_status(clear: bool = True) -> int:
     lib = load()
     out = c_int(0)
     call("sae_b200_get_device_status", ctypes.byref(out), 1 if clear else 0)
+    return out.value
+
+
+def aux_workspace_bytes(max_tokens: int, d_in: int, n_features: int, max_dead: int,
+                        k: int) -> int:
+    out = c_size_t(0)
+    call("sae_b200_aux_workspace_bytes", max_tokens, d_in, n_features, max_dead, k,
+         ctypes.byref(out))
     return out.value
 
 

@@ -88,10 +88,11 @@ class ShardedFusedStep(FusedStep):
 
     def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int, *,
                  group=None, csr_capacity: Optional[int] = None, force_simt: bool = False,
+                 grad_feat: str = "sampled",
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None,
                  rank: Optional[int] = None, world: Optional[int] = None):
         super().__init__(sae, optimizer, max_tokens, csr_capacity=csr_capacity,
-                         force_simt=force_simt)
+                         force_simt=force_simt, grad_feat=grad_feat)
         self.group = group
         if allreduce is not None:
             if rank is None or world is None or not 0 <= rank < world:
@@ -117,6 +118,9 @@ class ShardedFusedStep(FusedStep):
                    lambda_l0: float = 0.0, al_mu: float = 0.0, target_l0: float = 0.0,
                    x_hat_out: Optional[torch.Tensor] = None) -> dict:
         sae = self.sae
+        if self._aux is not None:
+            raise NotImplementedError("the dead-feature aux loss needs a top-k over the whole "
+                                      "dictionary; it is not available on a dictionary shard")
         x = self._check_input(x)
         n = x.shape[0]
         if first:

@@ -158,6 +158,9 @@ class B200Adam(torch.optim.Optimizer):
         return loss
 
 
+AUX_COEFF = 1.0 / 32   # sae_trainer_rolling.py:224 (Gao et al. 2024)
+
+
 def _csr_capacity_default(tokens: int) -> int:
     per_token = int(os.environ.get("SAE_B200_CSR_PER_TOKEN", "512"))
     return max(1024, tokens * per_token)
@@ -167,7 +170,8 @@ class FusedStep:
     """Per-microbatch fused forward/backward plus the optimizer step."""
 
     def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int,
-                 csr_capacity: Optional[int] = None, force_simt: bool = False):
+                 csr_capacity: Optional[int] = None, force_simt: bool = False,
+                 grad_feat: str = "sampled"):
         _require_cuda(sae.W_enc.weight)
         if not isinstance(optimizer, B200Adam) or optimizer.sae is not sae:
             raise TypeError("FusedStep needs the B200Adam built over the same SAE")
@@ -176,6 +180,11 @@ class FusedStep:
         self.max_tokens = int(max_tokens)
         self.csr_capacity = int(csr_capacity or _csr_capacity_default(self.max_tokens))
         self.force_simt = bool(force_simt)
+        if grad_feat not in ("sampled", "gemm"):
+            raise ValueError("grad_feat must be 'sampled' or 'gemm'")
+        # "sampled": grad_feat = go . W_dec[f] only where the backward uses it
+        # (active entries and the STE band); "gemm": the dense tcgen05 product.
+        self.grad_feat = grad_feat
         dev = sae.W_enc.weight.device
         self.device = dev
         F, d = sae.n_features, sae.d_in
@@ -196,6 +205,10 @@ class FusedStep:
             if torch.cuda.is_available() else None
         self.nnz_last = 0
         self.dense_fallbacks = 0
+        # dead-feature aux loss state (set per step by set_aux)
+        self._aux = None          # (dead int32 cuda tensor, k, coeff) or None
+        self._aux_ws = None
+        self._x_hat = None
 
     # ------------------------------------------------------------ pieces
     def _bind_grads(self):
@@ -217,7 +230,40 @@ class FusedStep:
         return L.StepConfig(int(n_tokens), self.csr_capacity, float(lambda_l0), float(al_mu),
                             float(target_l0), float(self.sae.ste_bandwidth), int(accum_steps),
                             0 if first else 1, 1 if self.sae.W_dec.weight.requires_grad else 0,
-                            1 if self.force_simt else 0)
+                            1 if self.force_simt else 0, 1 if self.grad_feat == "gemm" else 0)
+
+    def set_aux(self, dead_indices: Optional[torch.Tensor], k: int = 0,
+                coeff: float = AUX_COEFF) -> None:
+        """Turn the dead-feature aux loss on for the following microbatches
+        (sae_trainer_rolling.py:2986-2998): ``dead_indices`` are the features
+        the revival controller reports dead (its ``aux_dead_mask()``, as
+        ``torch.where(mask)[0]``), ``k`` the trainer's eff_k (clipped to the
+        dead count). None or an empty set turns it off."""
+        if dead_indices is None or dead_indices.numel() == 0 or k <= 0:
+            self._aux = None
+            return
+        key = (id(dead_indices), dead_indices._version, int(k), float(coeff))
+        if self._aux is not None and getattr(self, "_aux_key", None) == key:
+            return          # the trainer refreshes its dead set every 250 steps
+        self._aux_key = key
+        dead = dead_indices.to(device=self.device, dtype=torch.int32).contiguous()
+        lo, hi = int(dead.min()), int(dead.max())
+        if lo < 0 or hi >= self.sae.n_features:
+            raise ValueError("dead feature ids must lie in [0, n_features)")
+        if dead.numel() > 1 and not bool((dead[1:] > dead[:-1]).all()):
+            raise ValueError("dead feature ids must be strictly increasing")
+        k = int(min(k, dead.numel()))
+        need = L.aux_workspace_bytes(self.max_tokens, self.sae.d_in, self.sae.n_features,
+                                     dead.numel(), k)
+        if self._aux_ws is None or self._aux_ws.numel() < need:
+            self._aux_ws = torch.empty(need, device=self.device, dtype=torch.uint8)
+        if self._x_hat is None:
+            self._x_hat = torch.empty(self.max_tokens, self.sae.d_in, device=self.device)
+        self._aux = (dead, k, float(coeff))
+
+    def _aux_struct(self) -> L.AuxConfig:
+        dead, k, coeff = self._aux
+        return L.AuxConfig(L.ptr(dead), dead.numel(), k, coeff)
 
     def _check_input(self, x: torch.Tensor) -> torch.Tensor:
         _require_cuda(x)
@@ -260,10 +306,17 @@ class FusedStep:
         cfg = self._cfg(n, accum_steps, first, lambda_l0, al_mu, target_l0)
         model = sae._model_struct(need_shadows=True)
         stream = _stream()
-        L.call("sae_b200_train_forward", ctypes.byref(model), L.ptr(x),
-               L.DTYPE_BF16 if x.dtype == torch.bfloat16 else L.DTYPE_F32, ctypes.byref(cfg),
+        dt = L.DTYPE_BF16 if x.dtype == torch.bfloat16 else L.DTYPE_F32
+        if self._aux is not None and x_hat_out is None:
+            x_hat_out = self._x_hat[:n]
+        L.call("sae_b200_train_forward", ctypes.byref(model), L.ptr(x), dt, ctypes.byref(cfg),
                L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), L.ptr(x_hat_out),
                L.ptr(self.fired), stream)
+        if self._aux is not None:
+            aux = self._aux_struct()
+            L.call("sae_b200_aux_forward", ctypes.byref(model), L.ptr(x), dt, L.ptr(x_hat_out),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, ctypes.byref(aux),
+                   L.ptr(self._aux_ws), self._aux_ws.numel(), L.ptr(self.stats), stream)
         st = self.read_stats()
         self.nnz_last = st["nnz"]
         grads = self._grads_struct()
@@ -276,6 +329,11 @@ class FusedStep:
             sae._sparse_decode_calls += 1
             L.call("sae_b200_train_backward", ctypes.byref(model), ctypes.byref(grads),
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), stream)
+        if self._aux is not None:
+            aux = self._aux_struct()
+            L.call("sae_b200_aux_backward", ctypes.byref(model), ctypes.byref(grads),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, ctypes.byref(aux),
+                   L.ptr(self._aux_ws), self._aux_ws.numel(), stream)
         self._bind_grads()
         return st
 
@@ -293,10 +351,14 @@ class FusedStep:
     def step(self, batch: torch.Tensor, *, microbatch_tokens: Optional[int] = None,
              lambda_l0: float = 0.0, al_mu: float = 0.0, target_l0: float = 0.0,
              max_norm: float = 1.0,
-             wenc_dampen: Optional[Callable[[float], float]] = None) -> dict:
+             wenc_dampen: Optional[Callable[[float], float]] = None,
+             aux_dead: Optional[torch.Tensor] = None, aux_k: int = 0,
+             aux_coeff: float = AUX_COEFF) -> dict:
         """One optimizer step over ``batch`` split into microbatches, in the
         reference loop's order; returns recon / l0 / grad_norm as floats after
-        the same single stats read-back the loop does before Adam (3064-3066)."""
+        the same single stats read-back the loop does before Adam (3064-3066).
+        ``aux_dead`` / ``aux_k``: the dead-feature aux loss (see set_aux)."""
+        self.set_aux(aux_dead, aux_k, aux_coeff)
         mb = int(microbatch_tokens or batch.shape[0])
         n = batch.shape[0]
         if n % mb != 0:
@@ -305,12 +367,14 @@ class FusedStep:
         recon = 0.0
         l0 = 0.0
         loss = 0.0
+        aux = 0.0
         for i in range(accum):
             s = self.microbatch(batch[i * mb:(i + 1) * mb], accum_steps=accum, first=(i == 0),
                                 lambda_l0=lambda_l0, al_mu=al_mu, target_l0=target_l0)
             recon += s["recon_loss"] * accum     # accum_recon_t (3057)
             l0 += s["l0"]                        # accum_l0_t (3058)
             loss += s["loss"]
+            aux += s["aux_loss"]
         self.grad_norm(max_norm)
         s = self.read_stats()
         l0_step = l0 / accum
@@ -318,7 +382,7 @@ class FusedStep:
         self.optimizer_step(factor)
         return {"recon_loss": recon / accum, "l0": l0_step, "grad_norm": s["grad_norm"],
                 "clip_coef": s["clip_coef"], "nnz": s["nnz"], "loss": loss,
-                "wenc_factor": factor}
+                "aux_loss": aux, "wenc_factor": factor}
 
     @property
     def fired_mask(self) -> torch.Tensor:

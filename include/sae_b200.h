@@ -36,7 +36,7 @@ extern "C" {
 #define SAE_ERR_UNSUPPORTED_SHAPE 2  /* shape outside what the kernels handle */
 #define SAE_ERR_MISALIGNED 3         /* pointer / stride not 16-byte aligned */
 #define SAE_ERR_WORKSPACE_TOO_SMALL 4
-#define SAE_ERR_CSR_OVERFLOW 5       /* more active pairs than csr_capacity */
+#define SAE_ERR_CSR_OVERFLOW 5       /* more CSR entries than csr_capacity */
 #define SAE_ERR_CUDA 6               /* a CUDA runtime call failed */
 #define SAE_ERR_DEVICE_TIMEOUT 7     /* a bounded device-side wait ran out */
 #define SAE_ERR_NO_DEVICE 8
@@ -71,7 +71,8 @@ typedef struct SaeB200Grads {
  * sae_trainer_rolling.py:2914-3016). */
 typedef struct SaeB200StepConfig {
   int64_t n_tokens;        /* tokens in this microbatch (rows of x) */
-  int64_t csr_capacity;    /* active (token, feature) pairs the workspace holds */
+  int64_t csr_capacity;    /* CSR entries the workspace holds: active (token, feature)
+                              pairs, plus the inactive in-band pairs when sampled */
   float lambda_l0;         /* scheduler.lambda_l0 */
   float al_mu;             /* sae_cfg.al_mu */
   float target_l0;         /* sae_cfg.target_l0 */
@@ -80,6 +81,10 @@ typedef struct SaeB200StepConfig {
   int32_t accumulate;      /* 0: gradients overwrite, 1: gradients add */
   int32_t train_decoder;   /* 0: frozen decoder (no W_dec gradient) */
   int32_t force_simt;      /* 1: CUDA-core tile GEMM even where tcgen05 applies */
+  int32_t grad_feat_gemm;  /* backward: 0 = sampled grad_feat on the active and in-band
+                              entries only (default); 1 = the dense tcgen05 grad_feat
+                              GEMM with the STE epilogue. Same gradients; forward and
+                              backward of a microbatch must use the same value. */
 } SaeB200StepConfig;
 
 /* Step statistics, written on the device; copy back with one memcpy. */
@@ -92,8 +97,12 @@ typedef struct SaeB200StepStats {
   float grad_norm;      /* pre-clip global L2 norm of all gradients   (3049)   */
   float clip_coef;      /* min(1, max_norm / (grad_norm + 1e-6))               */
   int32_t nnz;          /* active (token, feature) pairs in this microbatch    */
-  int32_t csr_overflow; /* 1 when nnz > csr_capacity: use the dense backward   */
-  int32_t reserved[7];
+  int32_t csr_overflow; /* 1 when csr_pairs > csr_capacity: use the dense backward */
+  int32_t csr_pairs;    /* entries of the backward's CSR: nnz, plus the inactive
+                           in-band pairs when the sampled backward is on      */
+  float aux_loss;       /* dead-feature aux loss (2986-2998), 0 without it;
+                           sae_b200_aux_forward also adds it to `loss`        */
+  int32_t reserved[5];
 } SaeB200StepStats;
 
 /* Adam hyper-parameters for one parameter tensor. The five tensors are, in
@@ -209,6 +218,34 @@ int sae_b200_encode_decode(const SaeB200Model* model, const void* x, int x_dtype
                            int64_t n_tokens, void* workspace, size_t workspace_bytes,
                            float* x_hat_out, int32_t* active_counts_out, uint8_t* fired,
                            void* stream);
+
+/* ------------------------------------------------ dead-feature aux loss
+ * The trainer's aux reconstruction for features silent for AUX_DEAD_THRESHOLD
+ * steps (sae_trainer_rolling.py:2986-2998; helper 252-293): per token, the
+ * top-k of relu(pre[:, dead]) reconstruct the detached residual through their
+ * decoder columns, aux = coeff * mean((x - x_hat - x_aux)^2) / accum. Ties at
+ * the k-th value go to the lower dead-list index. Call sae_b200_aux_forward
+ * after sae_b200_train_forward (same workspace, which still holds pre; x_hat:
+ * the fp32 x_hat_out of that forward) and before reading the stats;
+ * sae_b200_aux_backward after sae_b200_train_backward(_dense): it adds the aux
+ * gradients of the dead features' W_enc rows, b_enc, W_dec rows and the b_dec
+ * term. Not available on a dictionary shard (the top-k spans all shards). */
+typedef struct SaeB200AuxConfig {
+  const int32_t* dead;  /* [n_dead] device array of feature ids in [0, F), ascending */
+  int64_t n_dead;
+  int32_t k;            /* eff_k = min(aux_k, n_dead), >= 1 */
+  float coeff;          /* AUX_COEFF (1/32) */
+} SaeB200AuxConfig;
+int sae_b200_aux_workspace_bytes(int64_t max_tokens, int64_t d_in, int64_t n_features,
+                                 int64_t max_dead, int32_t k, size_t* bytes_out);
+int sae_b200_aux_forward(const SaeB200Model* model, const void* x, int x_dtype,
+                         const float* x_hat, const SaeB200StepConfig* cfg, void* workspace,
+                         size_t workspace_bytes, const SaeB200AuxConfig* aux, void* aux_workspace,
+                         size_t aux_workspace_bytes, SaeB200StepStats* stats, void* stream);
+int sae_b200_aux_backward(const SaeB200Model* model, const SaeB200Grads* grads,
+                          const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
+                          const SaeB200AuxConfig* aux, void* aux_workspace,
+                          size_t aux_workspace_bytes, void* stream);
 
 /* ------------------------------------------- dictionary-sharded wide SAE
  * One wide SAE with its dictionary split over GPUs: each rank holds features

@@ -64,6 +64,10 @@ class StepConfig:
     weight_decay: tuple = (0.0, 1e-4, 0.0, 0.0)   # 2536-2540
     adam_eps: float = 1e-8
     train_decoder: bool = True
+    # dead-feature aux loss (2986-2998): sorted dead feature ids, top-k per token
+    aux_dead: np.ndarray | None = None
+    aux_k: int = 0
+    aux_coeff: float = 1.0 / 32      # AUX_COEFF, sae_trainer_rolling.py:224
 
 
 @dataclass
@@ -100,6 +104,9 @@ class ForwardOut:
     sparsity_loss: float
     gate_grad: float
     loss: float
+    aux_loss: float = 0.0
+    aux_acts: np.ndarray | None = None   # [B, n_dead] top-k relu(pre) of the dead features
+    x_aux: np.ndarray | None = None
 
 
 @dataclass
@@ -166,8 +173,70 @@ def forward(x: np.ndarray, p: Params, cfg: StepConfig, precision: str = "fp32",
     # d sparsity / d gate[b, f]: clamp(min=0) passes the gradient where diff >= 0,
     # the mean divides by B.
     gate_grad = ((cfg.lambda_l0 + cfg.al_mu * slack) / cfg.accum_steps / B) if diff >= 0 else 0.0
-    return ForwardOut(theta, xc, pre, gate, feat, x_hat, residual, counts, recon, l0, sparsity,
-                      gate_grad, recon + sparsity)
+    fw = ForwardOut(theta, xc, pre, gate, feat, x_hat, residual, counts, recon, l0, sparsity,
+                    gate_grad, recon + sparsity)
+    if cfg.aux_dead is not None and len(cfg.aux_dead) and cfg.aux_k > 0:
+        aux_forward(fw, p, cfg, precision)
+    return fw
+
+
+def aux_select(pre_dead: np.ndarray, k: int) -> np.ndarray:
+    """relu then top-k per row (torch.topk, 2988-2991), dense [B, n_dead] with
+    the unselected entries zero. Ties go to the lower dead index."""
+    v = np.maximum(pre_dead, 0)
+    idx = np.argsort(-v, axis=1, kind="stable")[:, :k]
+    out = np.zeros_like(v)
+    np.put_along_axis(out, idx, np.take_along_axis(v, idx, axis=1), axis=1)
+    return out
+
+
+def aux_forward(fw: ForwardOut, p: Params, cfg: StepConfig, precision: str) -> None:
+    """Dead-feature aux loss (sae_trainer_rolling.py:2986-2998): the top-k
+    relu'd pre-activations of the dead features reconstruct the (detached)
+    residual through their decoder columns; aux = AUX_COEFF * mean((r - x_aux)^2)
+    / accum. In bf16 mode x_aux is the bf16 output of the autocast matmul."""
+    dead = np.asarray(cfg.aux_dead)
+    k = min(int(cfg.aux_k), len(dead))
+    acts = aux_select(fw.pre[:, dead], k)
+    if precision == "bf16":
+        x_aux = bf16((acts.astype(np.float64) @ bf16(p.W_dec[:, dead]).astype(np.float64).T)
+                     .astype(np.float32))
+        err = fw.residual.astype(np.float64) - x_aux
+    else:
+        dt = _dt(precision)
+        x_aux = (acts.astype(dt) @ p.W_dec[:, dead].astype(dt).T).astype(dt)
+        err = fw.residual.astype(dt) - x_aux
+    fw.aux_acts = acts
+    fw.x_aux = x_aux
+    fw.aux_loss = float(np.square(err.astype(np.float64)).mean() * cfg.aux_coeff / cfg.accum_steps)
+    fw.loss += fw.aux_loss
+
+
+def aux_backward(x, p: Params, fw: ForwardOut, cfg: StepConfig, precision: str):
+    """Gradients of the aux loss: g = dAux/dx_aux = -2 coeff (r - x_aux) /
+    (B d accum); dpre[:, dead] = (g W_dec_dead) on the selected entries with
+    pre > 0 (topk gather + relu backward); dW_dec[:, dead] = g^T aux_acts.
+    The residual is detached (2996), so nothing flows into the main path."""
+    B, d = x.shape
+    dead = np.asarray(cfg.aux_dead)
+    scale = 2.0 * cfg.aux_coeff / (B * d * cfg.accum_steps)
+    sel = fw.aux_acts > 0
+    if precision == "bf16":
+        a = np.float64
+        err = (fw.residual.astype(np.float64) - fw.x_aux).astype(np.float32)
+        g = bf16((-np.float32(scale) * err).astype(np.float32))
+        wd = bf16(p.W_dec[:, dead]).astype(a)                  # [d, n_dead]
+        d_acts = bf16((g.astype(a) @ wd).astype(np.float32))   # [B, n_dead]
+        dpre_dead = np.where(sel, d_acts, 0.0).astype(np.float32)
+        dW_dead = g.astype(a).T @ bf16(fw.aux_acts).astype(a)  # [d, n_dead]
+    else:
+        dt = _dt(precision)
+        err = fw.residual.astype(dt) - fw.x_aux
+        g = (-scale * err).astype(dt)
+        d_acts = g @ p.W_dec[:, dead].astype(dt)
+        dpre_dead = np.where(sel, d_acts, 0.0).astype(dt)
+        dW_dead = g.T @ fw.aux_acts.astype(dt)
+    return dpre_dead, dW_dead
 
 
 # ----------------------------------------------------------------- backward
@@ -210,6 +279,18 @@ def backward(x: np.ndarray, p: Params, fw: ForwardOut, cfg: StepConfig,
         else:
             gb_dec_enc = -(db_enc @ We)
         g_logthr = -(thr_sum / (2 * eps)) * fw.theta.astype(a)
+        if fw.aux_acts is not None:
+            dead = np.asarray(cfg.aux_dead)
+            dpre_dead, dW_dead = aux_backward(x, p, fw, cfg, precision)
+            dpre_aux = np.zeros_like(dpre)
+            dpre_aux[:, dead] = dpre_dead
+            db_aux = dpre_aux.astype(a).sum(axis=0)
+            db_enc = db_enc + db_aux
+            dW_enc = dW_enc + dpre_aux.astype(a).T @ fw.xc.astype(a)
+            dW_dec = dW_dec.copy()
+            dW_dec[:, dead] += dW_dead
+            gb_dec_enc = -(db_enc @ We)
+            dpre = dpre + dpre_aux
         out = Grads(dW_enc.astype(np.float32), db_enc.astype(np.float32),
                     dW_dec.astype(np.float32), (gb_dec + gb_dec_enc).astype(np.float32),
                     g_logthr.astype(np.float32))
@@ -226,6 +307,13 @@ def backward(x: np.ndarray, p: Params, fw: ForwardOut, cfg: StepConfig,
         in_band = np.abs(fw.pre - fw.theta) < eps
         thr_sum = np.where(in_band, comb, 0.0).sum(axis=0)
         dpre = grad_feat * fw.gate
+        if fw.aux_acts is not None:
+            dead = np.asarray(cfg.aux_dead)
+            dpre_dead, dW_dead = aux_backward(x, p, fw, cfg, precision)
+            dpre = dpre.copy()
+            dpre[:, dead] += dpre_dead
+            dW_dec = dW_dec.copy()
+            dW_dec[:, dead] += dW_dead
         db_enc = dpre.sum(axis=0)
         dW_enc = dpre.T @ fw.xc
         gb_dec = gb_dec - db_enc @ p.W_enc.astype(dt)

@@ -39,8 +39,10 @@ def ref_params(sae):
             "b_dec": sae.b_dec, "log_threshold": sae.log_threshold}
 
 
-def run_reference_step(sae, xs, *, lam, mu, target, lr, wenc_factor=1.0):
-    """The trainer's loop body on CPU (no autocast), microbatches ``xs``."""
+def run_reference_step(sae, xs, *, lam, mu, target, lr, wenc_factor=1.0, dead=None, eff_k=0):
+    """The trainer's loop body on CPU (no autocast), microbatches ``xs``; with
+    ``dead`` (sorted feature ids) and ``eff_k``, the dead-feature aux loss of
+    sae_trainer_rolling.py:2986-2998 is added to each microbatch's loss."""
     optimizer = torch.optim.Adam(
         [{"params": sae.W_enc.parameters(), "weight_decay": 0},
          {"params": sae.W_dec.parameters(), "weight_decay": 1e-4},
@@ -49,7 +51,7 @@ def run_reference_step(sae, xs, *, lam, mu, target, lr, wenc_factor=1.0):
         lr=lr, betas=(0.9, 0.999))
     accum = len(xs)
     optimizer.zero_grad()
-    out = {"recon": [], "l0": [], "sparsity": [], "pre": [], "gate": [], "x_hat": []}
+    out = {"recon": [], "l0": [], "sparsity": [], "pre": [], "gate": [], "x_hat": [], "aux": []}
     for acts_mb in xs:
         pre = sae.encode_pre(acts_mb)
         feat_acts, gate = sae.jumprelu_with_gate(pre)
@@ -61,6 +63,17 @@ def run_reference_step(sae, xs, *, lam, mu, target, lr, wenc_factor=1.0):
         slack = (l0_mb - target).clamp(min=0.0)
         sparsity_loss = (lam * slack + 0.5 * mu * slack * slack) / accum
         loss = recon_loss + sparsity_loss
+        if dead is not None:
+            dead_t = torch.as_tensor(dead, dtype=torch.long)
+            pre_dead = pre[:, dead_t].relu()
+            topk_vals, topk_idx = pre_dead.topk(eff_k, dim=-1)
+            aux_acts = torch.zeros_like(pre_dead)
+            aux_acts.scatter_(-1, topk_idx, topk_vals)
+            w_dec_dead = sae.W_dec.weight.t()[dead_t]
+            x_aux = aux_acts @ w_dec_dead
+            aux_loss = ((residual.detach() - x_aux).pow(2).mean() * T.AUX_COEFF) / accum
+            loss = loss + aux_loss
+            out["aux"].append(float(aux_loss))
         loss.backward()
         out["recon"].append(float(recon_loss))
         out["l0"].append(float(l0_mb))
@@ -83,7 +96,7 @@ def run_reference_step(sae, xs, *, lam, mu, target, lr, wenc_factor=1.0):
 
 
 def make_case(name, *, d, F, xs, dtype, lam, mu, target, eps, lr, log_thr=None, b_dec=None,
-              wenc_factor=1.0, seed=0, keep_dense=True):
+              wenc_factor=1.0, seed=0, keep_dense=True, dead=None, eff_k=0):
     sae = T._make_sae(d, F, seed=seed).to(dtype)
     sae.ste_bandwidth = eps
     with torch.no_grad():
@@ -94,11 +107,14 @@ def make_case(name, *, d, F, xs, dtype, lam, mu, target, eps, lr, log_thr=None, 
     before = {k: v.detach().clone().numpy() for k, v in ref_params(sae).items()}
     xs_t = [torch.as_tensor(x, dtype=dtype) for x in xs]
     out, grads, gn, after = run_reference_step(sae, xs_t, lam=lam, mu=mu, target=target, lr=lr,
-                                               wenc_factor=wenc_factor)
+                                               wenc_factor=wenc_factor, dead=dead, eff_k=eff_k)
     rec = {"d": d, "F": F, "lam": lam, "mu": mu, "target": target, "eps": eps, "lr": lr,
            "wenc_factor": wenc_factor, "n_micro": len(xs), "grad_norm": gn,
            "recon": np.array(out["recon"]), "l0": np.array(out["l0"]),
            "sparsity": np.array(out["sparsity"])}
+    if dead is not None:
+        rec.update(dead=np.asarray(dead, np.int64), eff_k=eff_k, aux=np.array(out["aux"]),
+                   aux_coeff=T.AUX_COEFF)
     if keep_dense:
         for i, x in enumerate(xs):
             rec[f"x{i}"] = np.asarray(x)
@@ -160,7 +176,23 @@ def main():
     make_case("cfg1_f32", d=256, F=8192, xs=[xs], dtype=torch.float32, lam=1e-3, mu=1e-2,
               target=50.0, eps=0.2, lr=1e-4, log_thr=np.full(8192, math.log(0.05)),
               b_dec=xs.mean(0), seed=0, keep_dense=False)
-    # 6. known-answer gate (tests/test_sae_model.py:41-55).
+    # 6. dead-feature aux loss (2986-2998): float64 and a tile-aligned float32 case,
+    #    a sorted dead set with both positive and negative pre-activations.
+    g = torch.Generator().manual_seed(77)
+    x = torch.randn(64, 16, generator=g, dtype=torch.float64).numpy()
+    dead = np.sort(np.random.default_rng(5).choice(32, 13, replace=False))
+    make_case("aux_f64", d=16, F=32, xs=[x], dtype=torch.float64, lam=0.37, mu=0.05, target=4.0,
+              eps=0.2, lr=1e-3, log_thr=np.linspace(-1.5, 0.0, 32), seed=1234, dead=dead,
+              eff_k=4)
+    make_case("aux_f64_accum2", d=16, F=32, xs=list(np.split(x, 2)), dtype=torch.float64,
+              lam=0.37, mu=0.05, target=4.0, eps=0.2, lr=1e-3,
+              log_thr=np.linspace(-1.5, 0.0, 32), seed=1234, dead=dead, eff_k=4)
+    xs = superposition_batch(256, 128, 512, 8, math.log(8.0), 0.3, seed=13)
+    dead = np.sort(np.random.default_rng(6).choice(512, 160, replace=False))
+    make_case("aux_f32_tiles", d=128, F=512, xs=[xs], dtype=torch.float32, lam=1e-3, mu=1e-2,
+              target=8.0, eps=0.2, lr=1e-4, log_thr=np.full(512, math.log(1.2)),
+              b_dec=xs.mean(0), seed=0, dead=dead, eff_k=25)
+    # 7. known-answer gate (tests/test_sae_model.py:41-55).
     sae = T._make_sae(4, 4, seed=0)
     with torch.no_grad():
         sae.log_threshold.fill_(math.log(0.1))
@@ -169,7 +201,7 @@ def main():
     np.savez_compressed(HERE / "gate_known_answer.npz", pre=pre.numpy(),
                         log_threshold=sae.log_threshold.detach().numpy(),
                         feat=feat.detach().numpy(), gate=gate.detach().numpy())
-    # 7. reference init, bit for bit (_make_sae seeds, nn.Linear draws, orthogonal_).
+    # 8. reference init, bit for bit (_make_sae seeds, nn.Linear draws, orthogonal_).
     for (d, F, s) in ((4, 8, 0), (16, 32, 1234), (24, 160, 3)):
         sae = T._make_sae(d, F, seed=s)
         np.savez_compressed(HERE / f"init_d{d}_F{F}_s{s}.npz",

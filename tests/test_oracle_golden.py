@@ -19,10 +19,13 @@ def _params(g, tag="p0"):
 
 def _cfg(g):
     lr = float(g["lr"])
+    aux = {}
+    if "dead" in g:
+        aux = dict(aux_dead=g["dead"], aux_k=int(g["eff_k"]), aux_coeff=float(g["aux_coeff"]))
     return O.StepConfig(lambda_l0=float(g["lam"]), al_mu=float(g["mu"]),
                         target_l0=float(g["target"]), ste_bandwidth=float(g["eps"]),
                         accum_steps=int(g["n_micro"]), lr=(lr,) * 4,
-                        wenc_factor=float(g["wenc_factor"]))
+                        wenc_factor=float(g["wenc_factor"]), **aux)
 
 
 def _rel(a, b):
@@ -33,7 +36,10 @@ def _rel(a, b):
 
 CASES = [("ste_f64", "fp64", 1e-10), ("ste_f64_accum2", "fp64", 1e-10),
          ("ste_f64_accum4", "fp64", 1e-10), ("super_f32_odd", "fp32", 2e-5),
-         ("super_f32_tiles", "fp32", 2e-5)]
+         ("super_f32_tiles", "fp32", 2e-5),
+         # with the dead-feature aux loss (2986-2998)
+         ("aux_f64", "fp64", 1e-10), ("aux_f64_accum2", "fp64", 1e-10),
+         ("aux_f32_tiles", "fp32", 2e-5)]
 
 
 @pytest.mark.parametrize("name,precision,tol", CASES)
@@ -47,6 +53,8 @@ def test_oracle_step_matches_reference(name, precision, tol):
 
     for i, fw in enumerate(res.fw):
         assert fw.l0 == pytest.approx(float(g["l0"][i]), abs=1e-9)
+        if "aux" in g:
+            assert fw.aux_loss == pytest.approx(float(g["aux"][i]), rel=tol * 10)
         assert fw.recon_loss == pytest.approx(float(g["recon"][i]), rel=tol * 10)
         assert _rel(fw.pre, g[f"pre{i}"]) < tol
         assert _rel(fw.x_hat, g[f"x_hat{i}"]) < tol
@@ -57,6 +65,24 @@ def test_oracle_step_matches_reference(name, precision, tol):
     # Adam (L2 decay, per-group), clip, dampening, renormalisations.
     for k in O.PARAM_NAMES:
         assert _rel(getattr(res.params, k), g[f"p1_{k}"]) < tol * 10, k
+
+
+def test_aux_fixtures_exercise_the_aux_path():
+    """Some dead features are selected with positive values (else the aux
+    gradient is vacuous), and the aux term changes the gradients."""
+    for name in ("aux_f64", "aux_f32_tiles"):
+        g = load_golden(name)
+        cfg = _cfg(g)
+        fw = O.forward(g["x0"], _params(g), cfg, "fp64" if "f64" in name else "fp32")
+        assert (fw.aux_acts > 0).sum() > 50
+        assert fw.aux_loss > 0
+    g = load_golden("aux_f64")
+    cfg = _cfg(g)
+    cfg.aux_dead = None
+    fw = O.forward(g["x0"], _params(g), cfg, "fp64")
+    plain = O.backward(g["x0"], _params(g), fw, cfg, "fp64")
+    assert _rel(plain.W_enc, g["grad_W_enc"]) > 1e-6
+    assert _rel(plain.W_dec, g["grad_W_dec"]) > 1e-6
 
 
 def test_threshold_band_is_populated():
