@@ -83,9 +83,9 @@ DeviceInfo device_info() {
 
 // ------------------------------------------------------------ workspace
 struct Layout {
-  size_t theta, xc, pre, mask, tile_cnt, tile_band, col_tot, col_act, col_offs, go, tok_sqerr,
+  size_t theta, xc, pre, sbits, mask, tile_cnt, tile_band, col_tot, col_act, col_offs, go, tok_sqerr,
       tok_cnt, gosum_part, thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part,
-      counters, total;
+      order_k0, order_k1, order_v0, order_v1, order_tmp, order_tmp_bytes, counters, total;
 };
 
 // Row pitch (tokens) of the feature-major pre-activations: whole 64-token
@@ -95,6 +95,13 @@ inline int64_t pre_pitch(int64_t B) {
   int64_t p = (B + 63) / 64 * 64 + 64;
   if ((p & (p - 1)) == 0) p += 64;
   return p;
+}
+
+// Bits of a per-token active count (at most F).
+int count_key_bits(int64_t F) {
+  int b = 1;
+  while ((int64_t(1) << b) <= F) ++b;
+  return b;
 }
 
 Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
@@ -111,6 +118,7 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   L.theta = take(F * 4);
   L.xc = take(B * d * 2);
   L.pre = take(static_cast<size_t>(F) * pre_pitch(B) * 2);   // feature-major [F, ldp]
+  L.sbits = take(static_cast<size_t>(F) * (pre_pitch(B) / 32) * 4);
   L.mask = take(B * W * 4);
   L.tile_cnt = take(nT * F * 4);
   L.tile_band = take(nT * F * 4);
@@ -128,6 +136,19 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   L.csr_tok = take(cap * 4);
   L.csr_val = take(cap * 4);
   L.sumsq_part = take(NORM_GRID * 4);
+  // decode order: tokens sorted by active count, heaviest first
+  L.order_k0 = take(B * 4);
+  L.order_k1 = take(B * 4);
+  L.order_v0 = take(B * 4);
+  L.order_v1 = take(B * 4);
+  size_t sort_bytes = 0;
+  cub::DeviceRadixSort::SortPairsDescending(nullptr, sort_bytes, static_cast<int*>(nullptr),
+                                            static_cast<int*>(nullptr),
+                                            static_cast<int*>(nullptr),
+                                            static_cast<int*>(nullptr), static_cast<int>(B), 0,
+                                            count_key_bits(F));
+  L.order_tmp_bytes = sort_bytes;
+  L.order_tmp = take(sort_bytes);
   L.counters = take(256);
   L.total = off;
   return L;
@@ -137,6 +158,7 @@ struct Ws {
   float* theta;
   bf16* xc;
   bf16* pre;
+  uint32_t* sbits;
   uint32_t* mask;
   int* tile_cnt;
   int* tile_band;
@@ -154,6 +176,9 @@ struct Ws {
   int* csr_tok;
   uint32_t* csr_val;
   float* sumsq_part;
+  int *order_k0, *order_k1, *order_v0, *order_v1;
+  void* order_tmp;
+  size_t order_tmp_bytes;
   int* counters;
 };
 
@@ -163,6 +188,7 @@ Ws carve(void* base, const Layout& L) {
   w.theta = reinterpret_cast<float*>(at(L.theta));
   w.xc = reinterpret_cast<bf16*>(at(L.xc));
   w.pre = reinterpret_cast<bf16*>(at(L.pre));
+  w.sbits = reinterpret_cast<uint32_t*>(at(L.sbits));
   w.mask = reinterpret_cast<uint32_t*>(at(L.mask));
   w.tile_cnt = reinterpret_cast<int*>(at(L.tile_cnt));
   w.tile_band = reinterpret_cast<int*>(at(L.tile_band));
@@ -180,6 +206,12 @@ Ws carve(void* base, const Layout& L) {
   w.csr_tok = reinterpret_cast<int*>(at(L.csr_tok));
   w.csr_val = reinterpret_cast<uint32_t*>(at(L.csr_val));
   w.sumsq_part = reinterpret_cast<float*>(at(L.sumsq_part));
+  w.order_k0 = reinterpret_cast<int*>(at(L.order_k0));
+  w.order_k1 = reinterpret_cast<int*>(at(L.order_k1));
+  w.order_v0 = reinterpret_cast<int*>(at(L.order_v0));
+  w.order_v1 = reinterpret_cast<int*>(at(L.order_v1));
+  w.order_tmp = at(L.order_tmp);
+  w.order_tmp_bytes = L.order_tmp_bytes;
   w.counters = reinterpret_cast<int*>(at(L.counters));
   return w;
 }
@@ -512,6 +544,7 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
     e.mask = w.mask;
     e.tile_cnt = w.tile_cnt;
     e.tile_band = sampled ? w.tile_band : nullptr;
+    e.sbits = sampled ? w.sbits : nullptr;
     e.eps = cfg->ste_bandwidth;
     e.n_tokens = static_cast<int>(B);
     e.n_features = static_cast<int>(F);
@@ -542,12 +575,24 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
   const int V = vec_threads(d);
   const int G = std::min(4, std::max(1, 512 / V));   // row groups per token
   const size_t dyn = static_cast<size_t>(G - 1) * V * 2 * sizeof(float4);
+  // Tokens' active counts are heavy-tailed: blocks take tokens in order of
+  // decreasing count, round robin (a fixed, data-determined assignment, so the
+  // per-block go sums stay deterministic).
+  token_count_kernel<<<grid_for(B * 32, 256), 256, 0, stream>>>(w.mask, B, c.mask_words,
+                                                               w.order_k0, w.order_v0);
+  SAE_TRY(check_launch("token_count_kernel"));
+  size_t tmp_bytes = w.order_tmp_bytes;
+  if (cub::DeviceRadixSort::SortPairsDescending(w.order_tmp, tmp_bytes, w.order_k0, w.order_k1,
+                                                w.order_v0, w.order_v1, static_cast<int>(B), 0,
+                                                count_key_bits(F), stream) != cudaSuccess)
+    return fail(SAE_ERR_CUDA, "token order sort failed");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
 #define SAE_DECODE(XT, GG)                                                                   \
   decode_kernel<XT, GG><<<DECODE_GRID, V * GG, dyn, stream>>>(                              \
       w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,             \
       static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), c.mask_words, \
       static_cast<int>(pre_pitch(B)), c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt,  \
-      w.gosum_part, partial)
+      w.gosum_part, partial, w.order_v1)
   timer_begin(SAE_KERNEL_DECODE, stream);
   if (x_dtype == SAE_DTYPE_BF16) {
     if (G >= 4) SAE_DECODE(bf16, 4);
@@ -914,25 +959,31 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
   // STE epilogue, then the CSR weight-gradient gather. Same gradients.
   if (dense_scratch == nullptr && cfg->grad_feat_gemm == 0) {
     // 1. CSR of the active and in-band entries, feature-major, token order
-    csr_fill_kernel<<<grid_for(F * 32, 256, 16), 256, 0, stream>>>(
-        w.pre, w.theta, w.col_offs, static_cast<int>(F), B, static_cast<int>(pre_pitch(B)),
-        cfg->ste_bandwidth, stats, w.csr_tok, w.csr_val);
+    csr_fill_kernel<<<grid_for(F * 8, 256, 8), 256, 0, stream>>>(
+        w.pre, w.sbits, w.theta, w.col_offs, static_cast<int>(F), B,
+        static_cast<int>(pre_pitch(B)), cfg->ste_bandwidth, stats, w.csr_tok, w.csr_val);
     SAE_TRY(check_launch("csr_fill_kernel"));
-    // 2. sampled grad_feat + STE + weight gradients, one feature at a time
-    const int G = std::max(1, std::min(2, 512 / thr));
-    const size_t dyn = static_cast<size_t>(G - 1) * thr * 4 * sizeof(float4);
-    const int grid = device_info().sm_count * std::max(1, 2048 / (thr * G));
+    // 2. sampled grad_feat + STE + weight gradients, one feature per block
+    const int per_sm = thr <= 192 ? 4 : (thr <= 256 ? 2 : 1);
+    const int grid = device_info().sm_count * per_sm * 2;
     timer_begin(SAE_KERNEL_GRAD_GEMM, stream);
-#define SAE_SAMPLED(GG, MT)                                                                    \
-  sampled_backward_kernel<GG, MT><<<grid, thr * GG, dyn, stream>>>(                           \
+#define SAE_SAMPLED(CC, MT, MB)                                                                \
+  sampled_backward_kernel<CC, MT, MB><<<grid, thr, 0, stream>>>(                              \
       w.col_offs, w.csr_tok, w.csr_val, w.go, w.xc,                                           \
       static_cast<const bf16*>(model->W_dec_bf16), w.theta, static_cast<int>(F),               \
       static_cast<int>(B), static_cast<int>(d), cfg->ste_bandwidth, acc, g_wdec, grads->W_enc,  \
-      grads->log_threshold,                                                                    \
-      grads->b_enc, w.db_enc, w.counters, stats)
-    if (G >= 2) SAE_SAMPLED(2, 512);
-    else if (thr <= 512) SAE_SAMPLED(1, 512);
-    else SAE_SAMPLED(1, 1024);
+      grads->log_threshold, grads->b_enc, w.db_enc, w.counters, stats)
+#define SAE_SAMPLED_C(CC)                                                                      \
+  if (thr <= 192) SAE_SAMPLED(CC, 192, 3);                                                     \
+  else if (thr <= 256) SAE_SAMPLED(CC, 256, 2);                                                \
+  else if (thr <= 512) SAE_SAMPLED(CC, 512, 1);                                                \
+  else SAE_SAMPLED(CC, 1024, 1);
+    if (thr <= 192) {
+      SAE_SAMPLED(2, 192, 4);
+    } else {
+      SAE_SAMPLED_C(4)
+    }
+#undef SAE_SAMPLED_C
 #undef SAE_SAMPLED
     const int rc = check_launch("sampled_backward_kernel");
     timer_end(SAE_KERNEL_GRAD_GEMM, stream);

@@ -150,7 +150,13 @@ struct EncodeEpi {
   bf16* pre;          // [F, ldp]
   uint32_t* mask;
   int* tile_cnt;
-  int* tile_band;     // optional: inactive entries inside the STE band, |pre - theta| < eps
+  // Sampled backward (optional): its entries are the (token, feature) pairs with
+  // pre - theta > -eps, i.e. active (pre > theta) or inside the STE band
+  // |pre - theta| < eps. tile_band counts them per half tile; sbits
+  // [ldp / 32, F] holds one bit each (word w of feature f: tokens 32w..32w+31),
+  // so that the 32 features of an epilogue warp store one coalesced line.
+  int* tile_band;
+  uint32_t* sbits;
   float eps;
   int n_tokens, n_features, mask_words, ldp;
   // per-thread tile state
@@ -172,7 +178,10 @@ struct EncodeEpi {
     bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
     word = (m_tile * TILE_M + q * 32) >> 5;
   }
-  __device__ __forceinline__ void begin_half(int) { cnt = 0; bcnt = 0; }
+  __device__ __forceinline__ void begin_half(int) {
+    cnt = 0;
+    bcnt = 0;
+  }
   __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
     const int t0 = n0 + c;
     const int nj = row_ok ? min(32, n_tokens - t0) : 0;
@@ -182,7 +191,8 @@ struct EncodeEpi {
       const float2 s = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), make_float2(bias, bias));
       pk[i] = pack_bf2(s.x, s.y);
     }
-    uint32_t myword = 0;
+    uint32_t myword = 0, sword = 0;
+    const float neg_eps = -eps;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float p = (j & 1) ? bf_hi(pk[j >> 1]) : bf_lo(pk[j >> 1]);
@@ -190,7 +200,12 @@ struct EncodeEpi {
       const uint32_t bal = __ballot_sync(0xffffffffu, act);
       if (lane == j) myword = bal;
       cnt += act ? 1 : 0;
-      bcnt += ((j < nj) && !act && fabsf(__fsub_rn(p, th)) < eps) ? 1 : 0;
+      const bool ent = (j < nj) && __fsub_rn(p, th) > neg_eps;   // active or in band
+      sword |= ent ? (1u << j) : 0u;
+    }
+    if (sbits != nullptr) {
+      bcnt += __popc(sword);
+      if (nj > 0) sbits[static_cast<size_t>(t0 >> 5) * n_features + f] = sword;
     }
     if (aux != nullptr) {
       // tokens past n_tokens are clipped by the TMA store
@@ -386,8 +401,9 @@ struct GradEpi {
 // ------------------------------------------------------------------- scans
 // Per feature: exclusive prefix of the per-tile active counts (in place),
 // the feature's total, and the OR-accumulated fired flag.
-// With tile_band (sampled backward): col_tot counts the feature's CSR entries
-// -- active plus inactive in-band -- and col_act its active entries.
+// With tile_band (sampled backward: the per-half counts of its entries, active
+// or in band): col_tot counts the feature's CSR entries and col_act its
+// active entries.
 __global__ void scan_columns_kernel(int* __restrict__ tile_cnt, int* __restrict__ col_tot,
                                     uint8_t* __restrict__ fired, int n_tiles, int n_features,
                                     const int* __restrict__ tile_band = nullptr,
@@ -395,14 +411,37 @@ __global__ void scan_columns_kernel(int* __restrict__ tile_cnt, int* __restrict_
   for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < n_features;
        f += gridDim.x * blockDim.x) {
     int run = 0, band = 0;
-    for (int t = 0; t < n_tiles; ++t) {
-      const size_t i = static_cast<size_t>(t) * n_features + f;
-      const int v = tile_cnt[i];
-      tile_cnt[i] = run;
-      run += v;
-      if (tile_band != nullptr) band += tile_band[i];
+    if (tile_band != nullptr) {
+      // sampled backward: totals only (8 independent loads in flight)
+      int t = 0;
+      for (; t + 8 <= n_tiles; t += 8) {
+        int a[8], b[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const size_t i = static_cast<size_t>(t + u) * n_features + f;
+          a[u] = tile_cnt[i];
+          b[u] = tile_band[i];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          run += a[u];
+          band += b[u];
+        }
+      }
+      for (; t < n_tiles; ++t) {
+        const size_t i = static_cast<size_t>(t) * n_features + f;
+        run += tile_cnt[i];
+        band += tile_band[i];
+      }
+    } else {
+      for (int t = 0; t < n_tiles; ++t) {
+        const size_t i = static_cast<size_t>(t) * n_features + f;
+        const int v = tile_cnt[i];
+        tile_cnt[i] = run;
+        run += v;
+      }
     }
-    col_tot[f] = run + band;
+    col_tot[f] = tile_band != nullptr ? band : run;
     if (col_act != nullptr) col_act[f] = run;
     if (fired != nullptr && run > 0) fired[f] = 1;
   }
@@ -447,66 +486,81 @@ __global__ void __launch_bounds__(1024)
 // feature-major CSR of exactly those entries and computes each one as a dot
 // product of two bf16 rows.
 //
-// CSR fill: one warp per feature row of the feature-major pre-activations;
-// lane l covers tokens [t0 + 8l, t0 + 8l + 8) of each 256-token window, and a
-// warp scan places the entries in token order after the feature's offset.
+// CSR fill: the encoder epilogue left one bit per (feature, token) entry in
+// sbits [ldp / 32, F]. A block of 8 warps takes 32 consecutive features; per
+// 1024-token window it loads the [32 words x 32 features] bit tile with
+// coalesced rows, and warp w then walks features 4w..4w+3 of it: lane l holds
+// word l of the window, a warp scan places the entries in token order after the
+// feature's running offset, and each entry's bf16 pre-activation is read back.
 // Entry value: low 16 bits bf16 pre, bit 16 active (pre > theta), bit 17 in
 // band (|pre - theta| < eps).
 constexpr uint32_t CSR_ACTIVE = 1u << 16;
 constexpr uint32_t CSR_BAND = 1u << 17;
 
 __global__ void __launch_bounds__(256)
-    csr_fill_kernel(const bf16* __restrict__ pre, const float* __restrict__ theta,
-                    const int* __restrict__ col_offs, int n_features, int64_t n_tokens, int ldp,
-                    float eps, const SaeB200StepStats* stats, int* __restrict__ csr_tok,
+    csr_fill_kernel(const bf16* __restrict__ pre, const uint32_t* __restrict__ sbits,
+                    const float* __restrict__ theta, const int* __restrict__ col_offs,
+                    int n_features, int64_t n_tokens, int ldp, float eps,
+                    const SaeB200StepStats* stats, int* __restrict__ csr_tok,
                     uint32_t* __restrict__ csr_val) {
   if (stats->csr_overflow) return;
-  const int lane = threadIdx.x & 31;
-  const int warps = (gridDim.x * blockDim.x) >> 5;
-  for (int f = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; f < n_features; f += warps) {
-    const float th = theta[f];
-    const uint4* row = reinterpret_cast<const uint4*>(pre + static_cast<size_t>(f) * ldp);
-    int pos = col_offs[f];
-    const int end = col_offs[f + 1];   // the encoder counted exactly these entries
-    for (int64_t t0 = 0; t0 < n_tokens; t0 += 256) {
-      const int64_t tl = t0 + 8 * lane;
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (tl < n_tokens) u = __ldg(row + (tl >> 3));   // ldp % 64 == 0: the 8 stay in the row
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-      uint32_t flags = 0;   // 2 bits per token
+  __shared__ uint32_t tile[32][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n_words = static_cast<int>((n_tokens + 31) >> 5);
+  const uint16_t* pre16 = reinterpret_cast<const uint16_t*>(pre);
+  for (int f0 = blockIdx.x * 32; f0 < n_features; f0 += gridDim.x * 32) {
+    int pos[4], end[4];
+    float th[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float p = (j & 1) ? bf_hi(w[j >> 1]) : bf_lo(w[j >> 1]);
-        const bool ok = tl + j < n_tokens;
-        const uint32_t a = (ok && p > th) ? 1u : 0u;
-        const uint32_t bnd = (ok && fabsf(__fsub_rn(p, th)) < eps) ? 2u : 0u;
-        flags |= (a | bnd) << (2 * j);
+    for (int i = 0; i < 4; ++i) {
+      const int f = f0 + warp * 4 + i;
+      const bool ok = f < n_features;
+      pos[i] = ok ? col_offs[f] : 0;
+      end[i] = ok ? col_offs[f + 1] : 0;   // the encoder counted exactly these entries
+      th[i] = ok ? theta[f] : 0.f;
+    }
+    for (int w0 = 0; w0 < n_words; w0 += 32) {
+      __syncthreads();
+#pragma unroll
+      for (int r = warp; r < 32; r += 8) {
+        const int wi = w0 + r, f = f0 + lane;
+        tile[r][lane] = (wi < n_words && f < n_features)
+                            ? sbits[static_cast<size_t>(wi) * n_features + f] : 0u;
       }
-      int mine = 0;
+      __syncthreads();
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mine += ((flags >> (2 * j)) & 3u) ? 1 : 0;
-      int incl = mine;
+      for (int i = 0; i < 4; ++i) {
+        const int fl = warp * 4 + i;
+        const int f = f0 + fl;
+        if (f >= n_features) continue;   // uniform per warp
+        uint32_t bits = tile[lane][fl];
+        const int mine = __popc(bits);
+        int incl = mine;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const int tot = __shfl_sync(0xffffffffu, incl, 31);
-      if (mine) {
-        int q = pos + incl - mine;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t fl = (flags >> (2 * j)) & 3u;
-          if (fl) {
-            if (q < end) {
-              csr_tok[q] = static_cast<int>(tl + j);
-              csr_val[q] = ((w[j >> 1] >> (16 * (j & 1))) & 0xFFFFu) | (fl << 16);
-            }
-            ++q;
-          }
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
         }
+        const int tot = __shfl_sync(0xffffffffu, incl, 31);
+        int q = pos[i] + incl - mine;
+        const uint16_t* prow = pre16 + static_cast<size_t>(f) * ldp;
+        const int tbase = (w0 + lane) * 32;
+        while (bits) {
+          const int b = __ffs(bits) - 1;
+          bits &= bits - 1;
+          const int t = tbase + b;
+          const uint32_t u = prow[t];
+          const float p = __uint_as_float(u << 16);
+          const uint32_t fl2 = (p > th[i] ? CSR_ACTIVE : 0u) |
+                               (fabsf(__fsub_rn(p, th[i])) < eps ? CSR_BAND : 0u);
+          if (q < end[i]) {
+            csr_tok[q] = t;
+            csr_val[q] = u | fl2;
+          }
+          ++q;
+        }
+        pos[i] += tot;
       }
-      pos += tot;
     }
   }
 }
@@ -537,18 +591,58 @@ __device__ __forceinline__ float warp_sum8(float (&p)[8], int lane) {
   return q;
 }
 
-// Per feature (blocks take features from a global counter): for its CSR
-// entries, in chunks of 8, grad_feat = bf16(go[t] . W_dec[f]) (fp32
-// accumulation, the bf16 GEMM output of 643), then
+// Sum over the 32 lanes of each of 4 values: lane l with (l & 7) == 0 holds
+// the total of value ((l >> 3) & 3).
+__device__ __forceinline__ float warp_sum4(float (&p)[4], int lane) {
+  float q2[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const bool hi = lane & 16;
+    const float keep = hi ? p[k + 2] : p[k];
+    const float send = hi ? p[k] : p[k + 2];
+    q2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  const bool hi = lane & 8;
+  float q = (hi ? q2[1] : q2[0]) + __shfl_xor_sync(0xffffffffu, hi ? q2[0] : q2[1], 8);
+  q += __shfl_xor_sync(0xffffffffu, q, 4);
+  q += __shfl_xor_sync(0xffffffffu, q, 2);
+  q += __shfl_xor_sync(0xffffffffu, q, 1);
+  return q;
+}
+
+// Two values: lane l with (l & 15) == 0 holds the total of value (l >> 4) & 1.
+__device__ __forceinline__ float warp_sum2(float (&p)[2], int lane) {
+  const bool hi = lane & 16;
+  float q = (hi ? p[1] : p[0]) + __shfl_xor_sync(0xffffffffu, hi ? p[0] : p[1], 16);
+  q += __shfl_xor_sync(0xffffffffu, q, 8);
+  q += __shfl_xor_sync(0xffffffffu, q, 4);
+  q += __shfl_xor_sync(0xffffffffu, q, 2);
+  q += __shfl_xor_sync(0xffffffffu, q, 1);
+  return q;
+}
+
+template <int C>
+__device__ __forceinline__ float warp_sum_c(float (&p)[C], int lane) {
+  if constexpr (C == 8) return warp_sum8(p, lane);
+  else if constexpr (C == 4) return warp_sum4(p, lane);
+  else return warp_sum2(p, lane);
+}
+
+// Per feature (blocks take features from a global counter; one feature per
+// block of d/8 threads, blocks independent): its CSR entries in chunks of C,
+//   grad_feat = bf16(go[t] . W_dec[f])   (fp32 accumulation; the bf16 GEMM
+//                                          output of 643)
 //   active:  dpre = grad_feat; db_enc += dpre; dW_enc[f] += dpre * xc[t];
 //            dW_dec[f] += pre * go[t]
 //   in band: STE sum += pre * grad_feat + gate_grad
-// and at the end the threshold gradient -(sum / 2 eps) * theta. A block is G
-// row groups of V = d/8 threads; group g takes chunks g, g + G, ... and the
-// group sums are combined in a fixed order: the result does not depend on
-// timing.
-template <int G, int MAX_THREADS>
-__global__ void __launch_bounds__(MAX_THREADS)
+// and at the end the threshold gradient -(sum / 2 eps) * theta. The go and xc
+// rows of a chunk are all requested before the first is used. The C dot
+// products are reduced by a warp butterfly and one barrier per chunk: every
+// thread adds the warps' partials (double-buffered by chunk parity) in the
+// same order, so all threads hold the same grad_feat and the result does not
+// depend on timing.
+template <int C, int MAX_THREADS, int MIN_BLOCKS>
+__global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
     sampled_backward_kernel(const int* __restrict__ col_offs, const int* __restrict__ csr_tok,
                             const uint32_t* __restrict__ csr_val, const bf16* __restrict__ go,
                             const bf16* __restrict__ xc, const bf16* __restrict__ w_dec,
@@ -559,23 +653,16 @@ __global__ void __launch_bounds__(MAX_THREADS)
                             int* __restrict__ counter, const SaeB200StepStats* stats) {
   if (stats->csr_overflow) return;
   __shared__ int s_f[2];
-  __shared__ float s_red[G][32][8];   // per group, per warp, 8 partial dots
-  __shared__ float s_gf[G][8];
-  __shared__ float s_sc[G][2];
-  extern __shared__ float4 s_part[];   // (G - 1) x V x 4 float4
+  __shared__ float s_red[2][32][C];   // [chunk parity][warp][entry]
   const int tid = threadIdx.x;
-  const int V = blockDim.x / G;
-  const int g = tid / V;
-  const int col = tid - g * V;
-  const int lane = tid & 31;
-  const int wig = col >> 5;              // warp index inside the group
-  const int nwg = (V + 31) >> 5;
+  const int lane = tid & 31, wid = tid >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
   const int nvec = d / 8;
-  const bool has = col < nvec;
+  const bool has = tid < nvec;
   const float gate_grad = stats->gate_grad;
-  const uint4* go_v = reinterpret_cast<const uint4*>(go) + col;
-  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + col;
-  int it = 0;
+  const uint4* go_v = reinterpret_cast<const uint4*>(go) + tid;
+  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + tid;
+  int it = 0, par = 0;
   while (true) {
     if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
     __syncthreads();
@@ -584,113 +671,74 @@ __global__ void __launch_bounds__(MAX_THREADS)
     if (f >= n_features) break;
     const int s = col_offs[f], e = col_offs[f + 1];
     float wf[8];
-    if (has) unpack8(__ldg(reinterpret_cast<const uint4*>(w_dec) + static_cast<size_t>(f) * nvec + col), wf);
+    if (has) {
+      unpack8(__ldg(reinterpret_cast<const uint4*>(w_dec) + static_cast<size_t>(f) * nvec + tid),
+              wf);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wf[j] = 0.f;
+    }
     float ad[8], ae[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) ad[j] = ae[j] = 0.f;
     float thr = 0.f, db = 0.f;
-    const int n_chunks = (e - s + 7) >> 3;
-    for (int kb = 0; kb < n_chunks; kb += G) {   // same trip count in every group
-      const int i0 = s + 8 * (kb + g);
-      const int n = max(0, min(8, e - i0));
-      int t[8];
-      uint32_t v[8];
-      float part[8];
+    for (int i0 = s; i0 < e; i0 += C) {
+      const int n = min(C, e - i0);
+      int t[C];
+      uint32_t v[C];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
+      for (int r = 0; r < C; ++r) {
         // (the clamp only guards the row reads; the fill writes tokens < n_tokens)
         t[r] = r < n ? min(max(csr_tok[i0 + r], 0), n_tokens - 1) : 0;
         v[r] = r < n ? csr_val[i0 + r] : 0u;
       }
-      {
-        uint4 gu[8];
+      uint4 gu[C], xu[C];
 #pragma unroll
-        for (int r = 0; r < 8; ++r)
-          gu[r] = (has && r < n) ? __ldg(go_v + static_cast<size_t>(t[r]) * nvec)
-                                 : make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          float gf8[8];
-          unpack8(gu[r], gf8);
-          float a = 0.f;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) a = fmaf(gf8[j], has ? wf[j] : 0.f, a);
-          part[r] = a;
-        }
+      for (int r = 0; r < C; ++r) {
+        const bool ok = has && r < n;
+        gu[r] = ok ? __ldg(go_v + static_cast<size_t>(t[r]) * nvec) : make_uint4(0, 0, 0, 0);
+        xu[r] = (ok && (v[r] & CSR_ACTIVE)) ? __ldg(xc_v + static_cast<size_t>(t[r]) * nvec)
+                                            : make_uint4(0, 0, 0, 0);
       }
-      const float q = warp_sum8(part, lane);
-      if ((lane & 3) == 0) s_red[g][wig][lane >> 2] = q;
-      __syncthreads();
-      if (col < 8) {
+      float part[C];
+#pragma unroll
+      for (int r = 0; r < C; ++r) {
+        float g8[8];
+        unpack8(gu[r], g8);
         float a = 0.f;
-        for (int w = 0; w < nwg; ++w) a += s_red[g][w][col];
-        s_gf[g][col] = bf16_round(a);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a = fmaf(g8[j], wf[j], a);
+        part[r] = a;
       }
+      const float q = warp_sum_c<C>(part, lane);
+      constexpr int kStride = 32 / C;
+      if ((lane & (kStride - 1)) == 0) s_red[par][wid][lane / kStride] = q;
       __syncthreads();
-      // active entries: go rows again (just read, L1/L2-resident) and xc rows
-      uint4 gu[8], xu[8];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const bool a = has && r < n && (v[r] & CSR_ACTIVE);
-        gu[r] = a ? __ldg(go_v + static_cast<size_t>(t[r]) * nvec) : make_uint4(0, 0, 0, 0);
-        xu[r] = a ? __ldg(xc_v + static_cast<size_t>(t[r]) * nvec) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
+      for (int r = 0; r < C; ++r) {
         if (r < n) {
+          float a = 0.f;
+          for (int w = 0; w < nw; ++w) a += s_red[par][w][r];
+          const float gfv = bf16_round(a);
           const float p = __uint_as_float(v[r] << 16);
-          const float gfv = s_gf[g][r];
           if (v[r] & CSR_ACTIVE) {
-            float gf8[8], xf[8];
-            unpack8(gu[r], gf8);
-            unpack8(xu[r], xf);
+            float g8[8], x8[8];
+            unpack8(gu[r], g8);
+            unpack8(xu[r], x8);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              ad[j] = fmaf(p, gf8[j], ad[j]);
-              ae[j] = fmaf(gfv, xf[j], ae[j]);
+              ad[j] = fmaf(p, g8[j], ad[j]);
+              ae[j] = fmaf(gfv, x8[j], ae[j]);
             }
             db += gfv;
           }
           if (v[r] & CSR_BAND) thr += __fadd_rn(__fmul_rn(p, gfv), gate_grad);
         }
       }
+      par ^= 1;
     }
-    if constexpr (G > 1) {
-      if (n_chunks > 1) {   // uniform across the block
-        if (g > 0 && has) {
-          float4* p = s_part + ((g - 1) * V + col) * 4;
-          p[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
-          p[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
-          p[2] = make_float4(ae[0], ae[1], ae[2], ae[3]);
-          p[3] = make_float4(ae[4], ae[5], ae[6], ae[7]);
-        }
-        if (col == 0) {
-          s_sc[g][0] = thr;
-          s_sc[g][1] = db;
-        }
-        __syncthreads();
-        if (g == 0 && has) {
-#pragma unroll
-          for (int h = 0; h < G - 1; ++h) {
-            const float4* p = s_part + (h * V + col) * 4;
-            const float4 a0 = p[0], a1 = p[1], b0 = p[2], b1 = p[3];
-            ad[0] += a0.x; ad[1] += a0.y; ad[2] += a0.z; ad[3] += a0.w;
-            ad[4] += a1.x; ad[5] += a1.y; ad[6] += a1.z; ad[7] += a1.w;
-            ae[0] += b0.x; ae[1] += b0.y; ae[2] += b0.z; ae[3] += b0.w;
-            ae[4] += b1.x; ae[5] += b1.y; ae[6] += b1.z; ae[7] += b1.w;
-          }
-        }
-        if (tid == 0) {
-          for (int h = 1; h < G; ++h) {
-            thr += s_sc[h][0];
-            db += s_sc[h][1];
-          }
-        }
-        __syncthreads();
-      }
-    }
-    if (g == 0 && has) {
-      const size_t o = static_cast<size_t>(f) * d + col * 8;
+    if (has) {
+      const size_t o = static_cast<size_t>(f) * d + tid * 8;
       if (g_wdec != nullptr) {
         float4* p = reinterpret_cast<float4*>(g_wdec + o);
         if (accumulate) {
@@ -718,6 +766,7 @@ __global__ void __launch_bounds__(MAX_THREADS)
     }
   }
 }
+
 
 // ------------------------------------------------------------------ decode
 // One block per token (grid-stride). The block is G row groups of V threads;
@@ -781,7 +830,7 @@ __global__ void __launch_bounds__(1024)
                   int mask_words, int ldp, float go_scale, bf16* __restrict__ go,
                   float* __restrict__ x_hat, float* __restrict__ tok_sqerr,
                   int* __restrict__ tok_cnt, float* __restrict__ gosum_part,
-                  float* __restrict__ partial) {
+                  float* __restrict__ partial, const int* __restrict__ order) {
   __shared__ int s_f[DECODE_LIST_CAP];
   __shared__ float s_v[DECODE_LIST_CAP];
   __shared__ int s_itmp[33];
@@ -801,7 +850,8 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll
   for (int j = 0; j < 8; ++j) gsum[j] = 0.f;
 
-  for (int64_t b = blockIdx.x; b < n_tokens; b += gridDim.x) {
+  for (int64_t k = blockIdx.x; k < n_tokens; k += gridDim.x) {
+    const int64_t b = order != nullptr ? order[k] : k;
     const uint32_t* mrow = mask + b * mask_words;
     int mine = 0;
     for (int w = w0; w < w1; ++w) mine += __popc(mrow[w]);
@@ -909,6 +959,27 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll
     for (int j = 0; j < 8; ++j)
       gosum_part[static_cast<size_t>(blockIdx.x) * d + col * 8 + j] = gsum[j];
+  }
+}
+
+// Per token: its active count (popcount of the mask row) and its id, the
+// keys and values of the decode-order sort. One warp per token.
+__global__ void __launch_bounds__(256)
+    token_count_kernel(const uint32_t* __restrict__ mask, int64_t n_tokens, int mask_words,
+                       int* __restrict__ counts, int* __restrict__ ids) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t b = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+       b < n_tokens; b += warps) {
+    const uint32_t* row = mask + b * mask_words;
+    int c = 0;
+    for (int w = lane; w < mask_words; w += 32) c += __popc(row[w]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (lane == 0) {
+      counts[b] = c;
+      ids[b] = static_cast<int>(b);
+    }
   }
 }
 
