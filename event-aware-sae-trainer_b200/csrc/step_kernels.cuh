@@ -191,17 +191,27 @@ struct EncodeEpi {
       const float2 s = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), make_float2(bias, bias));
       pk[i] = pack_bf2(s.x, s.y);
     }
-    uint32_t myword = 0, sword = 0;
+    // aw: this feature's gate bits over the chunk's 32 tokens; sword: its
+    // sampled-backward entries (active or in band: pre - theta > -eps)
+    uint32_t aw = 0, sword = 0;
     const float neg_eps = -eps;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float p = (j & 1) ? bf_hi(pk[j >> 1]) : bf_lo(pk[j >> 1]);
-      const bool act = (j < nj) && (p > th);
-      const uint32_t bal = __ballot_sync(0xffffffffu, act);
-      if (lane == j) myword = bal;
-      cnt += act ? 1 : 0;
-      const bool ent = (j < nj) && __fsub_rn(p, th) > neg_eps;   // active or in band
-      sword |= ent ? (1u << j) : 0u;
+      aw |= ((j < nj) && (p > th)) ? (1u << j) : 0u;
+      sword |= ((j < nj) && __fsub_rn(p, th) > neg_eps) ? (1u << j) : 0u;
+    }
+    cnt += __popc(aw);
+    // 32x32 bit transpose across the warp (lane = feature -> lane = token):
+    // afterwards lane j holds the mask word of token t0 + j over the warp's
+    // 32 features
+    uint32_t myword = aw;
+#pragma unroll
+    for (int sh = 16; sh >= 1; sh >>= 1) {
+      const uint32_t m = sh == 16 ? 0x0000FFFFu : sh == 8 ? 0x00FF00FFu
+                       : sh == 4 ? 0x0F0F0F0Fu : sh == 2 ? 0x33333333u : 0x55555555u;
+      const uint32_t y = __shfl_xor_sync(0xffffffffu, myword, sh);
+      myword = (lane & sh) ? ((myword & ~m) | ((y >> sh) & m)) : ((myword & m) | ((y << sh) & ~m));
     }
     if (sbits != nullptr) {
       bcnt += __popc(sword);

@@ -64,12 +64,22 @@ def make_shard_sae(d_in: int, n_features: int, rank: int, world: int, seed: int 
     unit-norm Gaussian decoder columns (the reference's orthogonal init is
     impossible once F > d anyway; its columns are unit-norm), W_enc = W_dec^T,
     b_enc = 0, threshold 0.1 -- the reference's init values apart from the
-    orthogonalisation. Feature f's column depends only on (seed, f's shard)."""
+    orthogonalisation. Features are drawn in blocks of 4096 from a generator
+    seeded by (seed, block), so the whole dictionary is the same for every
+    world size whose shards are whole blocks."""
     s = shard_range(n_features, rank, world)
     per = s.stop - s.start
     dev = torch.device(device)
-    g = torch.Generator(device=dev).manual_seed(int(seed) * 1_000_003 + rank)
-    fm = torch.randn(per, d_in, generator=g, device=dev)
+    fm = torch.empty(per, d_in, device=dev)
+    g = torch.Generator(device=dev)
+    blk = 4096
+    for f0 in range(s.start, s.stop, blk):
+        b = f0 // blk
+        lo = f0 - b * blk                       # offset inside the block (0 when aligned)
+        n = min(blk - lo, s.stop - f0)
+        g.manual_seed(int(seed) * 1_000_003 + b)
+        rows = torch.randn(blk, d_in, generator=g, device=dev)[lo:lo + n]
+        fm[f0 - s.start:f0 - s.start + n] = rows
     fm /= fm.norm(dim=1, keepdim=True).clamp(min=1e-8)
     return sae_from_tensors(fm, torch.zeros(per, device=dev), fm, torch.zeros(d_in, device=dev),
                             torch.full((per,), math.log(INIT_THRESHOLD), device=dev))

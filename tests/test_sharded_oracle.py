@@ -141,3 +141,18 @@ def test_shard_ranges_split_evenly_and_reject_ragged():
         sae_b200.shard_range(64, 4, 4)
     with pytest.raises(ValueError):
         O.shard_params(_case("fp32")[1], 0, 3)
+
+
+def test_shard_init_is_the_same_dictionary_for_every_world_size():
+    """make_shard_sae draws features in seeded blocks: the shards of any split
+    concatenate to the same whole dictionary (so strong-scaling runs at
+    1/2/4/8 GPUs train the same SAE)."""
+    import torch
+    import sae_b200
+    d, F = 8, 3 * 4096 + 4096
+    whole = sae_b200.make_shard_sae(d, F, 0, 1, seed=7, device="cpu")
+    for world in (2, 4, 8):
+        parts = [sae_b200.make_shard_sae(d, F, r, world, seed=7, device="cpu") for r in range(world)]
+        assert torch.equal(torch.cat([p.W_enc.weight for p in parts]), whole.W_enc.weight)
+        assert torch.equal(torch.cat([p.W_dec.weight for p in parts], dim=1), whole.W_dec.weight)
+    torch.testing.assert_close(whole.W_dec.weight.norm(dim=0), torch.ones(F))
