@@ -49,7 +49,7 @@ NORM_MU, NORM_SIGMA = math.log(60.0), 0.4
 POOL_BATCHES = 4
 # DRAM bytes per launch of the two tile GEMMs at 32768 tokens: an ncu capture of a
 # 4096-token launch (read + write) scaled by 8 (their traffic grows with the tokens).
-TRAFFIC_ENCODER_GEMM = 8 * (0.198459e9 + 0.385634e9)
+TRAFFIC_ENCODER_GEMM = 8 * (0.204492e9 + 0.418109e9)
 TRAFFIC_GRAD_GEMM = 8 * (0.604495e9 + 0.014044e9)
 WORKLOAD = ("d_in=1536 F=49152 32768-token microbatch, L0~50, bf16 activations / "
             "fp32 master+Adam (Gemma-4-E2B residual shape)")
@@ -431,7 +431,9 @@ def run_b200(args):
     n_ev = args.steps
     k_start = [torch.cuda.Event(enable_timing=True) for _ in range(2 * n_ev)]
     k_stop = [torch.cuda.Event(enable_timing=True) for _ in range(2 * n_ev)]
-    for e in k_start + k_stop:
+    d_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    d_stop = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    for e in k_start + k_stop + d_start + d_stop:
         e.record()
     barrier()
     launches0 = L.launch_count()
@@ -442,12 +444,15 @@ def run_b200(args):
         for i in range(args.steps):
             L.set_kernel_timer(L.KERNEL_ENCODER_GEMM, k_start[2 * i], k_stop[2 * i])
             L.set_kernel_timer(L.KERNEL_GRAD_GEMM, k_start[2 * i + 1], k_stop[2 * i + 1])
+            L.set_kernel_timer(L.KERNEL_DECODE, d_start[i], d_stop[i])
             stats.append(step(i, pool[(args.warmup + i) % POOL_BATCHES]))
         ev1.record()
         barrier()
     L.set_kernel_timer(L.KERNEL_ENCODER_GEMM)
     L.set_kernel_timer(L.KERNEL_GRAD_GEMM)
+    L.set_kernel_timer(L.KERNEL_DECODE)
     launches = (L.launch_count() - launches0)
+    dec_ms = statistics.mean(d_start[i].elapsed_time(d_stop[i]) for i in range(n_ev))
     ms = ev0.elapsed_time(ev1) / args.steps
     ms = max_over_ranks(ms)
     enc_ms = statistics.mean(k_start[2 * i].elapsed_time(k_stop[2 * i]) for i in range(n_ev))
@@ -543,6 +548,7 @@ def run_b200(args):
                          "grad_gemm_ms": grad_ms, "grad_gemm_tflops": grad_tf} if gemm_bwd else
                         {"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
                          "sampled_backward_ms": grad_ms}) |
+                       {"decode_ms": dec_ms} |
                        {"step_dense_tflops": step_flop / (ms / 1e3) / 1e12},
             "clocks": clock,
             "e2e": {"value": e2e_value, "unit": "tokens/s",
