@@ -407,7 +407,8 @@ def run_b200(args):
     opt = sae_b200.B200Adam(sae_b200.reference_param_groups(sae, wl["lr"]), lr=wl["lr"],
                             betas=(0.9, 0.999), sae=sae, renorm=True)
     if sharded:
-        fs = sae_b200.ShardedFusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat)
+        fs = sae_b200.ShardedFusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat,
+                                       exchange=args.exchange)
     else:
         fs = sae_b200.FusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat)
 
@@ -519,7 +520,10 @@ def run_b200(args):
                        "model": f"JumpReLU SAE d_in={d} F={F_total}",
                        "d_in": d, "n_features": F_total, "features_per_gpu": F,
                        "tokens_per_step": tokens, "global_batch": job_tokens, "seq_len": None,
-                       "parallelism": (f"dictionary split over {world} GPU(s), NCCL all-reduce"
+                       "parallelism": (f"dictionary split over {world} GPU(s), "
+                                       + ("NVLink peer exchange of the partial x_hat"
+                                          if args.exchange == "p2p" and world > 1 else
+                                          "NCCL all-reduce of the partial x_hat")
                                        if sharded else
                                        f"atlas: {world} independent SAE(s), one per GPU"),
                        "l0_target": k_target, "l0_measured": l0_timed,
@@ -570,6 +574,8 @@ def run_b200(args):
                            "Adam/renorm over all 151M params; oracle restatement of the "
                            "reference fp32 CPU path")}
         print(json.dumps(line), flush=True)
+    if sharded:
+        fs.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -587,6 +593,9 @@ def main():
                          "sharded: one d=4096 F=131072 SAE split over the GPUs; inference: "
                          "encode + gathered decode at d=2304 F=65536")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--exchange", choices=["nccl", "p2p"], default="p2p",
+                    help="sharded workload: sum the shards' partial x_hat with an NCCL "
+                         "all-reduce, or with the fused NVLink peer exchange (default)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per step (default: the workload's); smaller values are for "
                          "profiler captures, not for the reported metric")

@@ -19,6 +19,7 @@
 #include "sae_b200.h"
 #include "step_kernels.cuh"
 #include "aux_kernels.cuh"
+#include "peer_kernels.cuh"
 #include "tile_gemm.cuh"
 
 using namespace sae;
@@ -893,6 +894,116 @@ int64_t sae_b200_shard_exchange_floats(int64_t n_tokens, int64_t d_in) {
   return n_tokens * d_in + n_tokens;
 }
 
+int sae_b200_peer_buffer_bytes(int64_t max_tokens, int64_t d_in, int64_t n_features,
+                               int64_t csr_capacity, size_t* bytes_out,
+                               uint64_t* exchange_offset_out, uint64_t* flags_offset_out) {
+  if (bytes_out == nullptr || exchange_offset_out == nullptr || flags_offset_out == nullptr ||
+      max_tokens <= 0 || d_in <= 0 || n_features <= 0 || csr_capacity < 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid peer buffer query");
+  const size_t ws = make_layout(max_tokens, d_in, n_features, csr_capacity).total;
+  const size_t ex = align_up(ws, 256);
+  const size_t fl = align_up(ex + static_cast<size_t>(max_tokens) * (d_in + 1) * 4, 256);
+  *exchange_offset_out = ex;
+  *flags_offset_out = fl;
+  *bytes_out = fl + 256;
+  return SAE_OK;
+}
+
+int sae_b200_peer_alloc(size_t bytes, void** ptr_out, void* handle_out) {
+  if (ptr_out == nullptr || handle_out == nullptr || bytes == 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid peer allocation");
+  static_assert(sizeof(cudaIpcMemHandle_t) == SAE_PEER_HANDLE_BYTES, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail(SAE_ERR_CUDA, "peer buffer cudaMalloc: %s", cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(SAE_ERR_CUDA, "peer buffer IPC handle: %s", cudaGetErrorString(e));
+  }
+  std::memcpy(handle_out, &h, sizeof(h));
+  *ptr_out = p;
+  return SAE_OK;
+}
+
+int sae_b200_peer_open(const void* handle, void** ptr_out) {
+  if (handle == nullptr || ptr_out == nullptr)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid peer handle");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(SAE_ERR_CUDA, "peer buffer open: %s", cudaGetErrorString(e));
+  return SAE_OK;
+}
+
+int sae_b200_peer_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? SAE_OK : fail(SAE_ERR_CUDA, "peer close: %s", cudaGetErrorString(e));
+}
+
+int sae_b200_peer_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? SAE_OK : fail(SAE_ERR_CUDA, "peer free: %s", cudaGetErrorString(e));
+}
+
+int sae_b200_shard_forward_p2p(const SaeB200Model* model, const void* x, int x_dtype,
+                               const SaeB200StepConfig* cfg, const SaeB200Peers* peers,
+                               SaeB200StepStats* stats, uint8_t* fired, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (peers == nullptr || peers->world < 1 || peers->world > SAE_MAX_PEERS || peers->rank < 0 ||
+      peers->rank >= peers->world)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid peer set");
+  for (int p = 0; p < peers->world; ++p)
+    if (peers->base[p] == nullptr || (reinterpret_cast<uintptr_t>(peers->base[p]) & 255u) != 0)
+      return fail(SAE_ERR_MISALIGNED, "peer buffer %d is NULL or not 256-byte aligned", p);
+  char* own = static_cast<char*>(peers->base[peers->rank]);
+  ForwardCtx c;
+  SAE_TRY(forward_checks(model, x, x_dtype, cfg, own, peers->exchange_offset, stats, nullptr, &c));
+  if (peers->flags_offset < peers->exchange_offset + static_cast<uint64_t>(c.B) * (c.d + 1) * 4)
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "peer exchange region too small for %lld tokens",
+                static_cast<long long>(c.B));
+  float* exchange = reinterpret_cast<float*>(own + peers->exchange_offset);
+  SAE_TRY(forward_encode(model, x, x_dtype, cfg, c, stats, fired, stream));
+  SAE_TRY(forward_decode(model, x, x_dtype, c, nullptr, exchange, stream));
+  // go-sum rows no rank writes (DECODE_GRID not a multiple of world) stay zero
+  const int gp = DECODE_GRID / peers->world;
+  const size_t used = static_cast<size_t>(gp) * peers->world;
+  if (used < static_cast<size_t>(DECODE_GRID) &&
+      cudaMemsetAsync(c.w.gosum_part + used * c.d, 0, (DECODE_GRID - used) * c.d * 4, stream) !=
+          cudaSuccess)
+    return fail(SAE_ERR_CUDA, "go-sum reset failed");
+  PeerArgs a{};
+  for (int p = 0; p < peers->world; ++p) a.base[p] = static_cast<char*>(peers->base[p]);
+  a.rank = peers->rank;
+  a.world = peers->world;
+  a.epoch = peers->epoch;
+  a.exchange_off = peers->exchange_offset;
+  a.flags_off = peers->flags_offset;
+  a.go_off = c.L.go;
+  a.tok_sqerr_off = c.L.tok_sqerr;
+  a.tok_cnt_off = c.L.tok_cnt;
+  a.gosum_off = c.L.gosum_part;
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(a, 0);
+  SAE_TRY(check_launch("peer_barrier_kernel"));
+  const int64_t lo = c.B * peers->rank / peers->world;
+  const int64_t hi = c.B * (peers->rank + 1) / peers->world;
+  const int V = vec_threads(c.d);
+  if (x_dtype == SAE_DTYPE_BF16)
+    exchange_reduce_kernel<bf16><<<gp, V, 0, stream>>>(a, static_cast<const bf16*>(x),
+                                                       model->b_dec, c.B, static_cast<int>(c.d),
+                                                       c.go_scale, lo, hi);
+  else
+    exchange_reduce_kernel<float><<<gp, V, 0, stream>>>(a, static_cast<const float*>(x),
+                                                        model->b_dec, c.B, static_cast<int>(c.d),
+                                                        c.go_scale, lo, hi);
+  SAE_TRY(check_launch("exchange_reduce_kernel"));
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(a, 1);
+  SAE_TRY(check_launch("peer_barrier_kernel"));
+  return forward_stats(cfg, c, stats, stream);
+}
+
 int sae_b200_shard_forward(const SaeB200Model* model, const void* x, int x_dtype,
                            const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
                            SaeB200StepStats* stats, uint8_t* fired, float* exchange,
@@ -963,27 +1074,30 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
         w.pre, w.sbits, w.theta, w.col_offs, static_cast<int>(F), B,
         static_cast<int>(pre_pitch(B)), cfg->ste_bandwidth, stats, w.csr_tok, w.csr_val);
     SAE_TRY(check_launch("csr_fill_kernel"));
-    // 2. sampled grad_feat + STE + weight gradients, one feature per block
-    const int per_sm = thr <= 192 ? 4 : (thr <= 256 ? 2 : 1);
+    // 2. sampled grad_feat + STE + weight gradients, one feature per block of
+    //    d / (8 U) threads (U = 2 for wide rows: more features in flight per SM)
+    const int nvec = static_cast<int>(d / 8);
+    const int U = (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
+    const int bthr = (nvec / U + 31) / 32 * 32;
+    const int per_sm = bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1);
     const int grid = device_info().sm_count * per_sm * 2;
     timer_begin(SAE_KERNEL_GRAD_GEMM, stream);
-#define SAE_SAMPLED(CC, MT, MB)                                                                \
-  sampled_backward_kernel<CC, MT, MB><<<grid, thr, 0, stream>>>(                              \
+#define SAE_SAMPLED(CC, UU, MT, MB)                                                            \
+  sampled_backward_kernel<CC, UU, MT, MB><<<grid, bthr, 0, stream>>>(                         \
       w.col_offs, w.csr_tok, w.csr_val, w.go, w.xc,                                           \
       static_cast<const bf16*>(model->W_dec_bf16), w.theta, static_cast<int>(F),               \
       static_cast<int>(B), static_cast<int>(d), cfg->ste_bandwidth, acc, g_wdec, grads->W_enc,  \
       grads->log_threshold, grads->b_enc, w.db_enc, w.counters, stats)
-#define SAE_SAMPLED_C(CC)                                                                      \
-  if (thr <= 192) SAE_SAMPLED(CC, 192, 3);                                                     \
-  else if (thr <= 256) SAE_SAMPLED(CC, 256, 2);                                                \
-  else if (thr <= 512) SAE_SAMPLED(CC, 512, 1);                                                \
-  else SAE_SAMPLED(CC, 1024, 1);
-    if (thr <= 192) {
-      SAE_SAMPLED(2, 192, 4);
+    if (U == 1) {
+      if (bthr <= 192) SAE_SAMPLED(2, 1, 192, 4);
+      else if (bthr <= 256) SAE_SAMPLED(4, 1, 256, 2);
+      else if (bthr <= 512) SAE_SAMPLED(4, 1, 512, 1);
+      else SAE_SAMPLED(4, 1, 1024, 1);
     } else {
-      SAE_SAMPLED_C(4)
+      if (bthr <= 192) SAE_SAMPLED(2, 2, 192, 2);
+      else if (bthr <= 256) SAE_SAMPLED(2, 2, 256, 2);
+      else SAE_SAMPLED(2, 2, 512, 1);
     }
-#undef SAE_SAMPLED_C
 #undef SAE_SAMPLED
     const int rc = check_launch("sampled_backward_kernel");
     timer_end(SAE_KERNEL_GRAD_GEMM, stream);

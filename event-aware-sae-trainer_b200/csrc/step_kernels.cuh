@@ -651,7 +651,7 @@ __device__ __forceinline__ float warp_sum_c(float (&p)[C], int lane) {
 // thread adds the warps' partials (double-buffered by chunk parity) in the
 // same order, so all threads hold the same grad_feat and the result does not
 // depend on timing.
-template <int C, int MAX_THREADS, int MIN_BLOCKS>
+template <int C, int U, int MAX_THREADS, int MIN_BLOCKS>
 __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
     sampled_backward_kernel(const int* __restrict__ col_offs, const int* __restrict__ csr_tok,
                             const uint32_t* __restrict__ csr_val, const bf16* __restrict__ go,
@@ -661,6 +661,7 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
                             float* __restrict__ g_wenc, float* __restrict__ g_logthr,
                             float* __restrict__ g_benc, float* __restrict__ db_enc,
                             int* __restrict__ counter, const SaeB200StepStats* stats) {
+  // thread tid owns columns [8 U tid, 8 U tid + 8 U): U consecutive 16-byte vectors
   if (stats->csr_overflow) return;
   __shared__ int s_f[2];
   __shared__ float s_red[2][32][C];   // [chunk parity][warp][entry]
@@ -668,10 +669,10 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
   const int lane = tid & 31, wid = tid >> 5;
   const int nw = (blockDim.x + 31) >> 5;
   const int nvec = d / 8;
-  const bool has = tid < nvec;
+  const bool has = (tid + 1) * U <= nvec;
   const float gate_grad = stats->gate_grad;
-  const uint4* go_v = reinterpret_cast<const uint4*>(go) + tid;
-  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + tid;
+  const uint4* go_v = reinterpret_cast<const uint4*>(go) + U * tid;
+  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + U * tid;
   int it = 0, par = 0;
   while (true) {
     if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
@@ -680,17 +681,23 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
     ++it;
     if (f >= n_features) break;
     const int s = col_offs[f], e = col_offs[f + 1];
-    float wf[8];
-    if (has) {
-      unpack8(__ldg(reinterpret_cast<const uint4*>(w_dec) + static_cast<size_t>(f) * nvec + tid),
-              wf);
-    } else {
+    float wf[8 * U];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) wf[j] = 0.f;
+    for (int u = 0; u < U; ++u) {
+      float w8[8];
+      if (has) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(w_dec) + static_cast<size_t>(f) * nvec +
+                      U * tid + u), w8);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w8[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wf[8 * u + j] = w8[j];
     }
-    float ad[8], ae[8];
+    float ad[8 * U], ae[8 * U];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ad[j] = ae[j] = 0.f;
+    for (int j = 0; j < 8 * U; ++j) ad[j] = ae[j] = 0.f;
     float thr = 0.f, db = 0.f;
     for (int i0 = s; i0 < e; i0 += C) {
       const int n = min(C, e - i0);
@@ -702,22 +709,30 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
         t[r] = r < n ? min(max(csr_tok[i0 + r], 0), n_tokens - 1) : 0;
         v[r] = r < n ? csr_val[i0 + r] : 0u;
       }
-      uint4 gu[C], xu[C];
+      uint4 gu[C][U], xu[C][U];
 #pragma unroll
       for (int r = 0; r < C; ++r) {
         const bool ok = has && r < n;
-        gu[r] = ok ? __ldg(go_v + static_cast<size_t>(t[r]) * nvec) : make_uint4(0, 0, 0, 0);
-        xu[r] = (ok && (v[r] & CSR_ACTIVE)) ? __ldg(xc_v + static_cast<size_t>(t[r]) * nvec)
-                                            : make_uint4(0, 0, 0, 0);
+        const bool act = ok && (v[r] & CSR_ACTIVE);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          gu[r][u] = ok ? __ldg(go_v + static_cast<size_t>(t[r]) * nvec + u)
+                        : make_uint4(0, 0, 0, 0);
+          xu[r][u] = act ? __ldg(xc_v + static_cast<size_t>(t[r]) * nvec + u)
+                         : make_uint4(0, 0, 0, 0);
+        }
       }
       float part[C];
 #pragma unroll
       for (int r = 0; r < C; ++r) {
-        float g8[8];
-        unpack8(gu[r], g8);
         float a = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) a = fmaf(g8[j], wf[j], a);
+        for (int u = 0; u < U; ++u) {
+          float g8[8];
+          unpack8(gu[r][u], g8);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a = fmaf(g8[j], wf[8 * u + j], a);
+        }
         part[r] = a;
       }
       const float q = warp_sum_c<C>(part, lane);
@@ -732,13 +747,16 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
           const float gfv = bf16_round(a);
           const float p = __uint_as_float(v[r] << 16);
           if (v[r] & CSR_ACTIVE) {
-            float g8[8], x8[8];
-            unpack8(gu[r], g8);
-            unpack8(xu[r], x8);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              ad[j] = fmaf(p, g8[j], ad[j]);
-              ae[j] = fmaf(gfv, x8[j], ae[j]);
+            for (int u = 0; u < U; ++u) {
+              float g8[8], x8[8];
+              unpack8(gu[r][u], g8);
+              unpack8(xu[r][u], x8);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                ad[8 * u + j] = fmaf(p, g8[j], ad[8 * u + j]);
+                ae[8 * u + j] = fmaf(gfv, x8[j], ae[8 * u + j]);
+              }
             }
             db += gfv;
           }
@@ -748,25 +766,26 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
       par ^= 1;
     }
     if (has) {
-      const size_t o = static_cast<size_t>(f) * d + tid * 8;
-      if (g_wdec != nullptr) {
-        float4* p = reinterpret_cast<float4*>(g_wdec + o);
-        if (accumulate) {
-          const float4 u = p[0], w = p[1];
-          ad[0] += u.x; ad[1] += u.y; ad[2] += u.z; ad[3] += u.w;
-          ad[4] += w.x; ad[5] += w.y; ad[6] += w.z; ad[7] += w.w;
+      const size_t o = static_cast<size_t>(f) * d + static_cast<size_t>(tid) * 8 * U;
+#pragma unroll
+      for (int q4 = 0; q4 < 2 * U; ++q4) {
+        if (g_wdec != nullptr) {
+          float4* p = reinterpret_cast<float4*>(g_wdec + o) + q4;
+          float4 a4 = make_float4(ad[4 * q4], ad[4 * q4 + 1], ad[4 * q4 + 2], ad[4 * q4 + 3]);
+          if (accumulate) {
+            const float4 u4 = *p;
+            a4.x += u4.x; a4.y += u4.y; a4.z += u4.z; a4.w += u4.w;
+          }
+          *p = a4;
         }
-        p[0] = make_float4(ad[0], ad[1], ad[2], ad[3]);
-        p[1] = make_float4(ad[4], ad[5], ad[6], ad[7]);
+        float4* p = reinterpret_cast<float4*>(g_wenc + o) + q4;
+        float4 e4 = make_float4(ae[4 * q4], ae[4 * q4 + 1], ae[4 * q4 + 2], ae[4 * q4 + 3]);
+        if (accumulate) {
+          const float4 u4 = *p;
+          e4.x += u4.x; e4.y += u4.y; e4.z += u4.z; e4.w += u4.w;
+        }
+        *p = e4;
       }
-      float4* p = reinterpret_cast<float4*>(g_wenc + o);
-      if (accumulate) {
-        const float4 u = p[0], w = p[1];
-        ae[0] += u.x; ae[1] += u.y; ae[2] += u.z; ae[3] += u.w;
-        ae[4] += w.x; ae[5] += w.y; ae[6] += w.z; ae[7] += w.w;
-      }
-      p[0] = make_float4(ae[0], ae[1], ae[2], ae[3]);
-      p[1] = make_float4(ae[4], ae[5], ae[6], ae[7]);
     }
     if (tid == 0) {
       const float gl = -(thr / (eps + eps)) * theta[f];
@@ -970,6 +989,8 @@ __global__ void __launch_bounds__(1024)
     for (int j = 0; j < 8; ++j)
       gosum_part[static_cast<size_t>(blockIdx.x) * d + col * 8 + j] = gsum[j];
   }
+  // sharded step: the partials may be read by other GPUs (peer exchange)
+  if (partial != nullptr) __threadfence_system();
 }
 
 // Per token: its active count (popcount of the mask row) and its id, the

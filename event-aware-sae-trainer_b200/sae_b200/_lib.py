@@ -107,6 +107,22 @@ class AuxConfig(ctypes.Structure):
     ]
 
 
+MAX_PEERS = 8
+PEER_HANDLE_BYTES = 64
+
+
+class Peers(ctypes.Structure):
+    _fields_ = [
+        ("rank", c_int32),
+        ("world", c_int32),
+        ("epoch", ctypes.c_uint32),
+        ("reserved", c_int32),
+        ("exchange_offset", ctypes.c_uint64),
+        ("flags_offset", ctypes.c_uint64),
+        ("base", c_void_p * MAX_PEERS),
+    ]
+
+
 class AdamTensor(ctypes.Structure):
     _fields_ = [
         ("lr", c_float),
@@ -156,6 +172,16 @@ _SIGNATURES = {
         [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t,
          POINTER(AuxConfig), c_void_p, c_size_t, c_void_p], c_int),
     "sae_b200_shard_exchange_floats": ([c_int64, c_int64], c_int64),
+    "sae_b200_peer_buffer_bytes": (
+        [c_int64, c_int64, c_int64, c_int64, POINTER(c_size_t), POINTER(ctypes.c_uint64),
+         POINTER(ctypes.c_uint64)], c_int),
+    "sae_b200_peer_alloc": ([c_size_t, POINTER(c_void_p), c_void_p], c_int),
+    "sae_b200_peer_open": ([c_void_p, POINTER(c_void_p)], c_int),
+    "sae_b200_peer_close": ([c_void_p], c_int),
+    "sae_b200_peer_free": ([c_void_p], c_int),
+    "sae_b200_shard_forward_p2p": (
+        [POINTER(Model), c_void_p, c_int, POINTER(StepConfig), POINTER(Peers), c_void_p, c_void_p,
+         c_void_p], c_int),
     "sae_b200_shard_forward": (
         [POINTER(Model), c_void_p, c_int, POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
          c_void_p, c_void_p, c_void_p], c_int),

@@ -85,6 +85,79 @@ def make_shard_sae(d_in: int, n_features: int, rank: int, world: int, seed: int 
                             torch.full((per,), math.log(INIT_THRESHOLD), device=dev))
 
 
+class _DeviceBytes:
+    """A raw device allocation seen as a torch uint8 tensor (no ownership)."""
+
+    def __init__(self, ptr: int, nbytes: int, device: torch.device):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+        self.device = device
+
+
+class PeerExchange:
+    """The ranks' peer buffers (workspace + exchange + flags), mapped into every
+    rank by CUDA IPC for sae_b200_shard_forward_p2p. Collective: every rank of
+    ``group`` constructs it with the same sizes."""
+
+    def __init__(self, max_tokens: int, d_in: int, n_features: int, csr_capacity: int, *,
+                 group=None, device: torch.device):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > L.MAX_PEERS:
+            raise ValueError(f"peer exchange supports at most {L.MAX_PEERS} ranks")
+        nbytes = ctypes.c_size_t(0)
+        ex = ctypes.c_uint64(0)
+        fl = ctypes.c_uint64(0)
+        L.call("sae_b200_peer_buffer_bytes", max_tokens, d_in, n_features, csr_capacity,
+               ctypes.byref(nbytes), ctypes.byref(ex), ctypes.byref(fl))
+        self.nbytes, self.exchange_offset, self.flags_offset = nbytes.value, ex.value, fl.value
+        own = ctypes.c_void_p(0)
+        handle = (ctypes.c_uint8 * L.PEER_HANDLE_BYTES)()
+        with torch.cuda.device(device):
+            L.call("sae_b200_peer_alloc", self.nbytes, ctypes.byref(own), handle)
+        self.own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.bases = [0] * self.world
+        self._opened = []
+        with torch.cuda.device(device):
+            for p in range(self.world):
+                if p == self.rank:
+                    self.bases[p] = self.own
+                    continue
+                h = (ctypes.c_uint8 * L.PEER_HANDLE_BYTES).from_buffer_copy(handles[p])
+                ptr = ctypes.c_void_p(0)
+                L.call("sae_b200_peer_open", h, ctypes.byref(ptr))
+                self.bases[p] = ptr.value
+                self._opened.append(ptr.value)
+        self.epoch = 0
+        self.workspace = torch.as_tensor(_DeviceBytes(self.own, self.exchange_offset, device),
+                                         device=device)
+
+    def next_peers(self) -> L.Peers:
+        self.epoch += 1
+        p = L.Peers()
+        p.rank, p.world, p.epoch = self.rank, self.world, self.epoch
+        p.exchange_offset, p.flags_offset = self.exchange_offset, self.flags_offset
+        for i, b in enumerate(self.bases):
+            p.base[i] = b
+        return p
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)   # no rank touches another's buffer any more
+        for ptr in self._opened:
+            L.call("sae_b200_peer_close", ptr)
+        dist.barrier(group=self.group)
+        L.call("sae_b200_peer_free", self.own)
+        self.own = None
+        self.workspace = None
+
+
 class ShardedFusedStep(FusedStep):
     """FusedStep over one dictionary shard, with the three cross-rank sums.
 
@@ -98,11 +171,13 @@ class ShardedFusedStep(FusedStep):
 
     def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int, *,
                  group=None, csr_capacity: Optional[int] = None, force_simt: bool = False,
-                 grad_feat: str = "sampled",
+                 grad_feat: str = "sampled", exchange: str = "nccl",
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None,
                  rank: Optional[int] = None, world: Optional[int] = None):
         super().__init__(sae, optimizer, max_tokens, csr_capacity=csr_capacity,
                          force_simt=force_simt, grad_feat=grad_feat)
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.group = group
         if allreduce is not None:
             if rank is None or world is None or not 0 <= rank < world:
@@ -114,9 +189,26 @@ class ShardedFusedStep(FusedStep):
         else:
             self.rank, self.world = 0, 1
         self._custom_allreduce = allreduce
-        n_ex = int(L.load().sae_b200_shard_exchange_floats(self.max_tokens, sae.d_in))
-        self.exchange = torch.empty(n_ex, device=self.device, dtype=torch.float32)
         self.sumsq = torch.zeros(1, device=self.device, dtype=torch.float32)
+        self.peers = None
+        if exchange == "p2p" and self.world > 1:
+            if allreduce is not None:
+                raise ValueError("the peer exchange runs over torch.distributed ranks")
+            # the step workspace lives in the IPC-mapped peer buffer
+            self.peers = PeerExchange(self.max_tokens, sae.d_in, sae.n_features,
+                                      self.csr_capacity, group=group, device=self.device)
+            self.ws = self.peers.workspace
+            self.ws_bytes = self.peers.exchange_offset
+            self.exchange = None
+        else:
+            n_ex = int(L.load().sae_b200_shard_exchange_floats(self.max_tokens, sae.d_in))
+            self.exchange = torch.empty(n_ex, device=self.device, dtype=torch.float32)
+
+    def close(self) -> None:
+        """Collective with the peer exchange: release the peer buffers."""
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
 
     def _allreduce(self, t: torch.Tensor) -> None:
         if self._custom_allreduce is not None:
@@ -139,15 +231,28 @@ class ShardedFusedStep(FusedStep):
         model = sae._model_struct(need_shadows=True)
         stream = _stream()
         dt = L.DTYPE_BF16 if x.dtype == torch.bfloat16 else L.DTYPE_F32
-        ex = self.exchange[:n * (sae.d_in + 1)]
-        L.call("sae_b200_shard_forward", ctypes.byref(model), L.ptr(x), dt, ctypes.byref(cfg),
-               L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), L.ptr(self.fired), L.ptr(ex),
-               stream)
-        self._allreduce(ex)                                    # partial x_hat + L0 counts
-        L.call("sae_b200_shard_finish_forward", ctypes.byref(model), L.ptr(x), dt,
-               ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), L.ptr(ex),
-               L.ptr(x_hat_out), stream)
-        st = self.read_stats()
+        if self.peers is not None:
+            if x_hat_out is not None:
+                raise ValueError("x_hat_out is not available with the peer exchange")
+            peers = self.peers.next_peers()
+            # encoder, decode partial, NVLink sum + residual, loss terms: one call
+            L.call("sae_b200_shard_forward_p2p", ctypes.byref(model), L.ptr(x), dt,
+                   ctypes.byref(cfg), ctypes.byref(peers), L.ptr(self.stats), L.ptr(self.fired),
+                   stream)
+            st = self.read_stats()
+            if L.device_status() != 0:
+                raise L.SaeB200Error(L.SAE_ERR_DEVICE_TIMEOUT,
+                                     "a peer exchange barrier timed out (a rank stopped)")
+        else:
+            ex = self.exchange[:n * (sae.d_in + 1)]
+            L.call("sae_b200_shard_forward", ctypes.byref(model), L.ptr(x), dt,
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
+                   L.ptr(self.fired), L.ptr(ex), stream)
+            self._allreduce(ex)                                # partial x_hat + L0 counts
+            L.call("sae_b200_shard_finish_forward", ctypes.byref(model), L.ptr(x), dt,
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
+                   L.ptr(ex), L.ptr(x_hat_out), stream)
+            st = self.read_stats()
         self.nnz_last = st["nnz"]
         grads = self._grads_struct()
         scratch = None

@@ -267,6 +267,37 @@ int sae_b200_aux_backward(const SaeB200Model* model, const SaeB200Grads* grads,
  * N = 1 the sequence gives the same result as the unsharded entry points up
  * to fp32 summation order. */
 int64_t sae_b200_shard_exchange_floats(int64_t n_tokens, int64_t d_in);
+
+/* NVLink peer exchange (alternative to the all-reduce of step 1): every rank's
+ * "peer buffer" -- [step workspace | exchange | flags] -- is mapped into every
+ * rank by CUDA IPC, and sae_b200_shard_forward_p2p does sae_b200_shard_forward,
+ * the cross-shard sum and sae_b200_shard_finish_forward in one call: rank r
+ * sums the partials of tokens [rB/N, (r+1)B/N) with peer loads and writes
+ * their go, squared error and count into every rank's workspace with peer
+ * stores, between two flag barriers (bounded: a barrier that waits over 2 s
+ * sets SAE_ERR_DEVICE_TIMEOUT in the device status word and returns). The
+ * backward and the two remaining scalar/vector sums are as above. Setup-time
+ * calls only: sae_b200_peer_alloc is the one entry point that allocates
+ * (cudaMalloc of the buffer, zero-filled); free it after every rank is done. */
+#define SAE_MAX_PEERS 8
+#define SAE_PEER_HANDLE_BYTES 64
+typedef struct SaeB200Peers {
+  int32_t rank, world;     /* world <= SAE_MAX_PEERS, one GPU per rank */
+  uint32_t epoch;          /* larger than any epoch used before with these buffers */
+  int32_t reserved;
+  uint64_t exchange_offset, flags_offset;   /* from sae_b200_peer_buffer_bytes */
+  void* base[SAE_MAX_PEERS];                /* rank p's buffer, mapped here (own included) */
+} SaeB200Peers;
+int sae_b200_peer_buffer_bytes(int64_t max_tokens, int64_t d_in, int64_t n_features,
+                               int64_t csr_capacity, size_t* bytes_out,
+                               uint64_t* exchange_offset_out, uint64_t* flags_offset_out);
+int sae_b200_peer_alloc(size_t bytes, void** ptr_out, void* handle_out /* 64 bytes, host */);
+int sae_b200_peer_open(const void* handle /* host */, void** ptr_out);
+int sae_b200_peer_close(void* ptr);
+int sae_b200_peer_free(void* ptr);
+int sae_b200_shard_forward_p2p(const SaeB200Model* model, const void* x, int x_dtype,
+                               const SaeB200StepConfig* cfg, const SaeB200Peers* peers,
+                               SaeB200StepStats* stats, uint8_t* fired, void* stream);
 /* Encoder GEMM + gate + CSR offsets + gathered decode of this shard's features
  * (decode / _SparseDecode.forward 922-950 restricted to the shard). */
 int sae_b200_shard_forward(const SaeB200Model* model, const void* x, int x_dtype,

@@ -125,7 +125,7 @@ def _dt(precision: str):
 
 # ------------------------------------------------------------------ forward
 def forward(x: np.ndarray, p: Params, cfg: StepConfig, precision: str = "fp32",
-            theta: np.ndarray | None = None) -> ForwardOut:
+            theta: np.ndarray | None = None, pre: np.ndarray | None = None) -> ForwardOut:
     """Encoder + JumpReLU + dense decode + loss terms of one microbatch.
 
     sae_trainer_rolling.py: _EncoderPreBias.forward 584-590 (pre = addmm(b_enc,
@@ -138,6 +138,8 @@ def forward(x: np.ndarray, p: Params, cfg: StepConfig, precision: str = "fp32",
     grid, so a threshold one float32 ulp away moves whole grid points across
     the gate or the STE band edge. Parity checks of a GPU path therefore pass
     the thresholds that path computed (after checking them against exp).
+    ``pre`` (bf16 mode) likewise replaces the pre-activations by the GPU's own
+    bf16 values, so that a backward check sees exactly the same gates.
     """
     B = x.shape[0]
     acc_dt = np.float64 if precision in ("fp64", "bf16") else np.float32
@@ -146,8 +148,10 @@ def forward(x: np.ndarray, p: Params, cfg: StepConfig, precision: str = "fp32",
             theta = np.exp(p.log_threshold.astype(np.float32)).astype(np.float32)
         theta = np.asarray(theta, np.float32)
         xc = bf16(x.astype(np.float32) - p.b_dec.astype(np.float32))
-        pre = bf16((xc.astype(acc_dt) @ bf16(p.W_enc).astype(acc_dt).T
-                    + bf16(p.b_enc).astype(acc_dt)).astype(np.float32))
+        if pre is None:
+            pre = bf16((xc.astype(acc_dt) @ bf16(p.W_enc).astype(acc_dt).T
+                        + bf16(p.b_enc).astype(acc_dt)).astype(np.float32))
+        pre = np.asarray(pre, np.float32)
         gate = (pre > theta).astype(np.float32)
         feat = pre * gate
         dec = bf16((bf16(feat).astype(acc_dt) @ bf16(p.W_dec).astype(acc_dt).T).astype(np.float32))

@@ -15,7 +15,7 @@ ROOT = Path(__file__).resolve().parents[1]
 sys.path[:0] = [str(ROOT), str(ROOT / "event-aware-sae-trainer_b200"), str(ROOT / "tests")]
 
 
-def main(out_dir):
+def main(out_dir, exchange="nccl"):
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -40,7 +40,7 @@ def main(out_dir):
     opt = B200Adam(reference_param_groups(sae, lr), lr=lr, betas=(0.9, 0.999), sae=sae,
                    renorm=True)
     x = torch.from_numpy(g["x0"].astype(np.float32)).to(dev)
-    fs = ShardedFusedStep(sae, opt, max_tokens=x.shape[0])
+    fs = ShardedFusedStep(sae, opt, max_tokens=x.shape[0], exchange=exchange)
     wf = float(g["wenc_factor"])
     out = fs.step(x, lambda_l0=float(g["lam"]), al_mu=float(g["mu"]), target_l0=float(g["target"]),
                   wenc_dampen=lambda l0: wf)
@@ -56,9 +56,14 @@ def main(out_dir):
              W_dec=sae.W_dec.weight.detach().cpu().numpy(), b_dec=sae.b_dec.detach().cpu().numpy(),
              log_threshold=sae.log_threshold.detach().cpu().numpy(), theta=theta)
     (Path(out_dir) / f"rank{rank}.json").write_text(json.dumps(out))
+    # a second step exercises the flag barriers' epochs and the buffers' reuse
+    out2 = fs.step(x, lambda_l0=float(g["lam"]), al_mu=float(g["mu"]),
+                   target_l0=float(g["target"]), wenc_dampen=lambda l0: wf)
+    assert np.isfinite(out2["loss"])
+    fs.close()
     dist.barrier()
     dist.destroy_process_group()
 
 
 if __name__ == "__main__":
-    main(sys.argv[1])
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "nccl")

@@ -265,3 +265,40 @@ def test_bf16_input_matches_oracle():
     ref = O.backward(xb.float().numpy(), oracle_params(g), fw, cfg, "bf16")
     assert _rel(fs.g_W_enc.cpu().numpy(), ref.W_enc) < BF16_TOL
     assert _rel(fs.g_log_thr.cpu().numpy(), ref.log_threshold) < BF16_TOL
+
+
+@pytest.mark.parametrize("grad_feat", ["sampled", "gemm"])
+def test_wide_rows_match_oracle(grad_feat):
+    """d = 2048: the wide-row variant of the sampled backward (two 16-byte
+    vectors per thread) against the oracle's backward on the same gates."""
+    import math
+    from sae_b200 import B200Adam, FusedStep, make_sae, reference_param_groups
+    d, F, B = 2048, 256, 192
+    x = O.superposition_batch(B, d, 512, 12, math.log(12.0), 0.3, seed=23)
+    sae = make_sae(d, F, seed=4)
+    with torch.no_grad():
+        sae.b_dec.copy_(torch.from_numpy(x.mean(0)))
+        sae.log_threshold.fill_(math.log(0.25))
+    p0 = O.Params(sae.W_enc.weight.detach().numpy().copy(), sae.W_enc.bias.detach().numpy().copy(),
+                  sae.W_dec.weight.detach().numpy().copy(), sae.b_dec.detach().numpy().copy(),
+                  sae.log_threshold.detach().numpy().copy())
+    sae = sae.cuda()
+    sae.ste_bandwidth = 0.05
+    lr = 1e-4
+    opt = B200Adam(reference_param_groups(sae, lr), lr=lr, sae=sae, renorm=True)
+    fs = FusedStep(sae, opt, max_tokens=B, grad_feat=grad_feat)
+    cfg = O.StepConfig(lambda_l0=1e-3, al_mu=1e-2, target_l0=8.0, ste_bandwidth=0.05,
+                       lr=(lr,) * 4)
+    xt = torch.from_numpy(x).cuda()
+    st = fs.microbatch(xt, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu, target_l0=cfg.target_l0)
+    torch.cuda.synchronize()
+    v = workspace_views(fs, B)
+    # the oracle's backward given the kernel's own thresholds and bf16 pre-activations
+    # (a dense case: ~17% active, many entries within one bf16 ulp of the threshold)
+    fw = O.forward(x, p0, cfg, "bf16", theta=v["theta"].cpu().numpy(),
+                   pre=v["pre"].float().cpu().numpy())
+    assert fw.l0 > 2 and st["l0"] == pytest.approx(fw.l0, rel=1e-6)
+    ref = O.backward(x, p0, fw, cfg, "bf16")
+    for k, t in {"W_enc": fs.g_W_enc, "b_enc": fs.g_b_enc, "W_dec": fs.g_W_dec_fm.t(),
+                 "b_dec": fs.g_b_dec, "log_threshold": fs.g_log_thr}.items():
+        assert _rel(t.cpu().numpy(), getattr(ref, k)) < 5e-3, k

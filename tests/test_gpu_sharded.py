@@ -174,12 +174,16 @@ def test_emulated_shards_accumulate_microbatches():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpu_nccl_shards_match_oracle(tmp_path):
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_two_gpu_shards_match_oracle(tmp_path, exchange):
+    """Two ranks over NCCL (all-reduce of the partial x_hat) or over the NVLink
+    peer exchange (peer loads of the partials, peer stores of go)."""
     env = dict(os.environ)
     env["NCCL_NVLS_ENABLE"] = "0"
+    port = "29517" if exchange == "nccl" else "29518"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29517",
-           str(ROOT / "tests" / "sharded_worker.py"), str(tmp_path)]
+           "--master-addr", "127.0.0.1", "--master-port", port,
+           str(ROOT / "tests" / "sharded_worker.py"), str(tmp_path), exchange]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     g = load_golden("super_f32_tiles")
