@@ -412,9 +412,18 @@ def run_b200(args):
     else:
         fs = sae_b200.FusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat)
 
+    aux_dead, aux_k = None, 0
+    if args.aux_dead > 0 and not sharded:
+        # a fixed dead set (the revival controller's aux_dead_mask) and the trainer's
+        # legacy eff_k = max(8, min(AUX_K=128, K // 2)) (sae_trainer_rolling.py:449-456)
+        gen = torch.Generator(device="cpu").manual_seed(99)
+        n_dead = int(args.aux_dead * F)
+        aux_dead = torch.randperm(F, generator=gen)[:n_dead].sort().values.to(dev)
+        aux_k = max(8, min(128, k_target // 2))
+
     def step(i, x):
         out = fs.step(x, lambda_l0=LAMBDA, al_mu=MU, target_l0=k_target,
-                      wenc_dampen=lambda l0: 1.0)
+                      wenc_dampen=lambda l0: 1.0, aux_dead=aux_dead, aux_k=aux_k)
         threshold_nudge(sae, out["l0"], k_target)
         return out
 
@@ -475,7 +484,14 @@ def run_b200(args):
     def h2d(j, src):
         with torch.cuda.stream(side):
             side.wait_stream(torch.cuda.current_stream())
-            bufs[j].copy_(src, non_blocking=True)
+            if sharded and world > 1:
+                # the replicated batch: each rank copies its 1/N of the rows over PCIe and
+                # the ranks all-gather the rest over NVLink
+                lo, hi = tokens * rank // world, tokens * (rank + 1) // world
+                bufs[j][lo:hi].copy_(src[lo:hi], non_blocking=True)
+                dist.all_gather_into_tensor(bufs[j], bufs[j][lo:hi].clone())
+            else:
+                bufs[j].copy_(src, non_blocking=True)
             ready[j].record(side)
 
     barrier()
@@ -527,6 +543,8 @@ def run_b200(args):
                                        if sharded else
                                        f"atlas: {world} independent SAE(s), one per GPU"),
                        "l0_target": k_target, "l0_measured": l0_timed,
+                       "aux_loss": ({"dead_fraction": args.aux_dead, "k": aux_k}
+                                    if aux_dead is not None else None),
                        "threshold_calibrated": thr,
                        "threshold_control": "proportional log-threshold nudge after each step "
                                             "(the trainer's L0 controller)",
@@ -556,11 +574,14 @@ def run_b200(args):
                        {"step_dense_tflops": step_flop / (ms / 1e3) / 1e12},
             "clocks": clock,
             "e2e": {"value": e2e_value, "unit": "tokens/s",
-                    "h2d_bytes_per_step": world * tokens * d * 2,
+                    "h2d_bytes_per_step": (tokens if sharded else world * tokens) * d * 2,
                     "d2h_bytes_per_step": world * 2 * 64,
-                    "note": "whole job: every rank copies its pinned host batch (H2D on a side "
-                            "stream overlapped with the previous step, as the trainer's double "
-                            "buffer) and reads its stats back every step"},
+                    "note": ("whole job: each rank copies 1/N of the pinned host batch over "
+                             "PCIe and the ranks all-gather the replicated batch over NVLink"
+                             if sharded and world > 1 else
+                             "whole job: every rank copies its pinned host batch") +
+                            " (on a side stream overlapped with the previous step, as the "
+                            "trainer's double buffer) and reads its stats back every step"},
             "gpu_launches": int(launches),
             "device_status": status,
         }
@@ -596,6 +617,10 @@ def main():
     ap.add_argument("--exchange", choices=["nccl", "p2p"], default="p2p",
                     help="sharded workload: sum the shards' partial x_hat with an NCCL "
                          "all-reduce, or with the fused NVLink peer exchange (default)")
+    ap.add_argument("--aux-dead", type=float, default=0.0,
+                    help="atlas workload: also run the dead-feature aux loss with this fraction "
+                         "of the dictionary marked dead (the trainer turns it on after 250 "
+                         "silent steps)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per step (default: the workload's); smaller values are for "
                          "profiler captures, not for the reported metric")

@@ -163,15 +163,18 @@ class ShardedFusedStep(FusedStep):
 
     ``group`` is the process group of the ranks sharing the dictionary
     (default: the whole world). With one rank (or no process group) the
-    sequence reduces to the unsharded step. ``allreduce`` (with ``rank`` and
-    ``world``) replaces the torch.distributed sum by the caller's own in-place
-    sum over the ranks, called with each of the three buffers in order.
+    sequence reduces to the unsharded step. ``exchange``: "p2p" (default) sums
+    the partial x_hat over NVLink peer memory fused with the residual
+    (``PeerExchange``, one GPU per rank on one node); "nccl" all-reduces it
+    with torch.distributed. ``allreduce`` (with ``rank`` and
+    ``world``) replaces both by the caller's own in-place sum over the ranks,
+    called with each of the three buffers in order.
     ``step()``, ``microbatch()``, ``grad_norm()`` and the returned statistics
     have FusedStep's meaning; ``nnz`` and ``csr_overflow`` are this shard's."""
 
     def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int, *,
                  group=None, csr_capacity: Optional[int] = None, force_simt: bool = False,
-                 grad_feat: str = "sampled", exchange: str = "nccl",
+                 grad_feat: str = "sampled", exchange: str = "p2p",
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None,
                  rank: Optional[int] = None, world: Optional[int] = None):
         super().__init__(sae, optimizer, max_tokens, csr_capacity=csr_capacity,
@@ -191,9 +194,7 @@ class ShardedFusedStep(FusedStep):
         self._custom_allreduce = allreduce
         self.sumsq = torch.zeros(1, device=self.device, dtype=torch.float32)
         self.peers = None
-        if exchange == "p2p" and self.world > 1:
-            if allreduce is not None:
-                raise ValueError("the peer exchange runs over torch.distributed ranks")
+        if exchange == "p2p" and self.world > 1 and allreduce is None:
             # the step workspace lives in the IPC-mapped peer buffer
             self.peers = PeerExchange(self.max_tokens, sae.d_in, sae.n_features,
                                       self.csr_capacity, group=group, device=self.device)
