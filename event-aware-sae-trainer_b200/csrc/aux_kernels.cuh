@@ -5,8 +5,9 @@
 // nothing (relu), so only the positive candidates are ever selected.
 //
 // Layout: the selected entries of token b sit at [b * k, b * k + cnt[b]) of
-// two arrays (dead-list index j, value), in increasing j; the backward works
-// on the same entries sorted by j (stable, so tokens ascend within a feature).
+// two arrays (dead-list index j, value), in increasing j; the backward sorts
+// them by j (stable, so tokens ascend within a feature) and runs the sampled
+// backward's kernel over that feature-major CSR.
 #pragma once
 #include <cuda_bf16.h>
 #include <cstdint>
@@ -51,9 +52,15 @@ __global__ void __launch_bounds__(256)
   // round 1: histogram of the high byte of every positive key
   for (int i = tid; i < AUX_TB * 257; i += blockDim.x) (&hist[0][0])[i] = 0u;
   __syncthreads();
-  for (int j = warp; j < n_dead; j += 8) {
-    const uint32_t key = key_at(j);
-    if (key) atomicAdd(&hist[lane][key >> 8], 1u);
+  // 8 rows per warp in flight: the dead id and the row segment are two
+  // dependent loads per row
+  for (int j0 = warp * 8; j0 < n_dead; j0 += 64) {
+    uint32_t key[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) key[u] = j0 + u < n_dead ? key_at(j0 + u) : 0u;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (key[u]) atomicAdd(&hist[lane][key[u] >> 8], 1u);
   }
   __syncthreads();
   if (tid < AUX_TB) {
@@ -78,9 +85,14 @@ __global__ void __launch_bounds__(256)
   // round 2: low byte inside the chosen high-byte bin
   for (int i = tid; i < AUX_TB * 257; i += blockDim.x) (&hist[0][0])[i] = 0u;
   __syncthreads();
-  for (int j = warp; j < n_dead; j += 8) {
-    const uint32_t key = key_at(j);
-    if (key && (key >> 8) == s_hi[lane]) atomicAdd(&hist[lane][key & 0xFFu], 1u);
+  for (int j0 = warp * 8; j0 < n_dead; j0 += 64) {
+    uint32_t key[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) key[u] = j0 + u < n_dead ? key_at(j0 + u) : 0u;
+    const uint32_t hi = s_hi[lane];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (key[u] && (key[u] >> 8) == hi) atomicAdd(&hist[lane][key[u] & 0xFFu], 1u);
   }
   __syncthreads();
   if (tid < AUX_TB) {
@@ -253,113 +265,16 @@ __global__ void aux_pack_kernel(const int32_t* __restrict__ list_j,
   }
 }
 
-// Per dead feature (blocks take them from a counter), over its entries in
-// token order: dpre = bf16(g_aux[b] . W_dec[f]) (the topk/relu backward of
-// the bf16 matmul), dW_enc[f] += dpre xc[b], db += dpre, dW_dec[f] += v g_aux[b].
-// Adds to the gradients of the main backward; db goes to db_full[f] for the
-// b_dec term. One row group of d/8 threads; 8 entries per chunk.
-template <int MAX_THREADS>
-__global__ void __launch_bounds__(MAX_THREADS)
-    aux_backward_kernel(const int32_t* __restrict__ offs, const uint64_t* __restrict__ vals,
-                        const int32_t* __restrict__ dead, int n_dead, int n_features,
-                        int64_t n_tokens,
-                        const bf16* __restrict__ g_aux, const bf16* __restrict__ xc,
-                        const bf16* __restrict__ w_dec, int d, float* __restrict__ g_wdec,
-                        float* __restrict__ g_wenc, float* __restrict__ g_benc,
-                        float* __restrict__ db_full, int* __restrict__ counter) {
-  __shared__ int s_f[2];
-  __shared__ float s_red[32][8];
-  __shared__ float s_gf[8];
-  const int tid = threadIdx.x, lane = tid & 31, wig = tid >> 5;
-  const int nwg = (blockDim.x + 31) >> 5;
-  const int nvec = d / 8;
-  const bool has = tid < nvec;
-  const uint4* ga_v = reinterpret_cast<const uint4*>(g_aux) + tid;
-  const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + tid;
-  int it = 0;
-  while (true) {
-    if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
-    __syncthreads();
-    const int jd = s_f[it & 1];
-    ++it;
-    if (jd >= n_dead) break;
-    const int f = min(max(dead[jd], 0), n_features - 1);
-    const int s = offs[jd], e = offs[jd + 1];
-    float wf[8];
-    if (has) unpack8(__ldg(reinterpret_cast<const uint4*>(w_dec) + static_cast<size_t>(f) * nvec + tid), wf);
-    float ad[8], ae[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ad[j] = ae[j] = 0.f;
-    float db = 0.f;
-    for (int i0 = s; i0 < e; i0 += 8) {
-      const int n = min(8, e - i0);
-      int t[8];
-      float v[8], part[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const uint64_t pv = r < n ? vals[i0 + r] : 0ull;
-        const int64_t tv = static_cast<int64_t>(pv >> 32);
-        t[r] = static_cast<int>(tv < n_tokens ? tv : n_tokens - 1);
-        v[r] = __uint_as_float(static_cast<uint32_t>(pv));
-      }
-      uint4 gu[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r)
-        gu[r] = (has && r < n) ? __ldg(ga_v + static_cast<size_t>(t[r]) * nvec)
-                               : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        float g8[8];
-        unpack8(gu[r], g8);
-        float a = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) a = fmaf(g8[j], has ? wf[j] : 0.f, a);
-        part[r] = a;
-      }
-      const float q = warp_sum8(part, lane);
-      if ((lane & 3) == 0) s_red[wig][lane >> 2] = q;
-      __syncthreads();
-      if (tid < 8) {
-        float a = 0.f;
-        for (int w = 0; w < nwg; ++w) a += s_red[w][tid];
-        s_gf[tid] = bf16_round(a);
-      }
-      __syncthreads();
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        if (r < n) {
-          const float dp = s_gf[r];
-          db += dp;
-          if (has) {
-            float g8[8], x8[8];
-            unpack8(gu[r], g8);
-            unpack8(__ldg(xc_v + static_cast<size_t>(t[r]) * nvec), x8);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              ad[j] = fmaf(v[r], g8[j], ad[j]);
-              ae[j] = fmaf(dp, x8[j], ae[j]);
-            }
-          }
-        }
-      }
-    }
-    if (has && e > s) {
-      const size_t o = static_cast<size_t>(f) * d + tid * 8;
-      if (g_wdec != nullptr) {
-        float4* p = reinterpret_cast<float4*>(g_wdec + o);
-        const float4 u = p[0], w = p[1];
-        p[0] = make_float4(u.x + ad[0], u.y + ad[1], u.z + ad[2], u.w + ad[3]);
-        p[1] = make_float4(w.x + ad[4], w.y + ad[5], w.z + ad[6], w.w + ad[7]);
-      }
-      float4* p = reinterpret_cast<float4*>(g_wenc + o);
-      const float4 u = p[0], w = p[1];
-      p[0] = make_float4(u.x + ae[0], u.y + ae[1], u.z + ae[2], u.w + ae[3]);
-      p[1] = make_float4(w.x + ae[4], w.y + ae[5], w.z + ae[6], w.w + ae[7]);
-    }
-    if (tid == 0) {
-      if (e > s) g_benc[f] += db;
-      db_full[f] = db;
-    }
+// Sorted aux entries -> the sampled backward's CSR format: token, and the
+// bf16 value (exact: it is a relu'd bf16 pre-activation) flagged active.
+__global__ void aux_unpack_kernel(const uint64_t* __restrict__ vals, const int32_t* __restrict__ offs,
+                                  int n_dead, int* __restrict__ csr_tok,
+                                  uint32_t* __restrict__ csr_val) {
+  const int total = offs[n_dead];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint64_t v = vals[i];
+    csr_tok[i] = static_cast<int>(v >> 32);
+    csr_val[i] = (static_cast<uint32_t>(v) >> 16) | CSR_ACTIVE;
   }
 }
 

@@ -273,6 +273,37 @@ bool tc_eligible(int64_t d, int64_t F, int force_simt) {
   return di.major == 10 && d % TILE_K == 0 && F % TILE_M == 0 && d <= 65536;
 }
 
+// The sampled backward over a feature-major CSR: one feature (segment) per
+// block of d / (8 U) threads (U = 2 for wide rows: more features in flight
+// per SM). seg_rows maps segments to feature rows (the aux backward).
+void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const bf16* go,
+                    const bf16* xc, const bf16* w_dec, const float* theta, int n_seg,
+                    int n_tokens, int d, float eps, int accumulate, float* g_wdec, float* g_wenc,
+                    float* g_logthr, float* g_benc, float* db_enc, int* counter,
+                    const SaeB200StepStats* stats, const int* seg_rows, int honor_overflow,
+                    cudaStream_t stream) {
+  const int nvec = d / 8;
+  const int U = (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
+  const int bthr = (nvec / U + 31) / 32 * 32;
+  const int per_sm = bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1);
+  const int grid = device_info().sm_count * per_sm * 2;
+#define SAE_SAMPLED(CC, UU, MT, MB)                                                            \
+  sampled_backward_kernel<CC, UU, MT, MB><<<grid, bthr, 0, stream>>>(                         \
+      offs, tok, val, go, xc, w_dec, theta, n_seg, n_tokens, d, eps, accumulate, g_wdec,       \
+      g_wenc, g_logthr, g_benc, db_enc, counter, stats, seg_rows, honor_overflow)
+  if (U == 1) {
+    if (bthr <= 192) SAE_SAMPLED(2, 1, 192, 4);
+    else if (bthr <= 256) SAE_SAMPLED(4, 1, 256, 2);
+    else if (bthr <= 512) SAE_SAMPLED(4, 1, 512, 1);
+    else SAE_SAMPLED(4, 1, 1024, 1);
+  } else {
+    if (bthr <= 192) SAE_SAMPLED(2, 2, 192, 2);
+    else if (bthr <= 256) SAE_SAMPLED(2, 2, 256, 2);
+    else SAE_SAMPLED(2, 2, 512, 1);
+  }
+#undef SAE_SAMPLED
+}
+
 // Launch the feature x token tile GEMM W [F, d] . T [B, d]^T with epilogue e.
 // aux: the [B, F]-sized bf16 tensor the epilogue reads (AUX_LOAD) or writes
 // (AUX_STORE) through the 64 KiB side tile: token-major [B, F], or
@@ -862,25 +893,26 @@ int sae_b200_aux_backward(const SaeB200Model* model, const SaeB200Grads* grads,
       cudaSuccess)
     return fail(SAE_ERR_CUDA, "aux scan failed");
   g_launches.fetch_add(1, std::memory_order_relaxed);
-  // 2. per dead feature: dpre, dW_enc, dW_dec, b_enc
+  // 2. per dead feature: dpre, dW_enc, dW_dec, b_enc -- the sampled backward's
+  //    kernel over the aux entries (all "active", no STE band), adding to the
+  //    main step's gradients; its db goes to db_full for the b_dec term
   if (cudaMemsetAsync(db_full, 0, F * sizeof(float), stream) != cudaSuccess ||
       cudaMemsetAsync(counter, 0, sizeof(int), stream) != cudaSuccess)
     return fail(SAE_ERR_CUDA, "aux reset failed");
-  const int V = vec_threads(d);
-#define SAE_AUX_BWD(MT)                                                                        \
-  aux_backward_kernel<MT><<<device_info().sm_count * std::max(1, 2048 / V), V, 0, stream>>>(   \
-      offs, vals1, aux->dead, n_dead, static_cast<int>(F), B,                                   \
-      reinterpret_cast<const bf16*>(at(A.g_aux)), w.xc,                                         \
-      static_cast<const bf16*>(model->W_dec_bf16), static_cast<int>(d),                         \
-      cfg->train_decoder ? grads->W_dec_fm : nullptr, grads->W_enc, grads->b_enc, db_full,      \
-      counter)
-  if (V <= 512) SAE_AUX_BWD(512);
-  else SAE_AUX_BWD(1024);
-#undef SAE_AUX_BWD
-  SAE_TRY(check_launch("aux_backward_kernel"));
+  int* tok2 = reinterpret_cast<int*>(keys0);          // free after the sort
+  uint32_t* val2 = reinterpret_cast<uint32_t*>(vals0);
+  aux_unpack_kernel<<<grid_for(items, 256), 256, 0, stream>>>(vals1, offs, n_dead, tok2, val2);
+  SAE_TRY(check_launch("aux_unpack_kernel"));
+  launch_sampled(offs, tok2, val2, reinterpret_cast<const bf16*>(at(A.g_aux)), w.xc,
+                 static_cast<const bf16*>(model->W_dec_bf16), w.theta, n_dead,
+                 static_cast<int>(B), static_cast<int>(d), cfg->ste_bandwidth, 1,
+                 cfg->train_decoder ? grads->W_dec_fm : nullptr, grads->W_enc,
+                 grads->log_threshold, grads->b_enc, db_full, counter, nullptr, aux->dead, 0,
+                 stream);
+  SAE_TRY(check_launch("sampled_backward_kernel (aux)"));
   // 3. b_dec: minus the aux encoder term -(sum dpre_aux) W_enc
   float* gemv_part = reinterpret_cast<float*>(at(A.gemv_part));
-  bdec_gemv_kernel<<<GEMV_GRID, V, 0, stream>>>(
+  bdec_gemv_kernel<<<GEMV_GRID, vec_threads(d), 0, stream>>>(
       db_full, static_cast<const bf16*>(model->W_enc_bf16), static_cast<int>(F),
       static_cast<int>(d), gemv_part);
   SAE_TRY(check_launch("bdec_gemv_kernel"));
@@ -1074,31 +1106,13 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
         w.pre, w.sbits, w.theta, w.col_offs, static_cast<int>(F), B,
         static_cast<int>(pre_pitch(B)), cfg->ste_bandwidth, stats, w.csr_tok, w.csr_val);
     SAE_TRY(check_launch("csr_fill_kernel"));
-    // 2. sampled grad_feat + STE + weight gradients, one feature per block of
-    //    d / (8 U) threads (U = 2 for wide rows: more features in flight per SM)
-    const int nvec = static_cast<int>(d / 8);
-    const int U = (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
-    const int bthr = (nvec / U + 31) / 32 * 32;
-    const int per_sm = bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1);
-    const int grid = device_info().sm_count * per_sm * 2;
+    // 2. sampled grad_feat + STE + weight gradients, one feature per block
     timer_begin(SAE_KERNEL_GRAD_GEMM, stream);
-#define SAE_SAMPLED(CC, UU, MT, MB)                                                            \
-  sampled_backward_kernel<CC, UU, MT, MB><<<grid, bthr, 0, stream>>>(                         \
-      w.col_offs, w.csr_tok, w.csr_val, w.go, w.xc,                                           \
-      static_cast<const bf16*>(model->W_dec_bf16), w.theta, static_cast<int>(F),               \
-      static_cast<int>(B), static_cast<int>(d), cfg->ste_bandwidth, acc, g_wdec, grads->W_enc,  \
-      grads->log_threshold, grads->b_enc, w.db_enc, w.counters, stats)
-    if (U == 1) {
-      if (bthr <= 192) SAE_SAMPLED(2, 1, 192, 4);
-      else if (bthr <= 256) SAE_SAMPLED(4, 1, 256, 2);
-      else if (bthr <= 512) SAE_SAMPLED(4, 1, 512, 1);
-      else SAE_SAMPLED(4, 1, 1024, 1);
-    } else {
-      if (bthr <= 192) SAE_SAMPLED(2, 2, 192, 2);
-      else if (bthr <= 256) SAE_SAMPLED(2, 2, 256, 2);
-      else SAE_SAMPLED(2, 2, 512, 1);
-    }
-#undef SAE_SAMPLED
+    launch_sampled(w.col_offs, w.csr_tok, w.csr_val, w.go, w.xc,
+                   static_cast<const bf16*>(model->W_dec_bf16), w.theta, static_cast<int>(F),
+                   static_cast<int>(B), static_cast<int>(d), cfg->ste_bandwidth, acc, g_wdec,
+                   grads->W_enc, grads->log_threshold, grads->b_enc, w.db_enc, w.counters, stats,
+                   nullptr, 1, stream);
     const int rc = check_launch("sampled_backward_kernel");
     timer_end(SAE_KERNEL_GRAD_GEMM, stream);
     SAE_TRY(rc);

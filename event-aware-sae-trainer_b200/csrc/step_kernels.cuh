@@ -660,9 +660,13 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
                             int d, float eps, int accumulate, float* __restrict__ g_wdec,
                             float* __restrict__ g_wenc, float* __restrict__ g_logthr,
                             float* __restrict__ g_benc, float* __restrict__ db_enc,
-                            int* __restrict__ counter, const SaeB200StepStats* stats) {
-  // thread tid owns columns [8 U tid, 8 U tid + 8 U): U consecutive 16-byte vectors
-  if (stats->csr_overflow) return;
+                            int* __restrict__ counter, const SaeB200StepStats* stats,
+                            const int* __restrict__ seg_rows = nullptr,
+                            int honor_overflow = 1) {
+  // thread tid owns columns [8 U tid, 8 U tid + 8 U): U consecutive 16-byte vectors.
+  // Segment sg of the CSR holds feature seg_rows[sg] (feature sg without seg_rows):
+  // the aux-loss backward runs the same kernel over the dead features' entries.
+  if (honor_overflow && stats != nullptr && stats->csr_overflow) return;
   __shared__ int s_f[2];
   __shared__ float s_red[2][32][C];   // [chunk parity][warp][entry]
   const int tid = threadIdx.x;
@@ -670,17 +674,18 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
   const int nw = (blockDim.x + 31) >> 5;
   const int nvec = d / 8;
   const bool has = (tid + 1) * U <= nvec;
-  const float gate_grad = stats->gate_grad;
+  const float gate_grad = stats != nullptr ? stats->gate_grad : 0.f;   // (band entries only)
   const uint4* go_v = reinterpret_cast<const uint4*>(go) + U * tid;
   const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + U * tid;
   int it = 0, par = 0;
   while (true) {
     if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
     __syncthreads();
-    const int f = s_f[it & 1];
+    const int sg = s_f[it & 1];
     ++it;
-    if (f >= n_features) break;
-    const int s = col_offs[f], e = col_offs[f + 1];
+    if (sg >= n_features) break;
+    const int s = col_offs[sg], e = col_offs[sg + 1];
+    const int f = seg_rows != nullptr ? seg_rows[sg] : sg;
     float wf[8 * U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
