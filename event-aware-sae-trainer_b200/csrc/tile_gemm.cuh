@@ -674,16 +674,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
       e.begin_half(h);
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * TILE_N);
-#pragma unroll 1
-      for (int c = c_begin; c < c_end; c += 32) {
-        float v[32];
-        tmem_ld_32cols(t_row + c, v);
-        if (c == c_end - 32) {
+      // the 4 chunks of the half, with the TMEM load of chunk i + 1 in flight
+      // while chunk i is processed
+      uint32_t r0[32], r1[32];
+      tmem_ld32_issue(t_row + c_begin, r0);
+      tmem_ld32_wait(r0);
+#pragma unroll
+      for (int i = 0; i < (TILE_N / 2) / 32; ++i) {
+        const int c = c_begin + 32 * i;
+        uint32_t(&cur)[32] = (i & 1) ? r1 : r0;
+        uint32_t(&nxt)[32] = (i & 1) ? r0 : r1;
+        if (i + 1 < (TILE_N / 2) / 32) {
+          tmem_ld32_issue(t_row + c + 32, nxt);
+        } else {
+          // every load of this accumulator has completed: the MMA warp may reuse it
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_remote(acc ? leader_acc_empty1 : leader_acc_empty0);
         }
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur[j]);
         e.chunk(c, v);
+        if (i + 1 < (TILE_N / 2) / 32) tmem_ld32_wait(nxt);
       }
       e.end_half(h);
       if (AUX == AUX_LOAD) {
