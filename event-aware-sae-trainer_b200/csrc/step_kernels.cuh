@@ -1131,13 +1131,34 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
   const uint4* wv = reinterpret_cast<const uint4*>(w_enc) + tid;
-  for (int f = blockIdx.x; f < n_features; f += gridDim.x) {
-    const float s = db_enc[f];
-    if (s == 0.f) continue;
+  // 8 rows in flight per thread; a zero coefficient (feature without active
+  // tokens) skips its row's load but keeps the fixed summation order
+  int f = blockIdx.x;
+  for (; f + 7 * static_cast<int>(gridDim.x) < n_features; f += 8 * gridDim.x) {
+    float sc[8];
+    uint4 u[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int fr = f + r * gridDim.x;
+      sc[r] = db_enc[fr];
+      u[r] = sc[r] != 0.f ? __ldg(wv + static_cast<size_t>(fr) * nvec) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (sc[r] == 0.f) continue;
+      float wf[8];
+      unpack8(u[r], wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = fmaf(sc[r], wf[j], acc[j]);
+    }
+  }
+  for (; f < n_features; f += gridDim.x) {
+    const float sc = db_enc[f];
+    if (sc == 0.f) continue;
     float wf[8];
     unpack8(__ldg(wv + static_cast<size_t>(f) * nvec), wf);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = fmaf(s, wf[j], acc[j]);
+    for (int j = 0; j < 8; ++j) acc[j] = fmaf(sc, wf[j], acc[j]);
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) part[static_cast<size_t>(blockIdx.x) * d + tid * 8 + j] = acc[j];

@@ -203,3 +203,48 @@ def test_two_gpu_shards_match_oracle(tmp_path, exchange):
         assert np.abs(got[k] - getattr(ref.params, k)).max() <= 2.5 * float(g["lr"]) + 1e-6, k
     stats = [json.loads((tmp_path / f"rank{r}.json").read_text()) for r in range(2)]
     assert stats[0]["l0"] == stats[1]["l0"] and stats[0]["grad_norm"] == stats[1]["grad_norm"]
+
+
+def test_peer_barrier_gives_up_and_reports_a_timeout():
+    """A rank whose peer never arrives: the exchange's flag barrier waits for a
+    flag nothing sets, gives up after its bounded wait (2 s), records
+    SAE_ERR_DEVICE_TIMEOUT in the device status word and returns; the host
+    sees the status, the context stays usable. One GPU: the "peer" is this
+    rank's own buffer mapped twice, so no other kernel is waited on."""
+    import ctypes
+    import math
+    import sae_b200
+    from sae_b200 import _lib as L
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    d, F, B = 128, 256, 256
+    sae = sae_b200.make_shard_sae(d, F, 0, 1, seed=1, device="cuda")
+    x = sae_b200.superposition_batch(B, d, 512, 8, math.log(8.0), 0.3, seed=3, device="cuda")
+    nbytes, ex, fl = ctypes.c_size_t(), ctypes.c_uint64(), ctypes.c_uint64()
+    L.call("sae_b200_peer_buffer_bytes", B, d, F, B * 64, ctypes.byref(nbytes), ctypes.byref(ex),
+           ctypes.byref(fl))
+    own = ctypes.c_void_p()
+    handle = (ctypes.c_uint8 * L.PEER_HANDLE_BYTES)()
+    L.call("sae_b200_peer_alloc", nbytes.value, ctypes.byref(own), handle)
+    try:
+        peers = L.Peers()
+        peers.rank, peers.world, peers.epoch = 0, 2, 1
+        peers.exchange_offset, peers.flags_offset = ex.value, fl.value
+        peers.base[0] = own.value
+        peers.base[1] = own.value
+        cfg = L.StepConfig(B, B * 64, 1e-3, 1e-2, 8.0, 0.2, 1, 0, 1, 0, 0)
+        stats = torch.zeros(L.STATS_FLOATS, device="cuda", dtype=torch.int32)
+        fired = torch.zeros(F, device="cuda", dtype=torch.uint8)
+        model = sae._model_struct(need_shadows=True)
+        L.call("sae_b200_shard_forward_p2p", ctypes.byref(model), L.ptr(x), L.DTYPE_BF16,
+               ctypes.byref(cfg), ctypes.byref(peers), L.ptr(stats), L.ptr(fired),
+               torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert L.device_status() == L.SAE_ERR_DEVICE_TIMEOUT   # read and cleared
+        assert L.device_status() == 0
+        # the context still works
+        y = torch.ones(4, device="cuda") * 2
+        assert float(y.sum()) == 8.0
+    finally:
+        torch.cuda.synchronize()
+        L.call("sae_b200_peer_free", own.value)
