@@ -47,9 +47,14 @@ D_IN, N_FEAT, TOKENS, K_TARGET = 1536, 49152, 32768, 50
 LAMBDA, MU, LR = 1e-3, 1e-2, 2e-4
 NORM_MU, NORM_SIGMA = math.log(60.0), 0.4
 POOL_BATCHES = 4
-# DRAM bytes per launch of the two tile GEMMs at 32768 tokens: an ncu capture of a
-# 4096-token launch (read + write) scaled by 8 (their traffic grows with the tokens).
-TRAFFIC_ENCODER_GEMM = 8 * (0.204492e9 + 0.418109e9)
+# DRAM bytes (read + write) per launch of the tile GEMMs at d=1536, F=49152, 32768
+# tokens. Encoder storing pre at the entries only (the default): a one-pass ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum) of a 32768-token launch of
+# this bench. Encoder storing all of pre, and the grad_feat GEMM: a 4096-token
+# launch scaled by 8 (their traffic is dominated by the [F, B] pre tensor, which
+# grows with the tokens).
+TRAFFIC_ENCODER_GEMM = 1.533931520e9 + 0.630690048e9
+TRAFFIC_ENCODER_GEMM_FULL_PRE = 8 * (0.204492e9 + 0.418109e9)
 TRAFFIC_GRAD_GEMM = 8 * (0.604495e9 + 0.014044e9)
 WORKLOAD = ("d_in=1536 F=49152 32768-token microbatch, L0~50, bf16 activations / "
             "fp32 master+Adam (Gemma-4-E2B residual shape)")
@@ -65,17 +70,63 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML
+    read every 10 ms on a side thread (read-only queries), so that a timed
+    region of a few tens of milliseconds still gets samples; nvidia-smi
+    (-lms 200) where NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_s: float = 0.01):
         self.index = index
+        self.period = period_s
         self.proc = None
+        self.thread = None
+        self.rows = []          # (sm_mhz, sm_max_mhz, {reason names})
+        self.error = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = getattr(torch.cuda.get_device_properties(self.index), "uuid", None)
+        if uuid is not None:
+            for key in (f"GPU-{uuid}", f"GPU-{uuid}".encode()):
+                try:
+                    return pynvml, pynvml.nvmlDeviceGetHandleByUUID(key)
+                except Exception:
+                    pass
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll(self, nv, h):
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        try:
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            while not self.stop.is_set():
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(sm), float(smax), {k for k, b in bits.items() if r & b}))
+                self.stop.wait(self.period)
+        except Exception as e:      # reported in the summary
+            self.error = f"{type(e).__name__}: {e}"
 
     def __enter__(self):
+        import threading
+        self.stop = threading.Event()
+        try:
+            nv, h = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            self.thread.start()
+            return self
+        except Exception as e:
+            self.error = f"{type(e).__name__}: {e}"
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
@@ -86,30 +137,33 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                out, _ = self.proc.communicate(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
+                out, _ = self.proc.communicate()
+            for line in (out or "").strip().splitlines():
+                p = [x.strip() for x in line.split(",")]
+                if len(p) >= 9 and p[1].replace(".", "").isdigit():
+                    self.rows.append((float(p[1]), float(p[2]),
+                                      {n for i, n in enumerate(self.NAMES) if p[5 + i] == "Active"}))
         return False
 
     def summary(self):
-        rows = []
-        for line in (self.out or "").strip().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        smax = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": reasons, "samples": len(rows)}
+        src = "nvml" if self.thread is not None else "nvidia-smi"
+        if self.error:
+            src += f" ({self.error})"
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "source": src}
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows),
+                "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": sorted(set().union(*(r[2] for r in self.rows))),
+                "samples": len(self.rows), "source": src}
 
 
 # ------------------------------------------------------------- CPU oracle
@@ -314,8 +368,8 @@ def run_inference(args):
             "config": {"workload": wl["description"], "d_in": d, "n_features": F,
                        "tokens_per_step": tokens, "l0_measured": l0,
                        "parallelism": f"replicas only: {world} independent GPU(s)",
-                       "l2": "inputs alternate between two 302 MB batches; each step writes the "
-                             "8.6 GB pre-activation tensor"},
+                       "l2": "inputs alternate between two 302 MB batches, each larger than "
+                             "the 126 MB L2"},
             "roofline": {"bound": "hbm", "kernel": "gathered decode (decode_kernel)",
                          "achieved": dec_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": dec_gbs / peaks["hbm_gbs"],
@@ -410,7 +464,8 @@ def run_b200(args):
         fs = sae_b200.ShardedFusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat,
                                        exchange=args.exchange)
     else:
-        fs = sae_b200.FusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat)
+        fs = sae_b200.FusedStep(sae, opt, max_tokens=tokens, grad_feat=args.grad_feat,
+                                pre_store=args.pre_store)
 
     aux_dead, aux_k = None, 0
     if args.aux_dead > 0 and not sharded:
@@ -516,9 +571,11 @@ def run_b200(args):
         grad_tf = gemm_flop / (grad_ms / 1e3) / 1e12
         traffic_scale = (d * F) / (D_IN * N_FEAT) * (tokens / TOKENS)
         gemm_bwd = args.grad_feat == "gemm"
+        entries = fs.pre_store == "entries" and not gemm_bwd and aux_dead is None
         dom_ms, dom_tf, dom_name, dom_traffic = (
             (enc_ms, enc_tf, "encoder tile GEMM (tcgen05 cta_group::2) + JumpReLU epilogue",
-             TRAFFIC_ENCODER_GEMM) if (enc_ms >= grad_ms or not gemm_bwd) else
+             TRAFFIC_ENCODER_GEMM if entries else TRAFFIC_ENCODER_GEMM_FULL_PRE)
+            if (enc_ms >= grad_ms or not gemm_bwd) else
             (grad_ms, grad_tf, "grad_feat tile GEMM (tcgen05 cta_group::2) + STE epilogue",
              TRAFFIC_GRAD_GEMM))
         peak = peaks["bf16_sustained"]
@@ -548,9 +605,9 @@ def run_b200(args):
                        "threshold_calibrated": thr,
                        "threshold_control": "proportional log-threshold nudge after each step "
                                             "(the trainer's L0 controller)",
-                       "l2": "inputs rotate over a 4-batch pool; every step writes the "
-                             f"{2 * tokens * F / 1e9:.1f} GB bf16 pre-activation tensor, which "
-                             "flushes the 126 MB L2",
+                       "l2": "inputs rotate over a 4-batch pool; every step's Adam pass "
+                             f"streams {30 * (2 * d * F + 2 * F + d) / 1e9:.1f} GB of parameters, "
+                             "gradients and moments, which flushes the 126 MB L2",
                        "dense_gemm_flop_per_token": dense_per_token,
                        "backward": ("dense tcgen05 grad_feat GEMM + STE epilogue, sparse CSR "
                                     "weight gradients: 4*d*F dense FLOP/token" if gemm_bwd else
@@ -562,9 +619,14 @@ def run_b200(args):
                          "frac": dom_tf / peak,
                          "peak_source": f"bf16_tflops_sustained ({peaks['src']})",
                          "traffic": dom_traffic * traffic_scale,
-                         "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
-                                         "4096-token d=1536 F=49152 launch, scaled by tokens "
-                                         "and by d*F",
+                         "traffic_note": ("ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                          "of one 32768-token d=1536 F=49152 launch (pre stored "
+                                          "at the entries only)" if entries else
+                                          "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                                          "4096-token d=1536 F=49152 launch, scaled by 8")
+                                         + ("" if traffic_scale == 1 else
+                                            f", scaled by tokens and d*F (x{traffic_scale:.3g})"),
+                         "pre_store": "entries" if entries else "full",
                          "per_launch_flop": gemm_flop, "launch_ms": dom_ms},
             "kernels": ({"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
                          "grad_gemm_ms": grad_ms, "grad_gemm_tflops": grad_tf} if gemm_bwd else
@@ -624,6 +686,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per step (default: the workload's); smaller values are for "
                          "profiler captures, not for the reported metric")
+    ap.add_argument("--pre-store", choices=["entries", "full"], default="entries",
+                    help="encoder stores pre only in the 32-token words holding a backward "
+                         "entry (default), or all of it")
     ap.add_argument("--grad-feat", choices=["sampled", "gemm"], default="sampled",
                     help="backward: grad_feat on the active + in-band entries only (default), "
                          "or the dense tcgen05 grad_feat GEMM")

@@ -547,6 +547,28 @@ int forward_checks(const SaeB200Model* model, const void* x, int x_dtype,
   return SAE_OK;
 }
 
+// The encoder GEMM with the JumpReLU epilogue, storing pre as PRE says.
+template <int PRE>
+int launch_encoder(const SaeB200Model* model, const ForwardCtx& c, int* tile_band,
+                   uint32_t* sbits, float eps, bool use_tc, cudaStream_t stream) {
+  const Ws& w = c.w;
+  EncodeEpiT<PRE> e{};
+  e.theta = w.theta;
+  e.b_enc = model->b_enc;
+  e.pre = w.pre;
+  e.mask = w.mask;
+  e.tile_cnt = w.tile_cnt;
+  e.tile_band = tile_band;
+  e.sbits = sbits;
+  e.eps = eps;
+  e.n_tokens = static_cast<int>(c.B);
+  e.n_features = static_cast<int>(c.F);
+  e.mask_words = c.mask_words;
+  e.ldp = static_cast<int>(pre_pitch(c.B));
+  return launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), w.xc, c.F, c.B, c.d, e,
+                          use_tc, stream, SAE_KERNEL_ENCODER_GEMM, w.pre);
+}
+
 // theta, xc, encoder GEMM + JumpReLU epilogue, per-feature scans -> CSR offsets.
 int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
                    const SaeB200StepConfig* cfg, const ForwardCtx& c, SaeB200StepStats* stats,
@@ -568,24 +590,13 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
     SAE_TRY(check_launch("prep_kernel"));
   }
   // 2. encoder GEMM + JumpReLU epilogue
-  {
-    EncodeEpi e{};
-    e.theta = w.theta;
-    e.b_enc = model->b_enc;
-    e.pre = w.pre;
-    e.mask = w.mask;
-    e.tile_cnt = w.tile_cnt;
-    e.tile_band = sampled ? w.tile_band : nullptr;
-    e.sbits = sampled ? w.sbits : nullptr;
-    e.eps = cfg->ste_bandwidth;
-    e.n_tokens = static_cast<int>(B);
-    e.n_features = static_cast<int>(F);
-    e.mask_words = c.mask_words;
-    e.ldp = static_cast<int>(pre_pitch(B));
-    SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), w.xc, F, B, d, e,
-                             tc_eligible(d, F, cfg->force_simt), stream, SAE_KERNEL_ENCODER_GEMM,
-                             w.pre));
-  }
+  if (sampled && cfg->pre_entries_only)
+    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, w.tile_band, w.sbits, cfg->ste_bandwidth,
+                                        tc_eligible(d, F, cfg->force_simt), stream));
+  else
+    SAE_TRY(launch_encoder<PRE_FULL>(model, c, sampled ? w.tile_band : nullptr,
+                                     sampled ? w.sbits : nullptr, cfg->ste_bandwidth,
+                                     tc_eligible(d, F, cfg->force_simt), stream));
   // 3. per-feature scans -> CSR offsets (active entries, plus the inactive
   //    in-band ones for the sampled backward)
   scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(
@@ -694,18 +705,10 @@ int sae_b200_encode_decode(const SaeB200Model* model, const void* x, int x_dtype
                                                 model->log_threshold, w.theta, w.xc, B,
                                                 static_cast<int>(d), static_cast<int>(F));
     SAE_TRY(check_launch("prep_kernel"));
-    EncodeEpi e{};
-    e.theta = w.theta;
-    e.b_enc = model->b_enc;
-    e.pre = w.pre;
-    e.mask = w.mask;
-    e.tile_cnt = w.tile_cnt;
-    e.n_tokens = static_cast<int>(B);
-    e.n_features = static_cast<int>(F);
-    e.mask_words = c.mask_words;
-    e.ldp = static_cast<int>(pre_pitch(B));
-    SAE_TRY(launch_tile_gemm(static_cast<const bf16*>(model->W_enc_bf16), w.xc, F, B, d, e,
-                             tc_eligible(d, F, 0), stream, SAE_KERNEL_ENCODER_GEMM, w.pre));
+    // pre is stored only in the 32-token words holding an active entry: the
+    // decode reads it there and nowhere else
+    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, nullptr, nullptr, 0.f, tc_eligible(d, F, 0),
+                                        stream));
   }
   if (fired != nullptr) {
     scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(w.tile_cnt, w.col_tot, fired,
@@ -815,6 +818,9 @@ int sae_b200_aux_forward(const SaeB200Model* model, const void* x, int x_dtype,
   ForwardCtx c;
   SAE_TRY(forward_checks(model, x, x_dtype, cfg, workspace, workspace_bytes, stats, x_hat, &c));
   if (x_hat == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "aux needs the forward's x_hat");
+  if (cfg->pre_entries_only && cfg->grad_feat_gemm == 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT,
+                "the aux loss reads the dead features' pre: run the forward with pre_entries_only = 0");
   AuxLayout A;
   SAE_TRY(check_aux(model, cfg, aux, aux_ws, aux_bytes, &A));
   auto at = [&](size_t o) { return static_cast<uint8_t*>(aux_ws) + o; };
@@ -1088,6 +1094,9 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
     return fail(SAE_ERR_INVALID_ARGUMENT, "gradient pointer is NULL");
   if (cfg->train_decoder && grads->W_dec_fm == nullptr)
     return fail(SAE_ERR_INVALID_ARGUMENT, "W_dec gradient is NULL with train_decoder set");
+  if (dense_scratch != nullptr && cfg->pre_entries_only && cfg->grad_feat_gemm == 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT,
+                "the dense backward reads all of pre: run the forward with pre_entries_only = 0");
   const int64_t B = cfg->n_tokens, d = model->d_in, F = model->n_features;
   const Layout L = make_layout(B, d, F, cfg->csr_capacity);
   SAE_TRY(check_ws(L, workspace, workspace_bytes));

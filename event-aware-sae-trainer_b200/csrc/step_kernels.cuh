@@ -142,8 +142,20 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
 // float(pre) > theta. Stores pre, one 32-feature mask word per token per
 // warp, and the active-token count of each feature in each 128-token half of
 // the tile (the unit the epilogue warps split a tile into).
-struct EncodeEpi {
-  static constexpr int kAux = AUX_STORE;   // pre goes out through a TMA store
+// What the encoder epilogue stores of pre:
+//   PRE_FULL     every element, through the side tile's TMA store (the dense
+//                backward and the aux loss read all of it)
+//   PRE_ENTRIES  only the 32-token words of a feature that hold an active or
+//                in-band entry (direct 64-byte stores): the decode reads pre
+//                at the active entries and the CSR fill at the sampled-
+//                backward entries, nothing else reads it. Of the d=1536,
+//                F=49152, L0~50 step's 3.2 GB of pre, a few percent is stored.
+constexpr int PRE_FULL = 0;
+constexpr int PRE_ENTRIES = 1;
+
+template <int PRE>
+struct EncodeEpiT {
+  static constexpr int kAux = PRE == PRE_FULL ? AUX_STORE : AUX_NONE;
   static constexpr bool kAuxFeatureMajor = true;
   const float* theta;
   const float* b_enc;
@@ -224,7 +236,7 @@ struct EncodeEpi {
       for (int q = 0; q < 4; ++q)
         *reinterpret_cast<uint4*>(base + aux_fm_offset(row, (c >> 3) + q)) =
             make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-    } else if (row_ok) {
+    } else if (row_ok && (PRE == PRE_FULL || (aw | sword) != 0u)) {
       bf16* dst = pre + static_cast<size_t>(f) * ldp + t0;
 #pragma unroll
       for (int q = 0; q < 4; ++q)
@@ -245,6 +257,7 @@ struct EncodeEpi {
   }
   __device__ __forceinline__ void end_tile() {}
 };
+using EncodeEpi = EncodeEpiT<PRE_FULL>;
 
 // pre only, token-major [B, F] (module API encode_pre in bf16 mode).
 struct PreOnlyEpi {

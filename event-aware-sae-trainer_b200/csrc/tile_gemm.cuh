@@ -478,9 +478,12 @@ constexpr int TC2_STAGE_BYTES = TC2_A_BYTES + TC2_B_BYTES;
 
 template <int AUX>
 struct Tc2Config {
-  static constexpr int STAGES = AUX == AUX_NONE ? 6 : 5;
+  // as many 32 KiB stages as the 227 KiB of shared memory a CTA may use hold
+  static constexpr int STAGES = AUX == AUX_NONE ? 7 : 5;
   static constexpr size_t SMEM = STAGES * TC2_STAGE_BYTES +
                                  (AUX == AUX_NONE ? 0 : TC_AUX_BYTES) + TC_BARRIER_BYTES + 1024;
+  static_assert(SMEM <= 227 * 1024, "tile GEMM stages exceed the shared memory of a CTA");
+  static_assert((2 * STAGES + 10) * 8 + 8 <= TC_BARRIER_BYTES, "barrier area too small");
 };
 
 // Pair tile t -> (feature pair index, token tile), same grouping as tile_coord.
@@ -653,7 +656,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
       epi_phase ^= 1;
       return r;
     };
-    const int c_begin = h * (TILE_N / 2), c_end = c_begin + TILE_N / 2;
+    const int c_begin = h * (TILE_N / 2);
     int it = 0;
     bool ok = true;
     for (int t = pair; t < total && ok; t += pairs, ++it) {

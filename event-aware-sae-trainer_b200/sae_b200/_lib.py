@@ -74,6 +74,7 @@ class StepConfig(ctypes.Structure):
         ("train_decoder", c_int32),
         ("force_simt", c_int32),
         ("grad_feat_gemm", c_int32),
+        ("pre_entries_only", c_int32),
     ]
 
 

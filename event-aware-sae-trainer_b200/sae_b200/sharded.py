@@ -177,8 +177,11 @@ class ShardedFusedStep(FusedStep):
                  grad_feat: str = "sampled", exchange: str = "p2p",
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None,
                  rank: Optional[int] = None, world: Optional[int] = None):
+        # pre is stored in full: a shard whose CSR overflows takes the dense
+        # backward without redoing the forward (which holds the exchange that
+        # every rank takes together)
         super().__init__(sae, optimizer, max_tokens, csr_capacity=csr_capacity,
-                         force_simt=force_simt, grad_feat=grad_feat)
+                         force_simt=force_simt, grad_feat=grad_feat, pre_store="full")
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.group = group

@@ -171,7 +171,7 @@ class FusedStep:
 
     def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int,
                  csr_capacity: Optional[int] = None, force_simt: bool = False,
-                 grad_feat: str = "sampled"):
+                 grad_feat: str = "sampled", pre_store: str = "entries"):
         _require_cuda(sae.W_enc.weight)
         if not isinstance(optimizer, B200Adam) or optimizer.sae is not sae:
             raise TypeError("FusedStep needs the B200Adam built over the same SAE")
@@ -185,6 +185,13 @@ class FusedStep:
         # "sampled": grad_feat = go . W_dec[f] only where the backward uses it
         # (active entries and the STE band); "gemm": the dense tcgen05 product.
         self.grad_feat = grad_feat
+        if pre_store not in ("entries", "full"):
+            raise ValueError("pre_store must be 'entries' or 'full'")
+        # "entries": the encoder stores pre only in the 32-token words that hold
+        # an active or in-band entry (all the sampled backward reads); "full":
+        # all of it (for callers that read the workspace's pre). The aux loss and
+        # the dense backward need it all and get it whatever this says.
+        self.pre_store = pre_store
         dev = sae.W_enc.weight.device
         self.device = dev
         F, d = sae.n_features, sae.d_in
@@ -227,10 +234,12 @@ class FusedStep:
                        L.ptr(self.g_log_thr))
 
     def _cfg(self, n_tokens, accum_steps, first, lambda_l0, al_mu, target_l0) -> L.StepConfig:
+        entries = self.grad_feat == "sampled" and self.pre_store == "entries" and self._aux is None
         return L.StepConfig(int(n_tokens), self.csr_capacity, float(lambda_l0), float(al_mu),
                             float(target_l0), float(self.sae.ste_bandwidth), int(accum_steps),
                             0 if first else 1, 1 if self.sae.W_dec.weight.requires_grad else 0,
-                            1 if self.force_simt else 0, 1 if self.grad_feat == "gemm" else 0)
+                            1 if self.force_simt else 0, 1 if self.grad_feat == "gemm" else 0,
+                            1 if entries else 0)
 
     def set_aux(self, dead_indices: Optional[torch.Tensor], k: int = 0,
                 coeff: float = AUX_COEFF) -> None:
@@ -322,6 +331,13 @@ class FusedStep:
         grads = self._grads_struct()
         if st["csr_overflow"]:
             self.dense_fallbacks += 1
+            if cfg.pre_entries_only:
+                # the dense backward reads all of pre: redo the forward storing it
+                # (same kernels, same inputs: the same stats, x_hat and fired bits)
+                cfg.pre_entries_only = 0
+                L.call("sae_b200_train_forward", ctypes.byref(model), L.ptr(x), dt,
+                       ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
+                       L.ptr(x_hat_out), L.ptr(self.fired), stream)
             L.call("sae_b200_train_backward_dense", ctypes.byref(model), ctypes.byref(grads),
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
                    L.ptr(self._dense_scratch_for(n)), stream)

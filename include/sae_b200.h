@@ -85,6 +85,11 @@ typedef struct SaeB200StepConfig {
                               entries only (default); 1 = the dense tcgen05 grad_feat
                               GEMM with the STE epilogue. Same gradients; forward and
                               backward of a microbatch must use the same value. */
+  int32_t pre_entries_only; /* forward, sampled backward only: 1 = store pre only in the
+                              32-token words holding an active or in-band entry (all
+                              that the decode and the sampled backward read); 0 = store
+                              all of it, as sae_b200_train_backward_dense and
+                              sae_b200_aux_forward need (they refuse a cfg with 1). */
 } SaeB200StepConfig;
 
 /* Step statistics, written on the device; copy back with one memcpy. */

@@ -49,7 +49,7 @@ def setup():
         sae.log_threshold.fill_(math.log(q))
     opt = sae_b200.B200Adam(sae_b200.reference_param_groups(sae, 2e-4), lr=2e-4, sae=sae,
                             renorm=True)
-    fs = sae_b200.FusedStep(sae, opt, max_tokens=B)
+    fs = sae_b200.FusedStep(sae, opt, max_tokens=B, pre_store="full")
     x_hat = torch.empty(B, D, device=dev)
     st = fs.microbatch(x, lambda_l0=1e-3, al_mu=1e-2, target_l0=50, x_hat_out=x_hat)
     torch.cuda.synchronize()
@@ -168,6 +168,22 @@ def test_sampled_and_gemm_backward_agree_at_full_size(setup):
     del fs2
 
 
+def test_entries_only_pre_store_is_bit_identical_at_full_size(setup):
+    """The default forward stores pre only where an entry is; at the full
+    workload its statistics and gradients equal the full store's bit for bit."""
+    import sae_b200
+    sae, x, g = setup["sae"], setup["x"], setup["grads"]
+    fs3 = sae_b200.FusedStep(sae, setup["fs"].opt, max_tokens=B)
+    assert fs3.pre_store == "entries"
+    st3 = fs3.microbatch(x, lambda_l0=1e-3, al_mu=1e-2, target_l0=50)
+    torch.cuda.synchronize()
+    assert st3 == setup["st"]
+    for k, t in (("W_enc", fs3.g_W_enc), ("b_enc", fs3.g_b_enc), ("W_dec_fm", fs3.g_W_dec_fm),
+                 ("b_dec", fs3.g_b_dec), ("log_threshold", fs3.g_log_thr)):
+        assert torch.equal(t, g[k]), k
+    del fs3
+
+
 def test_step_is_deterministic_at_full_size(setup):
     fs, x, g = setup["fs"], setup["x"], setup["grads"]
     fs.microbatch(x, lambda_l0=1e-3, al_mu=1e-2, target_l0=50)
@@ -192,3 +208,4 @@ def test_adam_renorm_and_bf16_copies(setup):
                                   bf16(sae.W_enc.weight.detach()[rows].cpu().numpy()))
     np.testing.assert_array_equal(sae._shadow_dec[rows].float().cpu().numpy(),
                                   bf16(sae.W_dec.weight.detach().t()[rows].cpu().numpy()))
+

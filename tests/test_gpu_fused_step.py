@@ -37,7 +37,8 @@ def _rel(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def build(g, *, force_simt=False, csr_capacity=None, renorm=True, grad_feat="sampled"):
+def build(g, *, force_simt=False, csr_capacity=None, renorm=True, grad_feat="sampled",
+          pre_store="entries"):
     from sae_b200 import B200Adam, B200JumpReLUSAE, FusedStep, reference_param_groups
     d, F = int(g["d"]), int(g["F"])
     sae = B200JumpReLUSAE(d, F)
@@ -54,7 +55,7 @@ def build(g, *, force_simt=False, csr_capacity=None, renorm=True, grad_feat="sam
     n = int(g["n_micro"])
     B = g["x0"].shape[0]
     fs = FusedStep(sae, opt, max_tokens=B, csr_capacity=csr_capacity, force_simt=force_simt,
-                   grad_feat=grad_feat)
+                   grad_feat=grad_feat, pre_store=pre_store)
     return sae, opt, fs
 
 
@@ -118,7 +119,7 @@ CASES = [
 @pytest.mark.parametrize("name,force_simt", CASES)
 def test_forward_matches_oracle_and_active_set_is_exact(name, force_simt):
     g = load_golden(name)
-    sae, opt, fs = build(g, force_simt=force_simt)
+    sae, opt, fs = build(g, force_simt=force_simt, pre_store="full")
     x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
     cfg = oracle_cfg(g)
     st = fs.microbatch(x, accum_steps=1, first=True, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu,
@@ -286,7 +287,7 @@ def test_wide_rows_match_oracle(grad_feat):
     sae.ste_bandwidth = 0.05
     lr = 1e-4
     opt = B200Adam(reference_param_groups(sae, lr), lr=lr, sae=sae, renorm=True)
-    fs = FusedStep(sae, opt, max_tokens=B, grad_feat=grad_feat)
+    fs = FusedStep(sae, opt, max_tokens=B, grad_feat=grad_feat, pre_store="full")
     cfg = O.StepConfig(lambda_l0=1e-3, al_mu=1e-2, target_l0=8.0, ste_bandwidth=0.05,
                        lr=(lr,) * 4)
     xt = torch.from_numpy(x).cuda()
@@ -302,3 +303,46 @@ def test_wide_rows_match_oracle(grad_feat):
     for k, t in {"W_enc": fs.g_W_enc, "b_enc": fs.g_b_enc, "W_dec": fs.g_W_dec_fm.t(),
                  "b_dec": fs.g_b_dec, "log_threshold": fs.g_log_thr}.items():
         assert _rel(t.cpu().numpy(), getattr(ref, k)) < 5e-3, k
+
+
+@pytest.mark.parametrize("name,force_simt", CASES)
+def test_entries_only_pre_store_matches_full_store(name, force_simt):
+    """The default forward stores pre only in the 32-token words that hold an
+    active or in-band entry. Stats and gradients are bit-identical to the full
+    store, the stored words hold the same values, and no other word is touched
+    (the workspace's pre region starts as NaN)."""
+    g = load_golden(name)
+    cfg = oracle_cfg(g)
+    x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
+    B = x.shape[0]
+    runs = {}
+    for mode in ("full", "entries"):
+        sae, opt, fs = build(g, force_simt=force_simt, pre_store=mode)
+        F = sae.n_features
+        from sae_b200 import _lib as L
+        ldp = L.pre_pitch(B)
+        o = L.workspace_offsets(B, sae.d_in, F, fs.csr_capacity)["pre"]
+        fs.ws[o:o + 2 * F * ldp].fill_(255)          # bf16 0xFFFF: NaN
+        st = fs.microbatch(x, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu, target_l0=cfg.target_l0)
+        torch.cuda.synchronize()
+        assert L.device_status() == 0
+        grads = [t.clone() for t in (fs.g_W_enc, fs.g_b_enc, fs.g_W_dec_fm, fs.g_b_dec,
+                                     fs.g_log_thr)]
+        pre = fs.ws[o:o + 2 * F * ldp].view(torch.bfloat16).view(F, ldp)[:, :B]
+        runs[mode] = (st, grads, pre.float().cpu().numpy(), kernel_theta(fs, B), fs.fired.clone())
+    st_f, g_f, pre_f, theta, fired_f = runs["full"]
+    st_e, g_e, pre_e, _, fired_e = runs["entries"]
+    assert st_f == st_e
+    assert torch.equal(fired_f, fired_e)
+    for a, b in zip(g_f, g_e):
+        assert torch.equal(a, b)
+    assert not np.isnan(pre_f).any()
+    eps = np.float32(g["eps"])
+    entry = (pre_f - theta[:, None]) > -eps              # active or in band, fp32 as the kernel
+    F = entry.shape[0]
+    nw = (B + 31) // 32
+    pad = np.zeros((F, nw * 32), dtype=bool)
+    pad[:, :B] = entry
+    word = np.repeat(pad.reshape(F, nw, 32).any(-1), 32, axis=1)[:, :B]
+    np.testing.assert_array_equal(pre_e[word], pre_f[word])
+    assert np.isnan(pre_e[~word]).all()

@@ -35,6 +35,11 @@ def test_reconstruct_matches_oracle_forward(name, dtype):
     sae, opt, fs = build(g)
     x = torch.from_numpy(g["x0"].astype(np.float32)).to(dtype).cuda()
     fired = torch.zeros(sae.n_features, dtype=torch.uint8, device="cuda")
+    from sae_b200 import _lib as L
+    # pre is stored only in the 32-token words holding an active entry; the
+    # rest of the workspace stays NaN (bf16 0xFFFF), which no gate passes
+    need = L.workspace_bytes(x.shape[0], sae.d_in, sae.n_features, 0)
+    sae._infer_ws = torch.full((need,), 255, dtype=torch.uint8, device="cuda")
     x_hat, counts = sae.reconstruct(x, fired=fired)
     torch.cuda.synchronize()
     from sae_b200 import _lib as L
@@ -42,6 +47,14 @@ def test_reconstruct_matches_oracle_forward(name, dtype):
     theta, pre = _views(sae, x.shape[0])
     gate = pre > theta
     np.testing.assert_array_equal(counts.cpu().numpy(), gate.sum(1))
+    B = x.shape[0]
+    nw = (B + 31) // 32
+    pad_g = np.zeros((nw * 32, sae.n_features), dtype=bool)
+    pad_g[:B] = gate
+    pad_w = np.zeros((nw * 32, sae.n_features), dtype=bool)
+    pad_w[:B] = ~np.isnan(pre)
+    # a word is stored exactly when it holds an active entry
+    np.testing.assert_array_equal(pad_w.reshape(nw, 32, -1).any(1), pad_g.reshape(nw, 32, -1).any(1))
     assert fired.bool().cpu().numpy().tolist() == gate.any(0).tolist()
     fw = O.forward(x.float().cpu().numpy(), oracle_params(g), oracle_cfg(g), "bf16", theta=theta)
     assert _rel(x_hat.cpu().numpy(), fw.x_hat) < BF16_TOL

@@ -125,7 +125,7 @@ def test_emulated_shards_match_oracle_and_unsharded(world):
     for s in shards[1:]:
         assert torch.equal(s.b_dec, shards[0].b_dec)
     # unsharded reference pass on the same GPU
-    sae, opt, fs = build(g)
+    sae, opt, fs = build(g, pre_store="full")
     wf = float(g["wenc_factor"])
     one = fs.step(x, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu, target_l0=cfg.target_l0,
                   wenc_dampen=lambda l0: wf)
