@@ -13,7 +13,7 @@ using bf16 = __nv_bfloat16;
 
 // Fixed grid sizes: partial sums are reduced in a fixed order, so a given
 // input produces bit-identical results on every run and every B200.
-constexpr int DECODE_GRID = 1184;   // 148 SMs x 8
+constexpr int DECODE_GRID = 2368;   // 148 SMs x 16 (blocks of a few tokens: short tails)
 constexpr int GEMV_GRID = 296;
 constexpr int NORM_GRID = SAE_GRAD_NORM_WORKSPACE_BYTES / 4;
 constexpr int DECODE_LIST_CAP = 2048;   // active features staged per pass
