@@ -84,7 +84,7 @@ DeviceInfo device_info() {
 
 // ------------------------------------------------------------ workspace
 struct Layout {
-  size_t theta, xc, pre, sbits, mask, tile_cnt, tile_band, col_tot, col_act, col_offs, go, tok_sqerr,
+  size_t theta, xc, pre, sbits, mask, tile_cnt, col_tot, col_act, col_offs, go, tok_sqerr,
       tok_cnt, gosum_part, thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part,
       order_k0, order_k1, order_v0, order_v1, order_tmp, order_tmp_bytes, counters, total;
 };
@@ -122,9 +122,11 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   L.sbits = take(static_cast<size_t>(F) * (pre_pitch(B) / 32) * 4);
   L.mask = take(B * W * 4);
   L.tile_cnt = take(nT * F * 4);
-  L.tile_band = take(nT * F * 4);
-  L.col_tot = take(F * 4);
-  L.col_act = take(F * 4);
+  // per-feature totals, adjacent (one memset): col_tot [F + 1] (entry
+  // counts, then a 0 so that the exclusive scan of F + 1 ends in the total),
+  // col_act [F] (active counts)
+  L.col_tot = take((2 * F + 1) * 4);
+  L.col_act = L.col_tot + (F + 1) * 4;
   L.col_offs = take((F + 1) * 4);
   L.go = take(B * d * 2);
   L.tok_sqerr = take(B * 4);
@@ -148,8 +150,11 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
                                             static_cast<int*>(nullptr),
                                             static_cast<int*>(nullptr), static_cast<int>(B), 0,
                                             count_key_bits(F));
-  L.order_tmp_bytes = sort_bytes;
-  L.order_tmp = take(sort_bytes);
+  size_t scan_bytes = 0;   // the same scratch serves the CSR offset scan
+  cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int*>(nullptr),
+                                static_cast<int*>(nullptr), static_cast<int>(F + 1));
+  L.order_tmp_bytes = std::max(sort_bytes, scan_bytes);
+  L.order_tmp = take(L.order_tmp_bytes);
   L.counters = take(256);
   L.total = off;
   return L;
@@ -162,7 +167,6 @@ struct Ws {
   uint32_t* sbits;
   uint32_t* mask;
   int* tile_cnt;
-  int* tile_band;
   int* col_tot;
   int* col_act;
   int* col_offs;
@@ -192,7 +196,6 @@ Ws carve(void* base, const Layout& L) {
   w.sbits = reinterpret_cast<uint32_t*>(at(L.sbits));
   w.mask = reinterpret_cast<uint32_t*>(at(L.mask));
   w.tile_cnt = reinterpret_cast<int*>(at(L.tile_cnt));
-  w.tile_band = reinterpret_cast<int*>(at(L.tile_band));
   w.col_tot = reinterpret_cast<int*>(at(L.col_tot));
   w.col_act = reinterpret_cast<int*>(at(L.col_act));
   w.col_offs = reinterpret_cast<int*>(at(L.col_offs));
@@ -548,9 +551,12 @@ int forward_checks(const SaeB200Model* model, const void* x, int x_dtype,
 }
 
 // The encoder GEMM with the JumpReLU epilogue, storing pre as PRE says.
+// sbits: the sampled backward's entry bitmap (NULL: none); act_sum /
+// entry_sum: per-feature totals the epilogue adds to (NULL: per-tile active
+// counts into tile_cnt instead).
 template <int PRE>
-int launch_encoder(const SaeB200Model* model, const ForwardCtx& c, int* tile_band,
-                   uint32_t* sbits, float eps, bool use_tc, cudaStream_t stream) {
+int launch_encoder(const SaeB200Model* model, const ForwardCtx& c, uint32_t* sbits,
+                   int* act_sum, int* entry_sum, float eps, bool use_tc, cudaStream_t stream) {
   const Ws& w = c.w;
   EncodeEpiT<PRE> e{};
   e.theta = w.theta;
@@ -558,7 +564,8 @@ int launch_encoder(const SaeB200Model* model, const ForwardCtx& c, int* tile_ban
   e.pre = w.pre;
   e.mask = w.mask;
   e.tile_cnt = w.tile_cnt;
-  e.tile_band = tile_band;
+  e.act_sum = act_sum;
+  e.entry_sum = entry_sum;
   e.sbits = sbits;
   e.eps = eps;
   e.n_tokens = static_cast<int>(c.B);
@@ -590,23 +597,38 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
     SAE_TRY(check_launch("prep_kernel"));
   }
   // 2. encoder GEMM + JumpReLU epilogue
-  if (sampled && cfg->pre_entries_only)
-    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, w.tile_band, w.sbits, cfg->ste_bandwidth,
-                                        tc_eligible(d, F, cfg->force_simt), stream));
+  const bool use_tc = tc_eligible(d, F, cfg->force_simt);
+  if (!sampled) {
+    SAE_TRY(launch_encoder<PRE_FULL>(model, c, nullptr, nullptr, nullptr, cfg->ste_bandwidth,
+                                     use_tc, stream));
+    // per-feature scans of the per-tile counts -> CSR offsets of the active
+    // entries and each tile's start inside them (the GEMM backward's CSR fill)
+    scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(
+        w.tile_cnt, w.col_tot, fired, 2 * c.n_tiles, static_cast<int>(F));
+    SAE_TRY(check_launch("scan_columns_kernel"));
+    scan_offsets_kernel<<<1, 1024, 0, stream>>>(w.col_tot, w.col_offs, static_cast<int>(F),
+                                                cfg->csr_capacity, stats, w.counters);
+    return check_launch("scan_offsets_kernel");
+  }
+  // sampled backward: the epilogue adds each feature's active and entry
+  // counts straight into per-feature totals (integer atomics: exact)
+  if (cudaMemsetAsync(w.col_tot, 0, (2 * F + 1) * sizeof(int), stream) != cudaSuccess)
+    return fail(SAE_ERR_CUDA, "count reset failed");
+  if (cfg->pre_entries_only)
+    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, w.sbits, w.col_act, w.col_tot,
+                                        cfg->ste_bandwidth, use_tc, stream));
   else
-    SAE_TRY(launch_encoder<PRE_FULL>(model, c, sampled ? w.tile_band : nullptr,
-                                     sampled ? w.sbits : nullptr, cfg->ste_bandwidth,
-                                     tc_eligible(d, F, cfg->force_simt), stream));
-  // 3. per-feature scans -> CSR offsets (active entries, plus the inactive
-  //    in-band ones for the sampled backward)
-  scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(
-      w.tile_cnt, w.col_tot, fired, 2 * c.n_tiles, static_cast<int>(F),
-      sampled ? w.tile_band : nullptr, sampled ? w.col_act : nullptr);
-  SAE_TRY(check_launch("scan_columns_kernel"));
-  scan_offsets_kernel<<<1, 1024, 0, stream>>>(w.col_tot, w.col_offs, static_cast<int>(F),
-                                              cfg->csr_capacity, stats, w.counters,
-                                              sampled ? w.col_act : nullptr);
-  return check_launch("scan_offsets_kernel");
+    SAE_TRY(launch_encoder<PRE_FULL>(model, c, w.sbits, w.col_act, w.col_tot,
+                                     cfg->ste_bandwidth, use_tc, stream));
+  // 3. CSR offsets of the entries = exclusive scan of the totals
+  size_t tmp_bytes = w.order_tmp_bytes;
+  if (cub::DeviceScan::ExclusiveSum(w.order_tmp, tmp_bytes, w.col_tot, w.col_offs,
+                                    static_cast<int>(F + 1), stream) != cudaSuccess)
+    return fail(SAE_ERR_CUDA, "CSR offset scan failed");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  count_stats_kernel<<<1, 1024, 0, stream>>>(w.col_act, w.col_offs, static_cast<int>(F),
+                                             cfg->csr_capacity, stats, w.counters, fired);
+  return check_launch("count_stats_kernel");
 }
 
 // Gathered decode; partial != NULL writes the shard's decoder sums and counts
@@ -707,8 +729,8 @@ int sae_b200_encode_decode(const SaeB200Model* model, const void* x, int x_dtype
     SAE_TRY(check_launch("prep_kernel"));
     // pre is stored only in the 32-token words holding an active entry: the
     // decode reads it there and nowhere else
-    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, nullptr, nullptr, 0.f, tc_eligible(d, F, 0),
-                                        stream));
+    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, nullptr, nullptr, nullptr, 0.f,
+                                        tc_eligible(d, F, 0), stream));
   }
   if (fired != nullptr) {
     scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(w.tile_cnt, w.col_tot, fired,

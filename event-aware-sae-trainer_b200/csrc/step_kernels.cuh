@@ -164,11 +164,14 @@ struct EncodeEpiT {
   int* tile_cnt;
   // Sampled backward (optional): its entries are the (token, feature) pairs with
   // pre - theta > -eps, i.e. active (pre > theta) or inside the STE band
-  // |pre - theta| < eps. tile_band counts them per half tile; sbits
-  // [ldp / 32, F] holds one bit each (word w of feature f: tokens 32w..32w+31),
-  // so that the 32 features of an epilogue warp store one coalesced line.
-  int* tile_band;
+  // |pre - theta| < eps. sbits [ldp / 32, F] holds one bit each (word w of
+  // feature f: tokens 32w..32w+31), so that the 32 features of an epilogue warp
+  // store one coalesced line.
   uint32_t* sbits;
+  // per-feature totals (optional): with act_sum set, each half tile's counts
+  // are added to act_sum[f] / entry_sum[f] instead of stored per tile
+  int* act_sum;
+  int* entry_sum;
   float eps;
   int n_tokens, n_features, mask_words, ldp;
   // per-thread tile state
@@ -249,11 +252,13 @@ struct EncodeEpiT {
       mask[static_cast<size_t>(t) * mask_words + word] = myword;
   }
   __device__ __forceinline__ void end_half(int h) {
-    if (row_ok) {
-      const size_t i = static_cast<size_t>(n0 / HALF_N + h) * n_features + f;
-      tile_cnt[i] = cnt;
-      if (tile_band != nullptr) tile_band[i] = bcnt;
+    if (!row_ok) return;
+    if (act_sum != nullptr) {
+      if (cnt != 0) atomicAdd(act_sum + f, cnt);
+      if (bcnt != 0) atomicAdd(entry_sum + f, bcnt);
+      return;
     }
+    tile_cnt[static_cast<size_t>(n0 / HALF_N + h) * n_features + f] = cnt;
   }
   __device__ __forceinline__ void end_tile() {}
 };
@@ -423,78 +428,70 @@ struct GradEpi {
 
 // ------------------------------------------------------------------- scans
 // Per feature: exclusive prefix of the per-tile active counts (in place),
-// the feature's total, and the OR-accumulated fired flag.
-// With tile_band (sampled backward: the per-half counts of its entries, active
-// or in band): col_tot counts the feature's CSR entries and col_act its
-// active entries.
+// the feature's total, and the OR-accumulated fired flag (the GEMM backward
+// and the inference forward; the sampled forward adds per-feature totals in
+// the encoder epilogue instead).
 __global__ void scan_columns_kernel(int* __restrict__ tile_cnt, int* __restrict__ col_tot,
-                                    uint8_t* __restrict__ fired, int n_tiles, int n_features,
-                                    const int* __restrict__ tile_band = nullptr,
-                                    int* __restrict__ col_act = nullptr) {
+                                    uint8_t* __restrict__ fired, int n_tiles, int n_features) {
   for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < n_features;
        f += gridDim.x * blockDim.x) {
-    int run = 0, band = 0;
-    if (tile_band != nullptr) {
-      // sampled backward: totals only (8 independent loads in flight)
-      int t = 0;
-      for (; t + 8 <= n_tiles; t += 8) {
-        int a[8], b[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const size_t i = static_cast<size_t>(t + u) * n_features + f;
-          a[u] = tile_cnt[i];
-          b[u] = tile_band[i];
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          run += a[u];
-          band += b[u];
-        }
-      }
-      for (; t < n_tiles; ++t) {
-        const size_t i = static_cast<size_t>(t) * n_features + f;
-        run += tile_cnt[i];
-        band += tile_band[i];
-      }
-    } else {
-      for (int t = 0; t < n_tiles; ++t) {
-        const size_t i = static_cast<size_t>(t) * n_features + f;
-        const int v = tile_cnt[i];
-        tile_cnt[i] = run;
-        run += v;
-      }
+    int run = 0;
+    for (int t = 0; t < n_tiles; ++t) {
+      const size_t i = static_cast<size_t>(t) * n_features + f;
+      const int v = tile_cnt[i];
+      tile_cnt[i] = run;
+      run += v;
     }
-    col_tot[f] = tile_band != nullptr ? band : run;
-    if (col_act != nullptr) col_act[f] = run;
+    col_tot[f] = run;
     if (fired != nullptr && run > 0) fired[f] = 1;
+  }
+}
+
+// After the CSR offset scan of the sampled forward (col_offs[F] = entries):
+// nnz = sum of the per-feature active counts (fixed-order block reduction),
+// the fired flags, csr_pairs and the overflow flag; resets the backward's
+// feature counter.
+__global__ void __launch_bounds__(1024)
+    count_stats_kernel(const int* __restrict__ col_act, const int* __restrict__ col_offs,
+                       int n_features, int64_t capacity, SaeB200StepStats* stats,
+                       int* counters, uint8_t* __restrict__ fired) {
+  __shared__ int s_tmp[33];
+  int local = 0;
+  for (int f = threadIdx.x; f < n_features; f += blockDim.x) {
+    const int a = col_act[f];
+    local += a;
+    if (fired != nullptr && a > 0) fired[f] = 1;
+  }
+  int total = 0;
+  block_excl_scan(local, s_tmp, total);
+  if (threadIdx.x == 0) {
+    const int pairs = col_offs[n_features];
+    stats->nnz = total;
+    stats->csr_pairs = pairs;
+    stats->csr_overflow = (static_cast<int64_t>(pairs) > capacity) ? 1 : 0;
+    counters[0] = 0;
   }
 }
 
 // Exclusive scan of the per-feature totals into CSR row offsets (one block).
 __global__ void __launch_bounds__(1024)
     scan_offsets_kernel(const int* __restrict__ col_tot, int* __restrict__ col_offs, int n_features,
-                        int64_t capacity, SaeB200StepStats* stats, int* counters,
-                        const int* __restrict__ col_act = nullptr) {
+                        int64_t capacity, SaeB200StepStats* stats, int* counters) {
   __shared__ int s_tmp[33];
   const int per = (n_features + blockDim.x - 1) / blockDim.x;
   const int b = threadIdx.x * per;
   const int e = min(n_features, b + per);
-  int local = 0, act = 0;
-  for (int i = b; i < e; ++i) {
-    local += col_tot[i];
-    if (col_act != nullptr) act += col_act[i];
-  }
+  int local = 0;
+  for (int i = b; i < e; ++i) local += col_tot[i];
   int total = 0;
   int run = block_excl_scan(local, s_tmp, total);
   for (int i = b; i < e; ++i) {
     col_offs[i] = run;
     run += col_tot[i];
   }
-  int act_total = total;   // without col_act every CSR entry is active
-  if (col_act != nullptr) block_excl_scan(act, s_tmp, act_total);
   if (threadIdx.x == 0) {
     col_offs[n_features] = total;
-    stats->nnz = act_total;
+    stats->nnz = total;   // every entry of this CSR is active
     stats->csr_pairs = total;
     stats->csr_overflow = (static_cast<int64_t>(total) > capacity) ? 1 : 0;
     counters[0] = 0;
@@ -566,23 +563,29 @@ __global__ void __launch_bounds__(256)
         }
         const int tot = __shfl_sync(0xffffffffu, incl, 31);
         int q = pos[i] + incl - mine;
-        const uint16_t* prow = pre16 + static_cast<size_t>(f) * ldp;
         const int tbase = (w0 + lane) * 32;
         while (bits) {
           const int b = __ffs(bits) - 1;
           bits &= bits - 1;
-          const int t = tbase + b;
-          const uint32_t u = prow[t];
-          const float p = __uint_as_float(u << 16);
-          const uint32_t fl2 = (p > th[i] ? CSR_ACTIVE : 0u) |
-                               (fabsf(__fsub_rn(p, th[i])) < eps ? CSR_BAND : 0u);
-          if (q < end[i]) {
-            csr_tok[q] = t;
-            csr_val[q] = u | fl2;
-          }
+          if (q < end[i]) csr_tok[q] = tbase + b;
           ++q;
         }
         pos[i] += tot;
+      }
+    }
+    // the entries' pre values and flags: independent loads, 32 in flight per warp
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = f0 + warp * 4 + i;
+      if (f >= n_features) continue;
+      const uint16_t* prow = pre16 + static_cast<size_t>(f) * ldp;
+      const int q1 = min(pos[i], end[i]);
+      for (int q = col_offs[f] + lane; q < q1; q += 32) {
+        const uint32_t u = prow[csr_tok[q]];
+        const float p = __uint_as_float(u << 16);
+        csr_val[q] = u | (p > th[i] ? CSR_ACTIVE : 0u) |
+                     (fabsf(__fsub_rn(p, th[i])) < eps ? CSR_BAND : 0u);
       }
     }
   }
