@@ -1086,14 +1086,33 @@ __global__ void __launch_bounds__(1024)
   __shared__ float s_tmp[33];
   __shared__ unsigned long long s_cnt;
   if (threadIdx.x == 0) s_cnt = 0;
+  // 8 loads in flight per thread; partial sums in a fixed order
   float sq = 0.f;
   unsigned long long cnt = 0;
-  for (int64_t i = threadIdx.x; i < n_tokens; i += blockDim.x) {
+  const int64_t step = static_cast<int64_t>(blockDim.x) * 8;
+  int64_t i0 = threadIdx.x;
+  for (; i0 + 7 * blockDim.x < n_tokens; i0 += step) {
+    float a[8];
+    int c[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      a[u] = tok_sqerr[i0 + u * blockDim.x];
+      c[u] = tok_cnt[i0 + u * blockDim.x];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      sq += a[u];
+      cnt += static_cast<unsigned long long>(c[u]);
+    }
+  }
+  for (int64_t i = i0; i < n_tokens; i += blockDim.x) {
     sq += tok_sqerr[i];
     cnt += static_cast<unsigned long long>(tok_cnt[i]);
   }
   const float total_sq = block_sum(sq, s_tmp);
-  atomicAdd(&s_cnt, cnt);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(&s_cnt, cnt);   // integer: exact in any order
   __syncthreads();
   if (threadIdx.x == 0) {
     const float inv_accum = 1.0f / static_cast<float>(accum);
