@@ -1154,7 +1154,7 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
     SAE_TRY(check_launch("bdec_gemv_kernel"));
     bdec_grad_kernel<<<static_cast<unsigned>((d + 31) / 32), 1024, 0, stream>>>(
         w.gosum_part, bdec_owner ? DECODE_GRID : 0, w.gemv_part, GEMV_GRID, static_cast<int>(d),
-        bdec_owner ? acc : 0, grads->b_dec);
+        bdec_owner ? acc : 0, grads->b_dec, stats);
     return check_launch("bdec_grad_kernel");
   }
 

@@ -1206,7 +1206,11 @@ __global__ void __launch_bounds__(1024)
 __global__ void __launch_bounds__(1024)
     bdec_grad_kernel(const float* __restrict__ gosum_part, int n_go,
                      const float* __restrict__ gemv_part, int n_gemv, int d, int accumulate,
-                     float* __restrict__ g_bdec) {
+                     float* __restrict__ g_bdec,
+                     const SaeB200StepStats* skip_on_overflow = nullptr) {
+  // (the sampled backward, queued before the host has seen the forward's
+  // statistics, leaves every gradient untouched when the CSR overflowed)
+  if (skip_on_overflow != nullptr && skip_on_overflow->csr_overflow) return;
   __shared__ float s1[32][33];
   __shared__ float s2[32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;

@@ -222,7 +222,8 @@ class ShardedFusedStep(FusedStep):
 
     def microbatch(self, x: torch.Tensor, *, accum_steps: int = 1, first: bool = True,
                    lambda_l0: float = 0.0, al_mu: float = 0.0, target_l0: float = 0.0,
-                   x_hat_out: Optional[torch.Tensor] = None) -> dict:
+                   x_hat_out: Optional[torch.Tensor] = None,
+                   after_backward: Optional[Callable[[], None]] = None) -> dict:
         sae = self.sae
         if self._aux is not None:
             raise NotImplementedError("the dead-feature aux loss needs a top-k over the whole "
@@ -269,6 +270,8 @@ class ShardedFusedStep(FusedStep):
                ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), self.rank,
                L.ptr(scratch), stream)
         self._allreduce(self.g_b_dec)                          # b_dec gradient
+        if after_backward is not None:
+            after_backward()
         self._bind_grads()
         return st
 

@@ -208,8 +208,9 @@ class FusedStep:
         self.g_W_dec_fm = torch.zeros(F, d, device=dev)
         self.g_b_dec = torch.zeros(d, device=dev)
         self.g_log_thr = torch.zeros(F, device=dev)
-        self._host_stats = torch.zeros(L.STATS_FLOATS, dtype=torch.int32).pin_memory() \
-            if torch.cuda.is_available() else None
+        # two pinned host copies of the StepStats: after the forward, after the norm
+        self._host_stats_slots = [torch.zeros(L.STATS_FLOATS, dtype=torch.int32).pin_memory()
+                                  for _ in range(2)] if torch.cuda.is_available() else None
         self.nnz_last = 0
         self.dense_fallbacks = 0
         # dead-feature aux loss state (set per step by set_aux)
@@ -295,18 +296,35 @@ class FusedStep:
 
     def read_stats(self) -> dict:
         """One device->host copy of the StepStats (synchronises the stream)."""
-        self._host_stats.copy_(self.stats, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        raw = L.StepStats.from_buffer_copy(self._host_stats.numpy().tobytes())
+        return self._wait_stats(self._copy_stats())
+
+    def _copy_stats(self, slot: int = 0):
+        """Queue a copy of the StepStats into pinned host slot ``slot``; returns
+        the event to wait on (the stream keeps running behind it)."""
+        buf = self._host_stats_slots[slot]
+        buf.copy_(self.stats, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream())
+        return slot, ev
+
+    def _wait_stats(self, pending) -> dict:
+        slot, ev = pending
+        ev.synchronize()
+        raw = L.StepStats.from_buffer_copy(self._host_stats_slots[slot].numpy().tobytes())
         return {k: getattr(raw, k) for k in L.STATS_FIELDS}
 
     def microbatch(self, x: torch.Tensor, *, accum_steps: int = 1, first: bool = True,
                    lambda_l0: float = 0.0, al_mu: float = 0.0, target_l0: float = 0.0,
-                   x_hat_out: Optional[torch.Tensor] = None) -> dict:
+                   x_hat_out: Optional[torch.Tensor] = None,
+                   after_backward: Optional[Callable[[], None]] = None) -> dict:
         """Forward + backward of one microbatch; gradients overwrite (first) or
-        add. Reads the forward statistics back once (this also chooses the
-        sparse or the dense weight-gradient path -- an active set larger than
-        the workspace is never truncated) and returns them."""
+        add. Reads the forward statistics back once and returns them. The
+        sampled backward is queued before that read: its kernels do nothing
+        when the active set overflowed the CSR, and the read then selects the
+        dense path (an active set larger than the workspace is never
+        truncated). ``after_backward`` (e.g. the gradient norm) is queued right
+        after the backward, before the host waits, and again if the backward
+        had to be redone."""
         sae = self.sae
         x = self._check_input(x)
         n = x.shape[0]
@@ -318,38 +336,56 @@ class FusedStep:
         dt = L.DTYPE_BF16 if x.dtype == torch.bfloat16 else L.DTYPE_F32
         if self._aux is not None and x_hat_out is None:
             x_hat_out = self._x_hat[:n]
-        L.call("sae_b200_train_forward", ctypes.byref(model), L.ptr(x), dt, ctypes.byref(cfg),
-               L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), L.ptr(x_hat_out),
-               L.ptr(self.fired), stream)
+
+        def forward():
+            L.call("sae_b200_train_forward", ctypes.byref(model), L.ptr(x), dt,
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
+                   L.ptr(x_hat_out), L.ptr(self.fired), stream)
+
+        forward()
         if self._aux is not None:
             aux = self._aux_struct()
             L.call("sae_b200_aux_forward", ctypes.byref(model), L.ptr(x), dt, L.ptr(x_hat_out),
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, ctypes.byref(aux),
                    L.ptr(self._aux_ws), self._aux_ws.numel(), L.ptr(self.stats), stream)
-        st = self.read_stats()
-        self.nnz_last = st["nnz"]
+        pending = self._copy_stats(0)
         grads = self._grads_struct()
+
+        def sparse_backward():
+            L.call("sae_b200_train_backward", ctypes.byref(model), ctypes.byref(grads),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), stream)
+
+        # without the aux loss, the sampled backward goes ahead of the read
+        ahead = self._aux is None and self.grad_feat == "sampled"
+        if ahead:
+            sparse_backward()
+            if after_backward is not None:
+                after_backward()
+        st = self._wait_stats(pending)
+        self.nnz_last = st["nnz"]
+        redone = not ahead
         if st["csr_overflow"]:
             self.dense_fallbacks += 1
             if cfg.pre_entries_only:
                 # the dense backward reads all of pre: redo the forward storing it
                 # (same kernels, same inputs: the same stats, x_hat and fired bits)
                 cfg.pre_entries_only = 0
-                L.call("sae_b200_train_forward", ctypes.byref(model), L.ptr(x), dt,
-                       ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
-                       L.ptr(x_hat_out), L.ptr(self.fired), stream)
+                forward()
             L.call("sae_b200_train_backward_dense", ctypes.byref(model), ctypes.byref(grads),
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
                    L.ptr(self._dense_scratch_for(n)), stream)
+            redone = True
         else:
             sae._sparse_decode_calls += 1
-            L.call("sae_b200_train_backward", ctypes.byref(model), ctypes.byref(grads),
-                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), stream)
+            if not ahead:
+                sparse_backward()
         if self._aux is not None:
             aux = self._aux_struct()
             L.call("sae_b200_aux_backward", ctypes.byref(model), ctypes.byref(grads),
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, ctypes.byref(aux),
                    L.ptr(self._aux_ws), self._aux_ws.numel(), stream)
+        if redone and after_backward is not None:
+            after_backward()
         self._bind_grads()
         return st
 
@@ -384,18 +420,25 @@ class FusedStep:
         l0 = 0.0
         loss = 0.0
         aux = 0.0
+        norm_stats = []
+
+        def norm():
+            # clip_grad_norm_ (3049) and its statistics read, queued ahead of Adam
+            self.grad_norm(max_norm)
+            norm_stats[:] = [self._copy_stats(1)]
+
         for i in range(accum):
             s = self.microbatch(batch[i * mb:(i + 1) * mb], accum_steps=accum, first=(i == 0),
-                                lambda_l0=lambda_l0, al_mu=al_mu, target_l0=target_l0)
+                                lambda_l0=lambda_l0, al_mu=al_mu, target_l0=target_l0,
+                                after_backward=norm if i == accum - 1 else None)
             recon += s["recon_loss"] * accum     # accum_recon_t (3057)
             l0 += s["l0"]                        # accum_l0_t (3058)
             loss += s["loss"]
             aux += s["aux_loss"]
-        self.grad_norm(max_norm)
-        s = self.read_stats()
         l0_step = l0 / accum
         factor = 1.0 if wenc_dampen is None else float(wenc_dampen(l0_step))
-        self.optimizer_step(factor)
+        self.optimizer_step(factor)              # clip coefficient applied on the device
+        s = self._wait_stats(norm_stats[0])      # Adam keeps running meanwhile
         return {"recon_loss": recon / accum, "l0": l0_step, "grad_norm": s["grad_norm"],
                 "clip_coef": s["clip_coef"], "nnz": s["nnz"], "loss": loss,
                 "aux_loss": aux, "wenc_factor": factor}

@@ -190,7 +190,10 @@ int sae_b200_train_forward(const SaeB200Model* model, const void* x, int x_dtype
  * gradients. Replaces loss.backward() through _SparseDecode.backward
  * (639-654), the hooks 784-825 and _EncoderPreBias.backward (592-607).
  * When stats->csr_overflow is set on the device the sparse scatter is
- * skipped; the caller then runs sae_b200_train_backward_dense. */
+ * skipped; the caller then runs sae_b200_train_backward_dense. With the
+ * sampled backward (grad_feat_gemm = 0) an overflowed microbatch leaves every
+ * gradient untouched, so the call may be queued before the host has read the
+ * forward's statistics. */
 int sae_b200_train_backward(const SaeB200Model* model, const SaeB200Grads* grads,
                             const SaeB200StepConfig* cfg, void* workspace,
                             size_t workspace_bytes, SaeB200StepStats* stats, void* stream);

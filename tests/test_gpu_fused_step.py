@@ -237,6 +237,48 @@ def test_dense_fallback_matches_sparse_path():
             assert _rel(b.cpu().numpy(), a.cpu().numpy()) < 2e-3
 
 
+@pytest.mark.parametrize("swap", [False, True])
+def test_overflow_inside_accumulation_matches_sparse_step(swap):
+    """The sampled backward is queued before the host reads the forward's
+    statistics; a microbatch whose entries overflow the CSR leaves the
+    gradients untouched and is redone on the dense path. With one of two
+    accumulated microbatches overflowing (first or second), the step equals
+    the step without overflow."""
+    g = load_golden("ste_f64_accum2")
+    cfg = oracle_cfg(g)
+    xs = [g[f"x{i}"].astype(np.float32) for i in range(2)]
+    if swap:
+        xs = xs[::-1]
+    mb = xs[0].shape[0]
+    x = torch.from_numpy(np.concatenate(xs)).cuda()
+    _, _, probe = build(g)
+    pairs = [probe.microbatch(torch.from_numpy(xi).cuda(), lambda_l0=cfg.lambda_l0,
+                              al_mu=cfg.al_mu, target_l0=cfg.target_l0)["csr_pairs"] for xi in xs]
+    if pairs[0] == pairs[1]:
+        pytest.skip("both microbatches have the same number of entries")
+    runs = []
+    for cap in (None, min(pairs)):
+        sae, opt, fs = build(g, csr_capacity=cap)
+        fs.max_tokens = x.shape[0]
+        out = fs.step(x, microbatch_tokens=mb, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu,
+                      target_l0=cfg.target_l0)
+        torch.cuda.synchronize()
+        runs.append((fs.dense_fallbacks, out,
+                     [t.clone() for t in (fs.g_W_enc, fs.g_b_enc, fs.g_W_dec_fm, fs.g_b_dec,
+                                          fs.g_log_thr)],
+                     [t.detach().clone() for t in (sae.W_enc.weight, sae.W_dec.weight,
+                                                   sae.log_threshold)]))
+    (f0, o0, g0, p0), (f1, o1, g1, p1) = runs
+    assert f0 == 0 and f1 == 1
+    for a, b in zip(g0, g1):
+        assert _rel(b.cpu().numpy(), a.cpu().numpy()) < 2e-3
+    assert o1["grad_norm"] == pytest.approx(o0["grad_norm"], rel=2e-3)
+    assert o1["l0"] == o0["l0"] and o1["recon_loss"] == o0["recon_loss"]
+    lr = float(g["lr"])
+    for a, b in zip(p0, p1):
+        assert float((a - b).abs().max()) <= 2.5 * lr
+
+
 def test_step_is_deterministic():
     g = load_golden("super_f32_tiles")
     cfg = oracle_cfg(g)
