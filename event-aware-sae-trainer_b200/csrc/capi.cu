@@ -1381,7 +1381,7 @@ int sae_b200_adam_step(const SaeB200Model* model, const SaeB200Grads* grads,
       }
     }
     if (row_kernel && vpt > 0) {
-      const int rpb = std::max(1, 512 / tpr);
+      const int rpb = std::max(1, 256 / tpr);   // small blocks: more of them resident per SM
       const int threads = rpb * tpr;
       const int64_t blocks_needed = (rows[k] + rpb - 1) / rpb;
       const int per_sm = std::max(1, 2048 / threads);
