@@ -107,9 +107,14 @@ __global__ void prep_kernel(const XT* __restrict__ x, const float* __restrict__ 
   for (int64_t f = tid; f < n_features; f += stride) theta[f] = expf(log_thr[f]);
   const int64_t nvec = n_tokens * (d / 8);
   const int dv = d / 8;
-  for (int64_t i = tid; i < nvec; i += stride) {
+  auto one = [&](int64_t i, const float (&xv)[8]) {
     const int c = static_cast<int>(i % dv) * 8;
-    float xv[8];
+    float r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __fsub_rn(xv[j], b_dec[c + j]);
+    reinterpret_cast<uint4*>(xc)[i] = pack8(r);
+  };
+  auto load = [&](int64_t i, float (&xv)[8]) {
     if constexpr (sizeof(XT) == 2) {
       unpack8(reinterpret_cast<const uint4*>(x)[i], xv);
     } else {
@@ -118,10 +123,20 @@ __global__ void prep_kernel(const XT* __restrict__ x, const float* __restrict__ 
       xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
       xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
     }
-    float r[8];
+  };
+  // four vectors per thread in flight
+  int64_t i = tid;
+  for (; i + 3 * stride < nvec; i += 4 * stride) {
+    float xv[4][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] = __fsub_rn(xv[j], b_dec[c + j]);
-    reinterpret_cast<uint4*>(xc)[i] = pack8(r);
+    for (int u = 0; u < 4; ++u) load(i + u * stride, xv[u]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) one(i + u * stride, xv[u]);
+  }
+  for (; i < nvec; i += stride) {
+    float xv[8];
+    load(i, xv);
+    one(i, xv);
   }
 }
 
