@@ -347,6 +347,59 @@ def test_wide_rows_match_oracle(grad_feat):
         assert _rel(t.cpu().numpy(), getattr(ref, k)) < 5e-3, k
 
 
+@pytest.mark.parametrize("B", [1, 33, 333])
+def test_ragged_token_counts_match_oracle(B):
+    """Token counts that fill no whole tile, 32-token word or 8-token group on
+    the tcgen05 path (d % 64 == 0, F % 256 == 0): gradients against the
+    oracle's backward on the kernel's own gates, and the default entries-only
+    pre store bit-identical to the full store."""
+    import math
+    from sae_b200 import B200Adam, FusedStep, make_sae, reference_param_groups
+    d, F = 128, 512
+    x = O.superposition_batch(B, d, 1024, 12, math.log(8.0), 0.3, seed=41 + B)
+    p0 = None
+    grads = {}
+    for store in ("full", "entries"):
+        sae = make_sae(d, F, seed=6)
+        with torch.no_grad():
+            sae.b_dec.copy_(torch.from_numpy(x.mean(0)))
+            sae.log_threshold.fill_(math.log(0.2))
+        if p0 is None:
+            p0 = O.Params(*(t.detach().numpy().copy() for t in (
+                sae.W_enc.weight, sae.W_enc.bias, sae.W_dec.weight, sae.b_dec,
+                sae.log_threshold)))
+        sae = sae.cuda()
+        sae.ste_bandwidth = 0.05
+        opt = B200Adam(reference_param_groups(sae, 1e-4), lr=1e-4, sae=sae, renorm=True)
+        fs = FusedStep(sae, opt, max_tokens=B, pre_store=store)
+        cfg = O.StepConfig(lambda_l0=1e-3, al_mu=1e-2, target_l0=4.0, ste_bandwidth=0.05,
+                           lr=(1e-4,) * 4)
+        st = fs.microbatch(torch.from_numpy(x).cuda(), lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu,
+                           target_l0=cfg.target_l0)
+        torch.cuda.synchronize()
+        from sae_b200 import _lib as L
+        assert L.device_status() == 0
+        grads[store] = (st, [t.clone() for t in (fs.g_W_enc, fs.g_b_enc, fs.g_W_dec_fm,
+                                                 fs.g_b_dec, fs.g_log_thr)])
+        if store == "full":
+            v = workspace_views(fs, B)
+            fw = O.forward(x, p0, cfg, "bf16", theta=v["theta"].cpu().numpy(),
+                           pre=v["pre"].float().cpu().numpy())
+            assert st["l0"] == pytest.approx(fw.l0, rel=1e-6)
+            assert st["nnz"] == int(round(fw.l0 * B))
+            ref = O.backward(x, p0, fw, cfg, "bf16")
+            for k, t in {"W_enc": fs.g_W_enc, "b_enc": fs.g_b_enc, "W_dec": fs.g_W_dec_fm.t(),
+                         "b_dec": fs.g_b_dec, "log_threshold": fs.g_log_thr}.items():
+                r = getattr(ref, k)
+                if np.linalg.norm(r) > 0:
+                    assert _rel(t.cpu().numpy(), r) < 5e-3, k
+                else:
+                    assert float(t.abs().max()) == 0.0, k
+    assert grads["full"][0] == grads["entries"][0]
+    for a, b in zip(grads["full"][1], grads["entries"][1]):
+        assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("name,force_simt", CASES)
 def test_entries_only_pre_store_matches_full_store(name, force_simt):
     """The default forward stores pre only in the 32-token words that hold an
