@@ -69,9 +69,11 @@ struct DeviceInfo {
   int major = 0;
 };
 
+constexpr int kMaxDevices = 64;
+
 DeviceInfo device_info() {
   static std::mutex mu;
-  static DeviceInfo cache[64];
+  static DeviceInfo cache[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
@@ -336,12 +338,17 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
     } else {
       tm_aux = tm_w;
     }
+    // Kernel attributes and the cluster occupancy belong to the current
+    // device's context: set up once per device.
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+      return fail(SAE_ERR_CUDA, "no usable current device");
     if (F % (2 * TILE_M) == 0 && pair_mode_enabled()) {
       // Paired CTAs: one 256-feature x 256-token tile per cluster of two.
       constexpr size_t smem2 = Tc2Config<Epi::kAux>::SMEM;
-      static std::once_flag attr2_once;
-      static int max_clusters = 0;
-      std::call_once(attr2_once, [] {
+      static std::once_flag attr2_once[kMaxDevices];
+      static int max_clusters_of[kMaxDevices] = {};
+      std::call_once(attr2_once[dev], [dev] {
         cudaFuncSetAttribute(tc2_tile_gemm<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem2));
         cudaLaunchConfig_t lc = {};
@@ -358,8 +365,9 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, tc2_tile_gemm<Epi>, &lc) != cudaSuccess) n = 0;
         cudaGetLastError();
-        max_clusters = n;
+        max_clusters_of[dev] = n;
       });
+      const int max_clusters = max_clusters_of[dev];
       if (max_clusters > 0) {
         // Each CTA of the pair loads half of the 256-token slab.
         CUtensorMap tm_t_half, tm_aux2 = tm_aux;
@@ -378,8 +386,8 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
         return rc;
       }
     }
-    static std::once_flag attr_once;
-    std::call_once(attr_once, [] {
+    static std::once_flag attr_once[kMaxDevices];
+    std::call_once(attr_once[dev], [] {
       cudaFuncSetAttribute(tc_tile_gemm<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
     });
