@@ -16,6 +16,7 @@
 namespace sae {
 
 constexpr int AUX_TB = 32;   // tokens per selection block (one per lane)
+constexpr int AUX_DECODE_STAGE = 256;   // selected entries staged per pass
 
 // bf16 bits of a positive value order like the value; everything else -> 0.
 __device__ __forceinline__ uint32_t aux_key(uint16_t bits) {
@@ -27,14 +28,33 @@ __device__ __forceinline__ uint32_t aux_key(uint16_t bits) {
 // many of the keys equal to T to take (the lowest dead indices first); a
 // third pass over the dead rows writes the selected entries in dead order.
 // 256 threads; rows are read as 64-byte segments of the feature-major
-// pre-activations (one row = one dead feature's 32 tokens).
-__global__ void __launch_bounds__(256)
+// pre-activations (one row = one dead feature's 32 tokens), 16 rows in flight
+// per warp. PACKED (fewer than 65536 dead features): two 16-bit bin counts
+// per 32-bit word, so the histograms take 16.5 KB and every block of a
+// 32768-token step is resident at once (one wave).
+template <bool PACKED>
+struct AuxHist {
+  static constexpr int kWords = PACKED ? 129 : 257;
+  uint32_t w[AUX_TB][kWords];
+  __device__ __forceinline__ void add(int t, uint32_t bin) {
+    if constexpr (PACKED) atomicAdd(&w[t][bin >> 1], 1u << ((bin & 1u) * 16));
+    else atomicAdd(&w[t][bin], 1u);
+  }
+  __device__ __forceinline__ uint32_t get(int t, int bin) const {
+    if constexpr (PACKED) return (w[t][bin >> 1] >> ((bin & 1) * 16)) & 0xFFFFu;
+    else return w[t][bin];
+  }
+};
+
+template <bool PACKED>
+__global__ void __launch_bounds__(256, PACKED ? 7 : 4)
     aux_select_kernel(const bf16* __restrict__ pre, int ldp, const int32_t* __restrict__ dead,
                       int n_dead, int n_features, int k, int64_t n_tokens,
                       int32_t* __restrict__ list_j,
                       float* __restrict__ list_v, int32_t* __restrict__ cnt,
                       int32_t* __restrict__ count_j) {
-  __shared__ uint32_t hist[AUX_TB][257];
+  constexpr int RW = PACKED ? 8 : 16;   // rows in flight per warp in the histogram rounds
+  __shared__ AuxHist<PACKED> hist;
   __shared__ uint16_t tile[32][AUX_TB + 2];
   __shared__ uint32_t s_hi[AUX_TB], s_above[AUX_TB], s_T[AUX_TB], s_m[AUX_TB];
   __shared__ int s_base[AUX_TB], s_ties[AUX_TB];
@@ -42,6 +62,8 @@ __global__ void __launch_bounds__(256)
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * AUX_TB;
   const bool tok_ok = t0 + lane < n_tokens;
   const uint16_t* pre16 = reinterpret_cast<const uint16_t*>(pre);
+  uint32_t* hw = &hist.w[0][0];
+  constexpr int HW = AUX_TB * AuxHist<PACKED>::kWords;
 
   auto key_at = [&](int j) -> uint32_t {
     if (!tok_ok) return 0u;
@@ -50,32 +72,31 @@ __global__ void __launch_bounds__(256)
   };
 
   // round 1: histogram of the high byte of every positive key
-  for (int i = tid; i < AUX_TB * 257; i += blockDim.x) (&hist[0][0])[i] = 0u;
+  for (int i = tid; i < HW; i += blockDim.x) hw[i] = 0u;
   __syncthreads();
-  // 8 rows per warp in flight: the dead id and the row segment are two
-  // dependent loads per row
-  for (int j0 = warp * 8; j0 < n_dead; j0 += 64) {
-    uint32_t key[8];
+  for (int j0 = warp * RW; j0 < n_dead; j0 += 8 * RW) {
+    uint32_t key[RW];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) key[u] = j0 + u < n_dead ? key_at(j0 + u) : 0u;
+    for (int u = 0; u < RW; ++u) key[u] = j0 + u < n_dead ? key_at(j0 + u) : 0u;
 #pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (key[u]) atomicAdd(&hist[lane][key[u] >> 8], 1u);
+    for (int u = 0; u < RW; ++u)
+      if (key[u]) hist.add(lane, key[u] >> 8);
   }
   __syncthreads();
   if (tid < AUX_TB) {
     uint32_t cum = 0, hi = 0, total = 0;
-    for (int b = 255; b >= 0; --b) total += hist[tid][b];
+    for (int b = 255; b >= 0; --b) total += hist.get(tid, b);
     if (total <= static_cast<uint32_t>(k)) {
       s_hi[tid] = 0xFFFFFFFFu;   // take every positive key
       s_above[tid] = 0;
     } else {
       for (int b = 255; b >= 0; --b) {
-        if (cum + hist[tid][b] >= static_cast<uint32_t>(k)) {
+        const uint32_t h = hist.get(tid, b);
+        if (cum + h >= static_cast<uint32_t>(k)) {
           hi = b;
           break;
         }
-        cum += hist[tid][b];
+        cum += h;
       }
       s_hi[tid] = hi;
       s_above[tid] = cum;
@@ -83,16 +104,18 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
   // round 2: low byte inside the chosen high-byte bin
-  for (int i = tid; i < AUX_TB * 257; i += blockDim.x) (&hist[0][0])[i] = 0u;
+  for (int i = tid; i < HW; i += blockDim.x) hw[i] = 0u;
   __syncthreads();
-  for (int j0 = warp * 8; j0 < n_dead; j0 += 64) {
-    uint32_t key[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) key[u] = j0 + u < n_dead ? key_at(j0 + u) : 0u;
+  {
     const uint32_t hi = s_hi[lane];
+    for (int j0 = warp * RW; j0 < n_dead; j0 += 8 * RW) {
+      uint32_t key[RW];
 #pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (key[u] && (key[u] >> 8) == hi) atomicAdd(&hist[lane][key[u] & 0xFFu], 1u);
+      for (int u = 0; u < RW; ++u) key[u] = j0 + u < n_dead ? key_at(j0 + u) : 0u;
+#pragma unroll
+      for (int u = 0; u < RW; ++u)
+        if (key[u] && (key[u] >> 8) == hi) hist.add(lane, key[u] & 0xFFu);
+    }
   }
   __syncthreads();
   if (tid < AUX_TB) {
@@ -103,11 +126,12 @@ __global__ void __launch_bounds__(256)
       uint32_t cum = s_above[tid];
       uint32_t lo = 0;
       for (int b = 255; b >= 0; --b) {
-        if (cum + hist[tid][b] >= static_cast<uint32_t>(k)) {
+        const uint32_t h = hist.get(tid, b);
+        if (cum + h >= static_cast<uint32_t>(k)) {
           lo = b;
           break;
         }
-        cum += hist[tid][b];
+        cum += h;
       }
       s_T[tid] = (s_hi[tid] << 8) | lo;
       s_m[tid] = static_cast<uint32_t>(k) - cum;   // keys equal to T still to take
@@ -115,15 +139,23 @@ __global__ void __launch_bounds__(256)
     s_base[tid] = 0;
     s_ties[tid] = 0;
   }
-  __syncthreads();
-  // round 3: rows in chunks of 32 through shared memory; warp w owns tokens
-  // w, w + 8, w + 16, w + 24 and walks the chunk's rows in order (lane = row)
+  // round 3: rows in chunks of 32 through shared memory; warp w loads rows
+  // w, w + 8, w + 16, w + 24 of the next chunk while the current one is
+  // scanned, owns tokens w, w + 8, w + 16, w + 24 and walks the chunk's rows
+  // in order (lane = row)
+  uint32_t nxt[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) nxt[q] = (8 * q + warp < n_dead) ? key_at(8 * q + warp) : 0u;
   for (int j0 = 0; j0 < n_dead; j0 += 32) {
-    for (int r = warp; r < 32; r += 8) {
-      const int j = j0 + r;
-      tile[r][lane] = (j < n_dead) ? static_cast<uint16_t>(key_at(j)) : 0;
-    }
+    __syncthreads();   // the previous chunk's tile is consumed (and round 2's state is set)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tile[8 * q + warp][lane] = static_cast<uint16_t>(nxt[q]);
     __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int j = j0 + 32 + 8 * q + warp;
+      nxt[q] = j < n_dead ? key_at(j) : 0u;
+    }
     const uint32_t lt = (1u << lane) - 1u;
     for (int q = warp; q < AUX_TB; q += 8) {
       const int64_t b = t0 + q;
@@ -149,8 +181,8 @@ __global__ void __launch_bounds__(256)
       }
       __syncwarp();
     }
-    __syncthreads();
   }
+  __syncthreads();
   if (tid < AUX_TB && t0 + tid < n_tokens) cnt[t0 + tid] = min(s_base[tid], k);
 }
 
@@ -166,7 +198,12 @@ __global__ void __launch_bounds__(1024)
                       const bf16* __restrict__ w_dec, const XT* __restrict__ x,
                       const float* __restrict__ x_hat, int64_t n_tokens, int d, float g_scale,
                       bf16* __restrict__ g_aux, float* __restrict__ aux_sq) {
+  // The token's selected entries (decoder row, value) are staged in shared
+  // memory by one load per thread, then the rows are gathered eight at a
+  // time; the sum runs over the entries in list order, as before staging.
   __shared__ float s_tmp[33];
+  __shared__ int s_f[AUX_DECODE_STAGE];
+  __shared__ float s_a[AUX_DECODE_STAGE];
   const int col = threadIdx.x;
   const int nvec = d / 8;
   const bool has = col < nvec;
@@ -177,33 +214,40 @@ __global__ void __launch_bounds__(1024)
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
     const int n = cnt[b];
     float sq = 0.f;
-    if (has) {
-      int i = 0;
-      for (; i + 3 < n; i += 4) {
-        uint4 u[4];
-        float a[4];
+    for (int w0 = 0; w0 < n; w0 += AUX_DECODE_STAGE) {
+      const int m = min(AUX_DECODE_STAGE, n - w0);
+      __syncthreads();   // the previous window's entries are consumed
+      for (int e = threadIdx.x; e < m; e += blockDim.x) {
+        const size_t li = static_cast<size_t>(b) * k + w0 + e;
+        s_f[e] = min(max(dead[list_j[li]], 0), n_features - 1);
+        s_a[e] = list_v[li];
+      }
+      __syncthreads();
+      if (has) {
+        int i = 0;
+        for (; i + 7 < m; i += 8) {
+          uint4 u[8];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int f = min(max(dead[list_j[b * k + i + r]], 0), n_features - 1);
-          a[r] = list_v[b * k + i + r];
-          u[r] = __ldg(wcol + static_cast<size_t>(f) * nvec);
+          for (int r = 0; r < 8; ++r) u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r]) * nvec);
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            float wf[8];
+            unpack8(u[r], wf);
+            const float a = s_a[i + r];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+          }
         }
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
+        for (; i < m; ++i) {
           float wf[8];
-          unpack8(u[r], wf);
+          unpack8(__ldg(wcol + static_cast<size_t>(s_f[i]) * nvec), wf);
+          const float a = s_a[i];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = fmaf(a[r], wf[j], acc[j]);
+          for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
         }
       }
-      for (; i < n; ++i) {
-        const int f = min(max(dead[list_j[b * k + i]], 0), n_features - 1);
-        float wf[8];
-        unpack8(__ldg(wcol + static_cast<size_t>(f) * nvec), wf);
-        const float a = list_v[b * k + i];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
-      }
+    }
+    if (has) {
       const size_t base = static_cast<size_t>(b) * d + col * 8;
       float xv[8];
       if constexpr (sizeof(XT) == 2) {

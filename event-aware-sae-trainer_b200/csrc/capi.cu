@@ -862,9 +862,14 @@ int sae_b200_aux_forward(const SaeB200Model* model, const void* x, int x_dtype,
   if (cudaMemsetAsync(count_j, 0, (n_dead + 1) * sizeof(int32_t), stream) != cudaSuccess)
     return fail(SAE_ERR_CUDA, "aux count reset failed");
   const unsigned blocks = static_cast<unsigned>((c.B + AUX_TB - 1) / AUX_TB);
-  aux_select_kernel<<<blocks, 256, 0, stream>>>(c.w.pre, static_cast<int>(pre_pitch(c.B)),
-                                                aux->dead, n_dead, static_cast<int>(c.F), aux->k,
-                                                c.B, list_j, list_v, cnt, count_j);
+  if (n_dead < 65536)   // bin counts fit 16 bits: packed histograms
+    aux_select_kernel<true><<<blocks, 256, 0, stream>>>(
+        c.w.pre, static_cast<int>(pre_pitch(c.B)), aux->dead, n_dead, static_cast<int>(c.F),
+        aux->k, c.B, list_j, list_v, cnt, count_j);
+  else
+    aux_select_kernel<false><<<blocks, 256, 0, stream>>>(
+        c.w.pre, static_cast<int>(pre_pitch(c.B)), aux->dead, n_dead, static_cast<int>(c.F),
+        aux->k, c.B, list_j, list_v, cnt, count_j);
   SAE_TRY(check_launch("aux_select_kernel"));
   const float g_scale = static_cast<float>(
       2.0 * aux->coeff / (static_cast<double>(c.B) * c.d * cfg->accum_steps));
