@@ -1252,6 +1252,28 @@ int sae_b200_train_backward(const SaeB200Model* model, const SaeB200Grads* grads
                          static_cast<cudaStream_t>(stream));
 }
 
+int sae_b200_store_full_pre(const SaeB200Model* model, const SaeB200StepConfig* cfg,
+                            void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  SAE_TRY(check_model(model, true));
+  SAE_TRY(check_cfg(cfg));
+  SAE_TRY(check_fused_shape(model));
+  ForwardCtx c;
+  c.B = cfg->n_tokens;
+  c.d = model->d_in;
+  c.F = model->n_features;
+  c.L = make_layout(c.B, c.d, c.F, cfg->csr_capacity);
+  SAE_TRY(check_ws(c.L, workspace, workspace_bytes));
+  c.w = carve(workspace, c.L);
+  c.mask_words = static_cast<int>((c.F + 31) / 32);
+  c.n_tiles = static_cast<int>((c.B + TILE_N - 1) / TILE_N);
+  // the forward's xc and thresholds are still in the workspace; the encoder
+  // writes pre in full, the mask again (same bits) and per-tile counts into
+  // scratch the sampled path does not use
+  return launch_encoder<PRE_FULL>(model, c, nullptr, nullptr, nullptr, cfg->ste_bandwidth,
+                                  tc_eligible(c.d, c.F, cfg->force_simt), stream);
+}
+
 int sae_b200_train_backward_dense(const SaeB200Model* model, const SaeB200Grads* grads,
                                   const SaeB200StepConfig* cfg, void* workspace,
                                   size_t workspace_bytes, SaeB200StepStats* stats,

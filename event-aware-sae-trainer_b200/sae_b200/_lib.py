@@ -158,6 +158,8 @@ _SIGNATURES = {
     "sae_b200_train_backward": (
         [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
          c_void_p], c_int),
+    "sae_b200_store_full_pre": (
+        [POINTER(Model), POINTER(StepConfig), c_void_p, c_size_t, c_void_p], c_int),
     "sae_b200_train_backward_dense": (
         [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
          c_void_p, c_void_p], c_int),

@@ -174,14 +174,11 @@ class ShardedFusedStep(FusedStep):
 
     def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int, *,
                  group=None, csr_capacity: Optional[int] = None, force_simt: bool = False,
-                 grad_feat: str = "sampled", exchange: str = "p2p",
+                 grad_feat: str = "sampled", exchange: str = "p2p", pre_store: str = "entries",
                  allreduce: Optional[Callable[[torch.Tensor], None]] = None,
                  rank: Optional[int] = None, world: Optional[int] = None):
-        # pre is stored in full: a shard whose CSR overflows takes the dense
-        # backward without redoing the forward (which holds the exchange that
-        # every rank takes together)
         super().__init__(sae, optimizer, max_tokens, csr_capacity=csr_capacity,
-                         force_simt=force_simt, grad_feat=grad_feat, pre_store="full")
+                         force_simt=force_simt, grad_feat=grad_feat, pre_store=pre_store)
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.group = group
@@ -264,6 +261,12 @@ class ShardedFusedStep(FusedStep):
         if st["csr_overflow"]:
             self.dense_fallbacks += 1
             scratch = self._dense_scratch_for(n)
+            if cfg.pre_entries_only:
+                # the dense path reads all of pre: this shard's encoder again,
+                # locally (the exchange is not repeated)
+                L.call("sae_b200_store_full_pre", ctypes.byref(model), ctypes.byref(cfg),
+                       L.ptr(self.ws), self.ws_bytes, stream)
+                cfg.pre_entries_only = 0
         else:
             sae._sparse_decode_calls += 1
         L.call("sae_b200_shard_backward", ctypes.byref(model), ctypes.byref(grads),

@@ -367,10 +367,11 @@ class FusedStep:
         if st["csr_overflow"]:
             self.dense_fallbacks += 1
             if cfg.pre_entries_only:
-                # the dense backward reads all of pre: redo the forward storing it
-                # (same kernels, same inputs: the same stats, x_hat and fired bits)
+                # the dense backward reads all of pre: store it (the forward's
+                # encoder again, on the same workspace)
+                L.call("sae_b200_store_full_pre", ctypes.byref(model), ctypes.byref(cfg),
+                       L.ptr(self.ws), self.ws_bytes, stream)
                 cfg.pre_entries_only = 0
-                forward()
             L.call("sae_b200_train_backward_dense", ctypes.byref(model), ctypes.byref(grads),
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
                    L.ptr(self._dense_scratch_for(n)), stream)

@@ -198,6 +198,14 @@ int sae_b200_train_backward(const SaeB200Model* model, const SaeB200Grads* grads
                             const SaeB200StepConfig* cfg, void* workspace,
                             size_t workspace_bytes, SaeB200StepStats* stats, void* stream);
 
+/* After a forward with pre_entries_only = 1 whose CSR overflowed: re-runs its
+ * encoder on the same workspace (the forward's xc and thresholds) and stores
+ * all of pre, which sae_b200_train_backward_dense and the sharded dense path
+ * read. Statistics, fired flags and CSR offsets are left as they are. No
+ * counterpart in the reference (its autograd keeps the dense pre tensor). */
+int sae_b200_store_full_pre(const SaeB200Model* model, const SaeB200StepConfig* cfg,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* Same gradients without the capacity limit, for microbatches whose active
  * set overflowed csr_capacity. dense_scratch: bf16 device buffer of
  * n_features * sae_b200_pre_pitch(n_tokens) elements owned by the caller. */

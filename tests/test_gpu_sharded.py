@@ -53,7 +53,8 @@ class ThreadSum:
         return allreduce
 
 
-def run_emulated(g, world, x, cfg, steps=1, microbatch_tokens=None):
+def run_emulated(g, world, x, cfg, steps=1, microbatch_tokens=None, pre_store="entries",
+                 csr_capacity=None):
     import sae_b200
     from sae_b200 import B200Adam, ShardedFusedStep, reference_param_groups
     full, _, _ = build(g)
@@ -66,7 +67,8 @@ def run_emulated(g, world, x, cfg, steps=1, microbatch_tokens=None):
         opt = B200Adam(reference_param_groups(s, lr), lr=lr, betas=(0.9, 0.999), sae=s,
                        renorm=True)
         steppers.append(ShardedFusedStep(s, opt, max_tokens=x.shape[0],
-                                         allreduce=ts.for_rank(r), rank=r, world=world))
+                                         allreduce=ts.for_rank(r), rank=r, world=world,
+                                         pre_store=pre_store, csr_capacity=csr_capacity))
         shards.append(s)
     outs = [None] * world
     errs = []
@@ -114,7 +116,8 @@ def test_emulated_shards_match_oracle_and_unsharded(world):
     g = load_golden("super_f32_tiles")
     cfg = oracle_cfg(g)
     x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
-    shards, steppers, outs = run_emulated(g, world, x, cfg)
+    # (pre stored in full: the test reads every shard's pre-activations)
+    shards, steppers, outs = run_emulated(g, world, x, cfg, pre_store="full")
     from sae_b200 import _lib as L
     assert L.device_status() == 0
     # every rank sees the same loss, L0 and grad norm, and the same b_dec
@@ -157,6 +160,33 @@ def test_emulated_shards_match_oracle_and_unsharded(world):
         diff = np.abs(got[k] - getattr(ref.params, k))
         assert diff.max() <= 2.5 * float(g["lr"]) + 1e-6, k
     assert outs[0]["grad_norm"] == pytest.approx(ref.grad_norm, rel=BF16_TOL)
+
+
+def test_emulated_shards_entries_only_and_overflow_match_full_store():
+    """The shards' default forward stores pre at the entries only; a shard
+    whose CSR overflows stores the rest locally (no second exchange) before
+    its dense backward. Against the full-store run without overflow: same
+    statistics, gradients within the sampled/dense tolerance."""
+    g = load_golden("super_f32_tiles")
+    cfg = oracle_cfg(g)
+    x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
+    ref_sh, ref_st, ref_out = run_emulated(g, 2, x, cfg, pre_store="full")
+    ref = gather(ref_sh, ref_st)
+    ent_sh, ent_st, ent_out = run_emulated(g, 2, x, cfg)
+    assert all(s.dense_fallbacks == 0 for s in ent_st)
+    ent = gather(ent_sh, ent_st)
+    for k in ("g_W_enc", "g_b_enc", "g_W_dec", "g_log_threshold", "g_b_dec"):
+        np.testing.assert_array_equal(ent[k], ref[k])
+    # a capacity below every shard's entry count: all shards take the dense path
+    ovf_sh, ovf_st, ovf_out = run_emulated(g, 2, x, cfg, csr_capacity=16)
+    assert all(s.dense_fallbacks == 1 for s in ovf_st)
+    from sae_b200 import _lib as L
+    assert L.device_status() == 0
+    ovf = gather(ovf_sh, ovf_st)
+    assert ovf_out[0]["l0"] == ref_out[0]["l0"]
+    assert ovf_out[0]["recon_loss"] == ref_out[0]["recon_loss"]
+    for k in ("g_W_enc", "g_b_enc", "g_W_dec", "g_log_threshold", "g_b_dec"):
+        assert _rel(ovf[k], ref[k]) < 2e-3, k
 
 
 def test_emulated_shards_accumulate_microbatches():
