@@ -14,7 +14,7 @@ using bf16 = __nv_bfloat16;
 // Fixed grid sizes: partial sums are reduced in a fixed order, so a given
 // input produces bit-identical results on every run and every B200.
 constexpr int DECODE_GRID = 2368;   // 148 SMs x 16 (blocks of a few tokens: short tails)
-constexpr int GEMV_GRID = 296;
+constexpr int GEMV_GRID = 1184;
 constexpr int NORM_GRID = SAE_GRAD_NORM_WORKSPACE_BYTES / 4;
 constexpr int DECODE_LIST_CAP = 2048;   // active features staged per pass
 
@@ -554,15 +554,25 @@ __global__ void __launch_bounds__(256)
       end[i] = ok ? col_offs[f + 1] : 0;   // the encoder counted exactly these entries
       th[i] = ok ? theta[f] : 0.f;
     }
+    // the next 32-word chunk of the bitmap is loaded while this one is scanned
+    uint32_t nxt[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int wi = warp + 8 * q, f = f0 + lane;
+      nxt[q] = (wi < n_words && f < n_features) ? sbits[static_cast<size_t>(wi) * n_features + f]
+                                                : 0u;
+    }
     for (int w0 = 0; w0 < n_words; w0 += 32) {
       __syncthreads();
 #pragma unroll
-      for (int r = warp; r < 32; r += 8) {
-        const int wi = w0 + r, f = f0 + lane;
-        tile[r][lane] = (wi < n_words && f < n_features)
-                            ? sbits[static_cast<size_t>(wi) * n_features + f] : 0u;
-      }
+      for (int q = 0; q < 4; ++q) tile[warp + 8 * q][lane] = nxt[q];
       __syncthreads();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int wi = w0 + 32 + warp + 8 * q, f = f0 + lane;
+        nxt[q] = (wi < n_words && f < n_features)
+                     ? sbits[static_cast<size_t>(wi) * n_features + f] : 0u;
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int fl = warp * 4 + i;
