@@ -62,3 +62,24 @@ def test_bad_arguments_are_rejected_without_a_device():
                                     None, None, None)
     assert rc == L.SAE_ERR_INVALID_ARGUMENT
     assert b"ste_bandwidth" in lib.sae_b200_last_error()
+
+
+def test_full_pre_store_and_pre_flag_are_checked_without_a_device():
+    """sae_b200_store_full_pre validates its model, config and workspace
+    before any launch; the dense backward and the aux forward refuse a
+    microbatch whose forward stored pre only at the entries."""
+    from sae_b200 import _lib as L
+    lib = L.load()
+    assert lib.sae_b200_store_full_pre(None, None, None, 0, None) == L.SAE_ERR_INVALID_ARGUMENT
+    m = L.Model(64, 128, 16, 16, 16, 16, 16, 16, 16)
+    bad = L.StepConfig(16, 1024, 0.0, 0.0, 0.0, 0.0, 1, 0, 1, 0)          # ste_bandwidth 0
+    assert lib.sae_b200_store_full_pre(ctypes.byref(m), ctypes.byref(bad), 256, 1 << 30,
+                                       None) == L.SAE_ERR_INVALID_ARGUMENT
+    entries = L.StepConfig(16, 1024, 0.0, 0.0, 0.0, 0.1, 1, 0, 1, 0, 0, 1)
+    assert entries.pre_entries_only == 1
+    m = L.Model(1536, 49152, 256, 256, 256, 256, 256, 256, 256)
+    g = L.Grads(256, 256, 256, 256, 256)
+    rc = lib.sae_b200_train_backward_dense(ctypes.byref(m), ctypes.byref(g), ctypes.byref(entries),
+                                           256, 1 << 30, 256, 256, None)
+    assert rc == L.SAE_ERR_INVALID_ARGUMENT
+    assert b"pre_entries_only" in lib.sae_b200_last_error()
