@@ -184,6 +184,48 @@ def test_entries_only_pre_store_is_bit_identical_at_full_size(setup):
     del fs3
 
 
+def test_aux_loss_at_full_size(setup):
+    """The dead-feature aux loss at the full workload (every 10th feature dead,
+    k = 25): the kernel's aux loss against the oracle's restatement of
+    2986-2998 evaluated on the kernel's own bf16 pre-activations and x_hat
+    (top-k with ties to the lower dead index, relu, bf16 decoder operands and
+    output, fp64 sums). Differences come from summation order only."""
+    import sae_b200
+    from sae_b200 import _lib as L
+    sae, x = setup["sae"], setup["x"]
+    dead = torch.arange(0, F, 10, device="cuda", dtype=torch.int32)
+    k, coeff = 25, 1.0 / 32
+    fs = sae_b200.FusedStep(sae, setup["fs"].opt, max_tokens=B)
+    fs.set_aux(dead, k, coeff)
+    st = fs.microbatch(x, lambda_l0=1e-3, al_mu=1e-2, target_l0=50)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    ldp = L.pre_pitch(B)
+    off = L.workspace_offsets(B, D, F, fs.csr_capacity)["pre"]
+    pre = fs.ws[off:off + 2 * F * ldp].view(torch.bfloat16).view(F, ldp)
+    dl = dead.long()
+    pre_dead = pre[dl, :B].t().float().cpu().numpy()                 # [B, n_dead]
+    resid = (x.float() - fs._x_hat[:B]).cpu().numpy().astype(np.float64)
+    wd = torch.from_numpy(bf16(sae.W_dec.weight.detach()[:, dl].t().contiguous().cpu().numpy()))
+    v = np.maximum(pre_dead, 0)
+    kth = -np.partition(-v, k - 1, axis=1)[:, k - 1:k]                # k-th largest per token
+    gt = v > kth
+    eq = (v == kth) & (kth > 0)
+    need = k - gt.sum(1, keepdims=True)
+    sel = gt | (eq & (np.cumsum(eq, axis=1) <= need))
+    sel &= v > 0
+    sq = 0.0
+    for b0 in range(0, B, 2048):
+        rows = slice(b0, b0 + 2048)
+        acts = torch.from_numpy(np.where(sel[rows], v[rows], 0).astype(np.float64))
+        x_aux = bf16((acts @ wd.double()).numpy().astype(np.float32)).astype(np.float64)
+        sq += float(np.square(resid[rows] - x_aux).sum())
+    aux_ref = coeff * sq / (B * D)
+    assert aux_ref > 0
+    assert st["aux_loss"] == pytest.approx(aux_ref, rel=1e-3)
+    del fs
+
+
 def test_step_is_deterministic_at_full_size(setup):
     fs, x, g = setup["fs"], setup["x"], setup["grads"]
     fs.microbatch(x, lambda_l0=1e-3, al_mu=1e-2, target_l0=50)
