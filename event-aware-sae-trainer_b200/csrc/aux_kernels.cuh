@@ -23,7 +23,7 @@ __device__ __forceinline__ uint32_t aux_key(uint16_t bits) {
   return (bits & 0x8000u) ? 0u : bits;
 }
 
-// Per block of 32 tokens: a two-round radix select (high byte, then low byte
+// Per block of 32 tokens: a two-pass radix select (high byte, then low byte
 // of the bf16 key) finds each token's k-th largest positive key T and how
 // many of the keys equal to T to take (the lowest dead indices first); a
 // third pass over the dead rows writes the selected entries in dead order.
@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(256, PACKED ? 7 : 4)
                       int32_t* __restrict__ list_j,
                       float* __restrict__ list_v, int32_t* __restrict__ cnt,
                       int32_t* __restrict__ count_j) {
-  constexpr int RW = PACKED ? 8 : 16;   // rows in flight per warp in the histogram rounds
+  constexpr int RW = PACKED ? 8 : 16;   // rows in flight per warp in the histogram passes
   __shared__ AuxHist<PACKED> hist;
   __shared__ uint16_t tile[32][AUX_TB + 2];
   __shared__ uint32_t s_hi[AUX_TB], s_above[AUX_TB], s_T[AUX_TB], s_m[AUX_TB];
@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256, PACKED ? 7 : 4)
     return aux_key(pre16[static_cast<size_t>(f) * ldp + t0 + lane]);
   };
 
-  // round 1: histogram of the high byte of every positive key
+  // pass 1: histogram of the high byte of every positive key
   for (int i = tid; i < HW; i += blockDim.x) hw[i] = 0u;
   __syncthreads();
   for (int j0 = warp * RW; j0 < n_dead; j0 += 8 * RW) {
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(256, PACKED ? 7 : 4)
     }
   }
   __syncthreads();
-  // round 2: low byte inside the chosen high-byte bin
+  // pass 2: low byte inside the chosen high-byte bin
   for (int i = tid; i < HW; i += blockDim.x) hw[i] = 0u;
   __syncthreads();
   {
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(256, PACKED ? 7 : 4)
     s_base[tid] = 0;
     s_ties[tid] = 0;
   }
-  // round 3: rows in chunks of 32 through shared memory; warp w loads rows
+  // pass 3: rows in chunks of 32 through shared memory; warp w loads rows
   // w, w + 8, w + 16, w + 24 of the next chunk while the current one is
   // scanned, owns tokens w, w + 8, w + 16, w + 24 and walks the chunk's rows
   // in order (lane = row)
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(256, PACKED ? 7 : 4)
 #pragma unroll
   for (int q = 0; q < 4; ++q) nxt[q] = (8 * q + warp < n_dead) ? key_at(8 * q + warp) : 0u;
   for (int j0 = 0; j0 < n_dead; j0 += 32) {
-    __syncthreads();   // the previous chunk's tile is consumed (and round 2's state is set)
+    __syncthreads();   // the previous chunk's tile is consumed (and pass 2's state is set)
 #pragma unroll
     for (int q = 0; q < 4; ++q) tile[8 * q + warp][lane] = static_cast<uint16_t>(nxt[q]);
     __syncthreads();
