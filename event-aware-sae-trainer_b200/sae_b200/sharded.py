@@ -168,7 +168,10 @@ class ShardedFusedStep(FusedStep):
     (``PeerExchange``, one GPU per rank on one node); "nccl" all-reduces it
     with torch.distributed. ``allreduce`` (with ``rank`` and
     ``world``) replaces both by the caller's own in-place sum over the ranks,
-    called with each of the three buffers in order.
+    called with each of the three buffers in order. ``pre_store`` as in
+    FusedStep: a shard whose CSR overflows after an entries-only forward
+    stores the rest of its pre locally before the dense backward (the
+    exchange is not repeated, so the ranks stay in step).
     ``step()``, ``microbatch()``, ``grad_norm()`` and the returned statistics
     have FusedStep's meaning; ``nnz`` and ``csr_overflow`` are this shard's."""
 
