@@ -28,8 +28,8 @@ __device__ __forceinline__ uint32_t aux_key(uint16_t bits) {
 // many of the keys equal to T to take (the lowest dead indices first); a
 // third pass over the dead rows writes the selected entries in dead order.
 // 256 threads; rows are read as 64-byte segments of the feature-major
-// pre-activations (one row = one dead feature's 32 tokens), 16 rows in flight
-// per warp. PACKED (fewer than 65536 dead features): two 16-bit bin counts
+// pre-activations (one row = one dead feature's 32 tokens), 8 rows in flight
+// per warp (16 without PACKED). PACKED (fewer than 65536 dead features): two 16-bit bin counts
 // per 32-bit word, so the histograms take 16.5 KB and every block of a
 // 32768-token step is resident at once (one wave).
 template <bool PACKED>
