@@ -498,7 +498,9 @@ def run_b200(args):
     k_stop = [torch.cuda.Event(enable_timing=True) for _ in range(2 * n_ev)]
     d_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     d_stop = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    for e in k_start + k_stop + d_start + d_stop:
+    a_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    a_stop = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    for e in k_start + k_stop + d_start + d_stop + a_start + a_stop:
         e.record()
     barrier()
     launches0 = L.launch_count()
@@ -510,14 +512,20 @@ def run_b200(args):
             L.set_kernel_timer(L.KERNEL_ENCODER_GEMM, k_start[2 * i], k_stop[2 * i])
             L.set_kernel_timer(L.KERNEL_GRAD_GEMM, k_start[2 * i + 1], k_stop[2 * i + 1])
             L.set_kernel_timer(L.KERNEL_DECODE, d_start[i], d_stop[i])
+            L.set_kernel_timer(L.KERNEL_ADAM, a_start[i], a_stop[i])
             stats.append(step(i, pool[(args.warmup + i) % POOL_BATCHES]))
         ev1.record()
         barrier()
     L.set_kernel_timer(L.KERNEL_ENCODER_GEMM)
     L.set_kernel_timer(L.KERNEL_GRAD_GEMM)
     L.set_kernel_timer(L.KERNEL_DECODE)
+    L.set_kernel_timer(L.KERNEL_ADAM)
     launches = (L.launch_count() - launches0)
     dec_ms = statistics.mean(d_start[i].elapsed_time(d_stop[i]) for i in range(n_ev))
+    adam_ms = statistics.mean(a_start[i].elapsed_time(a_stop[i]) for i in range(n_ev))
+    # mean entry counts of the timed microbatches (active, and active + in-band)
+    nnz_mean = statistics.mean(s["nnz"] for s in stats)
+    pairs_mean = statistics.mean(s.get("csr_pairs", s["nnz"]) for s in stats)
     ms = ev0.elapsed_time(ev1) / args.steps
     ms = max_over_ranks(ms)
     enc_ms = statistics.mean(k_start[2 * i].elapsed_time(k_stop[2 * i]) for i in range(n_ev))
@@ -579,6 +587,7 @@ def run_b200(args):
             (grad_ms, grad_tf, "grad_feat tile GEMM (tcgen05 cta_group::2) + STE epilogue",
              TRAFFIC_GRAD_GEMM))
         peak = peaks["bf16_sustained"]
+        adam_bytes = 30.0 * (2 * d * F + 2 * F + d)
         dense_per_token = (4 if gemm_bwd else 2) * d * F_total
         step_flop = float(dense_per_token) * tokens
         line = {
@@ -631,8 +640,18 @@ def run_b200(args):
             "kernels": ({"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
                          "grad_gemm_ms": grad_ms, "grad_gemm_tflops": grad_tf} if gemm_bwd else
                         {"encoder_gemm_ms": enc_ms, "encoder_gemm_tflops": enc_tf,
-                         "sampled_backward_ms": grad_ms}) |
-                       {"decode_ms": dec_ms} |
+                         "sampled_backward_ms": grad_ms,
+                         # go rows of every entry + xc rows of the active ones, bf16, through L2
+                         "sampled_backward_row_gbs":
+                             (pairs_mean + nnz_mean) * d * 2 / (grad_ms / 1e3) / 1e9}) |
+                       {"decode_ms": dec_ms,
+                        # gathered bf16 decoder rows (L2 hits included)
+                        "decode_row_gbs": nnz_mean * d * 2 / (dec_ms / 1e3) / 1e9,
+                        "adam_ms": adam_ms,
+                        # 30 B per parameter (p, g, m, v read; p, m, v written; bf16 copy)
+                        "adam_gbs": adam_bytes / (adam_ms / 1e3) / 1e9,
+                        "adam_frac_hbm": adam_bytes / (adam_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                        "hbm_peak_source": f"hbm_gbs ({peaks['src']})"} |
                        {"step_dense_tflops": step_flop / (ms / 1e3) / 1e12},
             "clocks": clock,
             "e2e": {"value": e2e_value, "unit": "tokens/s",
@@ -668,8 +687,8 @@ def run_b200(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["inference"], default="atlas",
                     help="atlas: the metric's d=1536 F=49152 SAE, one per GPU (default); "

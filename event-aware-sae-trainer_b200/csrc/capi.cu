@@ -28,8 +28,8 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<int64_t> g_launches{0};
-cudaEvent_t g_timer_start[3] = {nullptr, nullptr, nullptr};
-cudaEvent_t g_timer_stop[3] = {nullptr, nullptr, nullptr};
+cudaEvent_t g_timer_start[4] = {nullptr, nullptr, nullptr, nullptr};
+cudaEvent_t g_timer_stop[4] = {nullptr, nullptr, nullptr, nullptr};
 
 void timer_begin(int which, cudaStream_t s) {
   if (g_timer_start[which] != nullptr) cudaEventRecord(g_timer_start[which], s);
@@ -474,7 +474,7 @@ int64_t sae_b200_pre_pitch(int64_t n_tokens) { return pre_pitch(n_tokens); }
 
 int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event) {
   if (kernel != SAE_KERNEL_ENCODER_GEMM && kernel != SAE_KERNEL_GRAD_GEMM &&
-      kernel != SAE_KERNEL_DECODE)
+      kernel != SAE_KERNEL_DECODE && kernel != SAE_KERNEL_ADAM)
     return fail(SAE_ERR_INVALID_ARGUMENT, "unknown kernel id %d", kernel);
   if ((start_event == nullptr) != (stop_event == nullptr))
     return fail(SAE_ERR_INVALID_ARGUMENT, "set both timer events or neither");
@@ -1378,6 +1378,7 @@ int sae_b200_adam_step(const SaeB200Model* model, const SaeB200Grads* grads,
                       static_cast<bf16*>(model->W_dec_bf16), nullptr, nullptr};
   const int64_t rows[5] = {F, F, F, d, F};
   const int64_t cols[5] = {d, 1, d, 1, 1};
+  timer_begin(SAE_KERNEL_ADAM, stream);
   for (int k = 0; k < 5; ++k) {
     const SaeB200AdamTensor& h = hyper[k];
     if (h.skip) continue;
@@ -1468,6 +1469,7 @@ int sae_b200_adam_step(const SaeB200Model* model, const SaeB200Grads* grads,
       }
     }
   }
+  timer_end(SAE_KERNEL_ADAM, stream);
   return SAE_OK;
 }
 

@@ -258,6 +258,7 @@ def call(name: str, *args) -> None:
 KERNEL_ENCODER_GEMM = 0
 KERNEL_GRAD_GEMM = 1
 KERNEL_DECODE = 2
+KERNEL_ADAM = 3
 
 
 def pre_pitch(n_tokens: int) -> int:

@@ -441,7 +441,8 @@ class FusedStep:
         self.optimizer_step(factor)              # clip coefficient applied on the device
         s = self._wait_stats(norm_stats[0])      # Adam keeps running meanwhile
         return {"recon_loss": recon / accum, "l0": l0_step, "grad_norm": s["grad_norm"],
-                "clip_coef": s["clip_coef"], "nnz": s["nnz"], "loss": loss,
+                "clip_coef": s["clip_coef"], "nnz": s["nnz"], "csr_pairs": s["csr_pairs"],
+                "loss": loss,
                 "aux_loss": aux, "wenc_factor": factor}
 
     @property

@@ -141,11 +141,13 @@ int64_t sae_b200_launch_count(void);
  * stop_event after every launch of the chosen kernel on the launch stream
  * (cudaEvent_t handles owned by the caller; NULL, NULL clears it).
  * kernel: SAE_KERNEL_ENCODER_GEMM (tile GEMM of the forwards),
- * SAE_KERNEL_GRAD_GEMM (tile GEMM of the backwards) or SAE_KERNEL_DECODE
- * (gathered decode of the forwards). */
+ * SAE_KERNEL_GRAD_GEMM (tile GEMM of the backwards, or the sampled backward),
+ * SAE_KERNEL_DECODE (gathered decode of the forwards) or SAE_KERNEL_ADAM (all
+ * launches of one sae_b200_adam_step). */
 #define SAE_KERNEL_ENCODER_GEMM 0
 #define SAE_KERNEL_GRAD_GEMM 1
 #define SAE_KERNEL_DECODE 2   /* the gathered decode of every forward */
+#define SAE_KERNEL_ADAM 3     /* one optimizer update (Adam + renorm + bf16 copies) */
 int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event);
 
 /* Bytes of scratch the training step needs for up to max_tokens tokens. */
