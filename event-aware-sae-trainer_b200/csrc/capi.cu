@@ -88,7 +88,7 @@ DeviceInfo device_info() {
 struct Layout {
   size_t theta, xc, pre, sbits, mask, tile_cnt, col_tot, col_act, col_offs, go, tok_sqerr,
       tok_cnt, gosum_part, thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part,
-      order_k0, order_k1, order_v0, order_v1, order_tmp, order_tmp_bytes, counters, total;
+      row_sumsq, order_k0, order_k1, order_v0, order_v1, order_tmp, order_tmp_bytes, counters, total;
 };
 
 // Row pitch (tokens) of the feature-major pre-activations: whole 64-token
@@ -141,6 +141,9 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   L.csr_tok = take(cap * 4);
   L.csr_val = take(cap * 4);
   L.sumsq_part = take(NORM_GRID * 4);
+  // per-(feature, warp) sums of squares of the final W_enc / W_dec / b_enc /
+  // log_threshold gradients, written by the sampled backward (<= 32 warps)
+  L.row_sumsq = take(static_cast<size_t>(F) * 32 * 4);
   // decode order: tokens sorted by active count, heaviest first
   L.order_k0 = take(B * 4);
   L.order_k1 = take(B * 4);
@@ -183,6 +186,7 @@ struct Ws {
   int* csr_tok;
   uint32_t* csr_val;
   float* sumsq_part;
+  float* row_sumsq;
   int *order_k0, *order_k1, *order_v0, *order_v1;
   void* order_tmp;
   size_t order_tmp_bytes;
@@ -212,6 +216,7 @@ Ws carve(void* base, const Layout& L) {
   w.csr_tok = reinterpret_cast<int*>(at(L.csr_tok));
   w.csr_val = reinterpret_cast<uint32_t*>(at(L.csr_val));
   w.sumsq_part = reinterpret_cast<float*>(at(L.sumsq_part));
+  w.row_sumsq = reinterpret_cast<float*>(at(L.row_sumsq));
   w.order_k0 = reinterpret_cast<int*>(at(L.order_k0));
   w.order_k1 = reinterpret_cast<int*>(at(L.order_k1));
   w.order_v0 = reinterpret_cast<int*>(at(L.order_v0));
@@ -281,21 +286,28 @@ bool tc_eligible(int64_t d, int64_t F, int force_simt) {
 // The sampled backward over a feature-major CSR: one feature (segment) per
 // block of d / (8 U) threads (U = 2 for wide rows: more features in flight
 // per SM). seg_rows maps segments to feature rows (the aux backward).
+// Threads per block of the sampled backward at row width d (a multiple of 32).
+int sampled_threads(int d) {
+  const int nvec = d / 8;
+  const int U = (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
+  return (nvec / U + 31) / 32 * 32;
+}
+
 void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const bf16* go,
                     const bf16* xc, const bf16* w_dec, const float* theta, int n_seg,
                     int n_tokens, int d, float eps, int accumulate, float* g_wdec, float* g_wenc,
                     float* g_logthr, float* g_benc, float* db_enc, int* counter,
                     const SaeB200StepStats* stats, const int* seg_rows, int honor_overflow,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, float* row_sumsq = nullptr) {
   const int nvec = d / 8;
   const int U = (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
-  const int bthr = (nvec / U + 31) / 32 * 32;
+  const int bthr = sampled_threads(d);
   const int per_sm = bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1);
   const int grid = device_info().sm_count * per_sm * 2;
 #define SAE_SAMPLED(CC, UU, MT, MB)                                                            \
   sampled_backward_kernel<CC, UU, MT, MB><<<grid, bthr, 0, stream>>>(                         \
       offs, tok, val, go, xc, w_dec, theta, n_seg, n_tokens, d, eps, accumulate, g_wdec,       \
-      g_wenc, g_logthr, g_benc, db_enc, counter, stats, seg_rows, honor_overflow)
+      g_wenc, g_logthr, g_benc, db_enc, counter, stats, seg_rows, honor_overflow, row_sumsq)
   if (U == 1) {
     if (bthr <= 192) SAE_SAMPLED(2, 1, 192, 4);
     else if (bthr <= 256) SAE_SAMPLED(4, 1, 256, 2);
@@ -1156,7 +1168,7 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
                    static_cast<const bf16*>(model->W_dec_bf16), w.theta, static_cast<int>(F),
                    static_cast<int>(B), static_cast<int>(d), cfg->ste_bandwidth, acc, g_wdec,
                    grads->W_enc, grads->log_threshold, grads->b_enc, w.db_enc, w.counters, stats,
-                   nullptr, 1, stream);
+                   nullptr, 1, stream, w.row_sumsq);
     const int rc = check_launch("sampled_backward_kernel");
     timer_end(SAE_KERNEL_GRAD_GEMM, stream);
     SAE_TRY(rc);
@@ -1323,6 +1335,41 @@ int sae_b200_grad_norm(const SaeB200Model* model, const SaeB200Grads* grads, flo
   float* part = static_cast<float*>(workspace);
   grad_sumsq_kernel<<<NORM_GRID, 512, 0, stream>>>(gl, part);
   SAE_TRY(check_launch("grad_sumsq_kernel"));
+  grad_norm_final_kernel<<<1, 1024, 0, stream>>>(part, NORM_GRID, max_norm, stats);
+  return check_launch("grad_norm_final_kernel");
+}
+
+int sae_b200_grad_norm_sampled(const SaeB200Model* model, const SaeB200Grads* grads,
+                               const SaeB200StepConfig* cfg, const void* workspace,
+                               size_t workspace_bytes, float max_norm, void* norm_workspace,
+                               size_t norm_workspace_bytes, SaeB200StepStats* stats,
+                               void* stream_) {
+  SAE_TRY(check_model(model, false));
+  SAE_TRY(check_cfg(cfg));
+  if (grads == nullptr || stats == nullptr || grads->b_dec == nullptr)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (cfg->grad_feat_gemm != 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT,
+                "grad_norm_sampled follows the sampled backward (grad_feat_gemm = 0) only");
+  if (norm_workspace == nullptr || norm_workspace_bytes < NORM_GRID * sizeof(float))
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "grad_norm_sampled needs %zu workspace bytes",
+                NORM_GRID * sizeof(float));
+  const int64_t d = model->d_in, F = model->n_features;
+  const Layout L = make_layout(cfg->n_tokens, d, F, cfg->csr_capacity);
+  SAE_TRY(check_ws(L, const_cast<void*>(workspace), workspace_bytes));
+  const Ws w = carve(const_cast<void*>(workspace), L);
+  GradList gl{};
+  gl.p[0] = grads->b_dec;
+  gl.n[0] = d;
+  if (!cfg->train_decoder && grads->W_dec_fm != nullptr) {   // not covered by the rows
+    gl.p[1] = grads->W_dec_fm;
+    gl.n[1] = F * d;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  float* part = static_cast<float*>(norm_workspace);
+  grad_sumsq_rows_kernel<<<NORM_GRID, 512, 0, stream>>>(
+      w.row_sumsq, F, sampled_threads(static_cast<int>(d)) / 32, gl, part);
+  SAE_TRY(check_launch("grad_sumsq_rows_kernel"));
   grad_norm_final_kernel<<<1, 1024, 0, stream>>>(part, NORM_GRID, max_norm, stats);
   return check_launch("grad_norm_final_kernel");
 }

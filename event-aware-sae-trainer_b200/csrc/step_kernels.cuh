@@ -703,10 +703,16 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
                             float* __restrict__ g_benc, float* __restrict__ db_enc,
                             int* __restrict__ counter, const SaeB200StepStats* stats,
                             const int* __restrict__ seg_rows = nullptr,
-                            int honor_overflow = 1) {
+                            int honor_overflow = 1, float* __restrict__ row_sumsq = nullptr) {
   // thread tid owns columns [8 U tid, 8 U tid + 8 U): U consecutive 16-byte vectors.
   // Segment sg of the CSR holds feature seg_rows[sg] (feature sg without seg_rows):
   // the aux-loss backward runs the same kernel over the dead features' entries.
+  // row_sumsq != NULL: warp w of the block that finishes feature f writes the sum
+  // of squares of its columns of the final (accumulated) W_dec and W_enc gradient
+  // rows of f to row_sumsq[f * 32 + w], warp 0 adding the final log_threshold and
+  // b_enc gradients of f; warps the block does not have leave their slots alone,
+  // so a reader sums the block's warps only. The global gradient norm then needs
+  // only these F * warps partials instead of another pass over the gradients.
   if (honor_overflow && stats != nullptr && stats->csr_overflow) return;
   __shared__ int s_f[2];
   __shared__ float s_red[2][32][C];   // [chunk parity][warp][entry]
@@ -811,6 +817,7 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
       }
       par ^= 1;
     }
+    float sq = 0.f;
     if (has) {
       const size_t o = static_cast<size_t>(f) * d + static_cast<size_t>(tid) * 8 * U;
 #pragma unroll
@@ -823,6 +830,8 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
             a4.x += u4.x; a4.y += u4.y; a4.z += u4.z; a4.w += u4.w;
           }
           *p = a4;
+          sq = fmaf(a4.x, a4.x, sq); sq = fmaf(a4.y, a4.y, sq);
+          sq = fmaf(a4.z, a4.z, sq); sq = fmaf(a4.w, a4.w, sq);
         }
         float4* p = reinterpret_cast<float4*>(g_wenc + o) + q4;
         float4 e4 = make_float4(ae[4 * q4], ae[4 * q4 + 1], ae[4 * q4 + 2], ae[4 * q4 + 3]);
@@ -831,16 +840,27 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
           e4.x += u4.x; e4.y += u4.y; e4.z += u4.z; e4.w += u4.w;
         }
         *p = e4;
+        sq = fmaf(e4.x, e4.x, sq); sq = fmaf(e4.y, e4.y, sq);
+        sq = fmaf(e4.z, e4.z, sq); sq = fmaf(e4.w, e4.w, sq);
       }
     }
     if (tid == 0) {
       const float gl = -(thr / (eps + eps)) * theta[f];
-      g_logthr[f] = accumulate ? g_logthr[f] + gl : gl;
-      g_benc[f] = accumulate ? g_benc[f] + db : db;
+      const float glv = accumulate ? g_logthr[f] + gl : gl;
+      const float gbv = accumulate ? g_benc[f] + db : db;
+      g_logthr[f] = glv;
+      g_benc[f] = gbv;
       db_enc[f] = db;
+      sq = fmaf(glv, glv, sq);
+      sq = fmaf(gbv, gbv, sq);
+    }
+    if (row_sumsq != nullptr) {
+      sq = warp_sum(sq);
+      if (lane == 0) row_sumsq[static_cast<size_t>(f) * 32 + wid] = sq;
     }
   }
 }
+
 
 
 // ------------------------------------------------------------------ decode
@@ -1409,6 +1429,30 @@ __global__ void __launch_bounds__(512)
       acc = fmaf(v.w, v.w, acc);
     }
     for (int64_t i = n4 * 4 + tid; i < n; i += stride) acc = fmaf(p[i], p[i], acc);
+  }
+  const float s = block_sum(acc, s_tmp);
+  if (threadIdx.x == 0) part[blockIdx.x] = s;
+}
+
+// Sum of squares for the global gradient norm after the sampled backward:
+// part[block] = sum of the row_sumsq partials (32 slots per feature, the first
+// n_warps of each filled) + the squares of the gradients in gl (those the
+// sampled backward does not cover: the b_dec gradient, and a W_dec gradient
+// buffer when the decoder is frozen). Fixed order: deterministic.
+__global__ void __launch_bounds__(512)
+    grad_sumsq_rows_kernel(const float* __restrict__ row_sumsq, int64_t n_features, int n_warps,
+                           GradList gl, float* __restrict__ part) {
+  __shared__ float s_tmp[33];
+  float acc = 0.f;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t n_slots = n_features * n_warps;
+  for (int64_t i = tid; i < n_slots; i += stride)
+    acc += row_sumsq[(i / n_warps) * 32 + i % n_warps];
+  for (int k = 0; k < 5; ++k) {
+    const float* p = gl.p[k];
+    if (p == nullptr) continue;
+    for (int64_t i = tid; i < gl.n[k]; i += stride) acc = fmaf(p[i], p[i], acc);
   }
   const float s = block_sum(acc, s_tmp);
   if (threadIdx.x == 0) part[blockIdx.x] = s;

@@ -199,6 +199,9 @@ _SIGNATURES = {
     "sae_b200_clip_from_sumsq": ([c_void_p, c_float, c_void_p, c_void_p], c_int),
     "sae_b200_grad_norm": (
         [POINTER(Model), POINTER(Grads), c_float, c_void_p, c_size_t, c_void_p, c_void_p], c_int),
+    "sae_b200_grad_norm_sampled": (
+        [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_float,
+         c_void_p, c_size_t, c_void_p, c_void_p], c_int),
     "sae_b200_adam_step": (
         [POINTER(Model), POINTER(Grads), POINTER(AdamState), POINTER(AdamTensor), c_void_p,
          c_void_p], c_int),

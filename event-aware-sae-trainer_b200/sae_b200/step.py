@@ -360,7 +360,13 @@ class FusedStep:
         if ahead:
             sparse_backward()
             if after_backward is not None:
-                after_backward()
+                # the norm from the backward's per-feature sums of squares; if the
+                # CSR overflowed, the dense redo below queues the full norm again
+                self._rows_cfg = cfg
+                try:
+                    after_backward()
+                finally:
+                    self._rows_cfg = None
         st = self._wait_stats(pending)
         self.nnz_last = st["nnz"]
         redone = not ahead
@@ -391,9 +397,17 @@ class FusedStep:
         return st
 
     def grad_norm(self, max_norm: float = 1.0) -> None:
-        """Global L2 norm of all gradients + clip coefficient, on the device."""
+        """Global L2 norm of all gradients + clip coefficient, on the device.
+        Straight after a sampled backward (no aux loss) it is summed from that
+        backward's per-feature partials instead of a pass over the gradients."""
         model = self.sae._model_struct(need_shadows=False)
         grads = self._grads_struct()
+        cfg = getattr(self, "_rows_cfg", None)
+        if cfg is not None:
+            L.call("sae_b200_grad_norm_sampled", ctypes.byref(model), ctypes.byref(grads),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, float(max_norm),
+                   L.ptr(self.norm_ws), self.norm_ws.numel(), L.ptr(self.stats), _stream())
+            return
         L.call("sae_b200_grad_norm", ctypes.byref(model), ctypes.byref(grads), float(max_norm),
                L.ptr(self.norm_ws), self.norm_ws.numel(), L.ptr(self.stats), _stream())
 

@@ -226,6 +226,21 @@ int sae_b200_grad_norm(const SaeB200Model* model, const SaeB200Grads* grads, flo
                        void* workspace, size_t workspace_bytes, SaeB200StepStats* stats,
                        void* stream);
 
+/* The same norm and clip coefficient (clip_grad_norm_, 3049) straight after
+ * sae_b200_train_backward with grad_feat_gemm = 0: the sampled backward leaves
+ * per-feature sums of squares of the final W_enc, W_dec, b_enc and
+ * log_threshold gradients in the step workspace, so this call reads those
+ * F x warps partials and the b_dec gradient instead of all the gradients
+ * again. Valid only when that backward ran to completion on these gradients
+ * (no CSR overflow, no aux backward or other gradient edit since); otherwise
+ * call sae_b200_grad_norm. cfg and workspace: those of the backward;
+ * norm_workspace: SAE_GRAD_NORM_WORKSPACE_BYTES. */
+int sae_b200_grad_norm_sampled(const SaeB200Model* model, const SaeB200Grads* grads,
+                               const SaeB200StepConfig* cfg, const void* workspace,
+                               size_t workspace_bytes, float max_norm, void* norm_workspace,
+                               size_t norm_workspace_bytes, SaeB200StepStats* stats,
+                               void* stream);
+
 /* Inference: encoder GEMM + JumpReLU gate + gathered decode, no loss and no
  * backward state: x_hat_out [n_tokens, d] fp32 = bf16(gathered decoder sum) +
  * b_dec, the forward of the module (encode 910-912 + decode 922-950; also the

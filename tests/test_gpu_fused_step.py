@@ -441,3 +441,33 @@ def test_entries_only_pre_store_matches_full_store(name, force_simt):
     word = np.repeat(pad.reshape(F, nw, 32).any(-1), 32, axis=1)[:, :B]
     np.testing.assert_array_equal(pre_e[word], pre_f[word])
     assert np.isnan(pre_e[~word]).all()
+
+
+@pytest.mark.parametrize("case", ["single", "accum2", "frozen_decoder", "overflow"])
+def test_norm_from_backward_partials_matches_full_pass(case):
+    """The clip norm queued straight after the sampled backward is summed from
+    that backward's per-feature partials (sae_b200_grad_norm_sampled); it must
+    equal the norm of a full pass over the final gradients (sae_b200_grad_norm)
+    up to the fp32 summation order, after accumulation, with a frozen decoder,
+    and when an overflowing microbatch sends the backward down the dense path
+    (which queues the full pass again)."""
+    name = "ste_f64_accum2" if case == "accum2" else "super_f32_tiles"
+    g = load_golden(name)
+    sae, opt, fs = build(g, csr_capacity=16 if case == "overflow" else None)
+    if case == "frozen_decoder":
+        sae.W_dec.weight.requires_grad_(False)
+    cfg = oracle_cfg(g)
+    n = 2 if case == "accum2" else 1
+    xs = [torch.from_numpy(g[f"x{i}"].astype(np.float32)).cuda() for i in range(n)]
+    fs.max_tokens = max(x.shape[0] for x in xs)
+    for i, x in enumerate(xs):
+        fs.microbatch(x, accum_steps=n, first=(i == 0), lambda_l0=cfg.lambda_l0,
+                      al_mu=cfg.al_mu, target_l0=cfg.target_l0,
+                      after_backward=(lambda: fs.grad_norm(1.0)) if i == n - 1 else None)
+    fused = fs.read_stats()
+    fs.grad_norm(1.0)
+    full = fs.read_stats()
+    assert fs.dense_fallbacks == (1 if case == "overflow" else 0)
+    assert full["grad_norm"] > 0
+    assert fused["grad_norm"] == pytest.approx(full["grad_norm"], rel=1e-5)
+    assert fused["clip_coef"] == pytest.approx(full["clip_coef"], rel=1e-5)
