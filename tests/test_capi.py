@@ -83,3 +83,30 @@ def test_full_pre_store_and_pre_flag_are_checked_without_a_device():
                                            256, 1 << 30, 256, 256, None)
     assert rc == L.SAE_ERR_INVALID_ARGUMENT
     assert b"pre_entries_only" in lib.sae_b200_last_error()
+
+
+def test_norm_from_backward_partials_is_checked_without_a_device():
+    """sae_b200_grad_norm_sampled validates its arguments before any launch:
+    NULL gradients, a GEMM-backward config (whose backward writes no
+    per-feature partials), a too-small norm workspace and a step workspace
+    smaller than the backward's layout are refused."""
+    from sae_b200 import _lib as L
+    lib = L.load()
+    m = L.Model(64, 128, 256, 256, 256, 256, 256, 256, 256)
+    g = L.Grads(256, 256, 256, 256, 256)
+    ok = L.StepConfig(16, 1024, 0.0, 0.0, 0.0, 0.1, 1, 0, 1, 0, 0, 1)
+    gemm = L.StepConfig(16, 1024, 0.0, 0.0, 0.0, 0.1, 1, 0, 1, 0, 1, 0)
+    norm_ws = L.GRAD_NORM_WORKSPACE_BYTES
+    assert lib.sae_b200_grad_norm_sampled(ctypes.byref(m), None, ctypes.byref(ok), 256, 1 << 30,
+                                          1.0, 256, norm_ws, 256, None) \
+        == L.SAE_ERR_INVALID_ARGUMENT
+    assert lib.sae_b200_grad_norm_sampled(ctypes.byref(m), ctypes.byref(g), ctypes.byref(gemm),
+                                          256, 1 << 30, 1.0, 256, norm_ws, 256, None) \
+        == L.SAE_ERR_INVALID_ARGUMENT
+    assert b"grad_feat_gemm" in lib.sae_b200_last_error()
+    assert lib.sae_b200_grad_norm_sampled(ctypes.byref(m), ctypes.byref(g), ctypes.byref(ok),
+                                          256, 1 << 30, 1.0, 256, 4, 256, None) \
+        == L.SAE_ERR_WORKSPACE_TOO_SMALL
+    assert lib.sae_b200_grad_norm_sampled(ctypes.byref(m), ctypes.byref(g), ctypes.byref(ok),
+                                          256, 64, 1.0, 256, norm_ws, 256, None) \
+        == L.SAE_ERR_WORKSPACE_TOO_SMALL
