@@ -324,7 +324,9 @@ class FusedStep:
         dense path (an active set larger than the workspace is never
         truncated). ``after_backward`` (e.g. the gradient norm) is queued right
         after the backward, before the host waits, and again if the backward
-        had to be redone."""
+        had to be redone. A ``grad_norm`` that it calls straight after the
+        sampled backward is summed from that backward's per-feature partials,
+        so it must not edit the gradients before that call.
         sae = self.sae
         x = self._check_input(x)
         n = x.shape[0]
