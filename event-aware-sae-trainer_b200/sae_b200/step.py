@@ -326,7 +326,7 @@ class FusedStep:
         after the backward, before the host waits, and again if the backward
         had to be redone. A ``grad_norm`` that it calls straight after the
         sampled backward is summed from that backward's per-feature partials,
-        so it must not edit the gradients before that call.
+        so it must not edit the gradients before that call."""
         sae = self.sae
         x = self._check_input(x)
         n = x.shape[0]
