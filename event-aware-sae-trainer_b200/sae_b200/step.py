@@ -215,6 +215,9 @@ class FusedStep:
         self.dense_fallbacks = 0
         # dead-feature aux loss state (set per step by set_aux)
         self._aux = None          # (dead int32 cuda tensor, k, coeff) or None
+        # the StepConfig of a sampled backward whose per-feature sums of squares
+        # grad_norm may use (set only while its after_backward runs)
+        self._rows_cfg = None
         self._aux_ws = None
         self._x_hat = None
 
