@@ -11,10 +11,12 @@ weight_decay, not AdamW), one library call for all five tensors.
 
 ``FusedStep`` is the loop body of ``train_sae_on_activations``
 (sae_trainer_rolling.py:2840-3090) as a handful of library calls per
-microbatch: encoder GEMM + JumpReLU epilogue, gathered decode + loss,
-grad_feat GEMM + STE epilogue + sparse weight gradients, global gradient norm,
-Adam fused with the decoder-column / encoder-row renormalisation. No [B, F]
-tensor other than the bf16 pre-activations is ever written.
+microbatch: encoder GEMM + JumpReLU epilogue, gathered decode + loss, the
+sampled backward (grad_feat on the active and in-band entries only, or the
+dense grad_feat GEMM) with the STE and the sparse weight gradients, the global
+gradient norm (summed from the sampled backward's per-feature partials), Adam
+fused with the decoder-column / encoder-row renormalisation. No [B, F] tensor
+other than the bf16 pre-activations is ever written.
 """
 from __future__ import annotations
 
