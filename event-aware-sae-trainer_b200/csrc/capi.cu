@@ -70,6 +70,7 @@ struct DeviceInfo {
 };
 
 constexpr int kMaxDevices = 64;
+constexpr int kMaxGridY = 65535;   // CUDA's limit on gridDim.y
 
 DeviceInfo device_info() {
   static std::mutex mu;
@@ -1599,6 +1600,10 @@ int sae_b200_jumprelu_backward(const void* pre, int pre_dtype, const float* log_
       n_tokens <= 0 || n_features <= 0 || !(eps > 0.f))
     return fail(SAE_ERR_INVALID_ARGUMENT, "invalid jumprelu_backward arguments");
   const int64_t slabs = (n_tokens + JB_TOK - 1) / JB_TOK;
+  if (slabs > kMaxGridY)
+    return fail(SAE_ERR_UNSUPPORTED_SHAPE,
+                "jumprelu_backward takes at most %d token slabs of %d (n_tokens <= %lld)",
+                kMaxGridY, JB_TOK, static_cast<long long>(kMaxGridY) * JB_TOK);
   const size_t need = static_cast<size_t>(slabs * n_features) * sizeof(float);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "jumprelu_backward needs %zu workspace bytes", need);
@@ -1671,6 +1676,10 @@ int sae_b200_jumprelu_backward_static(const void* pre, int pre_dtype, const floa
   if (pre_dtype != SAE_DTYPE_BF16 && pre_dtype != SAE_DTYPE_F32)
     return fail(SAE_ERR_INVALID_ARGUMENT, "pre_dtype must be F32 or BF16");
   const int64_t slabs = (n_tokens + JB_TOK - 1) / JB_TOK;
+  if (slabs > kMaxGridY)
+    return fail(SAE_ERR_UNSUPPORTED_SHAPE,
+                "jumprelu_backward_static takes at most %d token slabs of %d (n_tokens <= %lld)",
+                kMaxGridY, JB_TOK, static_cast<long long>(kMaxGridY) * JB_TOK);
   if (n_features > SAE_JUMPRELU_BWD_STATIC_FLOATS ||
       slabs > SAE_JUMPRELU_BWD_STATIC_FLOATS / n_features)
     return fail(SAE_ERR_UNSUPPORTED_SHAPE,

@@ -384,7 +384,9 @@ int sae_b200_jumprelu_forward(const void* pre, int pre_dtype, const float* log_t
 /* Straight-through backward of the JumpReLU (hooks 784-825 / _JumpReLUWithGate
  * 700-731): grad_pre = grad_feat * gate; combined = pre * grad_feat + grad_gate;
  * grad_log_threshold += -sum_t where(|pre - theta| < eps, combined) / (2 eps) * theta.
- * grad_feat / grad_gate may be NULL (treated as zero); grad_pre_out may be NULL. */
+ * grad_feat / grad_gate may be NULL (treated as zero); grad_pre_out may be NULL.
+ * n_tokens <= 65535 * 256 (one grid row per 256-token slab); larger calls
+ * return SAE_ERR_UNSUPPORTED_SHAPE. */
 int sae_b200_jumprelu_backward(const void* pre, int pre_dtype, const float* log_threshold,
                                int64_t n_tokens, int64_t n_features, const float* grad_feat,
                                const float* grad_gate, float eps, void* grad_pre_out,
@@ -404,7 +406,8 @@ int sae_b200_jumprelu_backward(const void* pre, int pre_dtype, const float* log_
  * until the process exits.
  *  - Limit: ceil(n_tokens / 256) * n_features must not exceed
  *    SAE_JUMPRELU_BWD_STATIC_FLOATS (e.g. 65536 tokens x 4096 features);
- *    larger calls return SAE_ERR_UNSUPPORTED_SHAPE and do nothing.
+ *    larger calls return SAE_ERR_UNSUPPORTED_SHAPE and do nothing, as do
+ *    calls with more than 65535 * 256 tokens (one grid row per slab).
  *  - The first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress, with that device current); make that first call
  *    before capturing any stream into a CUDA graph.

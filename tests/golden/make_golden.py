@@ -5,10 +5,10 @@ Runs the reference trainer's own SAE module and step sequence
 decode 903-950, the loss lines 2954-2974, loss.backward(), clip_grad_norm_
 3049, the 4-group torch.optim.Adam 2536-2541 and the renormalisations
 3086-3090) on CPU and stores inputs and outputs as .npz files beside this
-script. It needs the reference checkout (default /root/reference, or
-$SAE_REFERENCE_DIR) and is run by hand:
+script. It needs the reference checkout, named by $SAE_REFERENCE_DIR, and is
+run by hand:
 
-    python tests/golden/make_golden.py
+    SAE_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py
 
 The fixtures are committed; nothing at test time imports the reference.
 """
@@ -23,7 +23,10 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("SAE_REFERENCE_DIR", "/root/reference"))
+if not os.environ.get("SAE_REFERENCE_DIR"):
+    sys.exit("set SAE_REFERENCE_DIR to a checkout of the reference trainer "
+             "(the directory holding sae_trainer_rolling.py)")
+REF = Path(os.environ["SAE_REFERENCE_DIR"])
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(HERE.parents[1]))
 

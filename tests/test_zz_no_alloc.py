@@ -12,25 +12,14 @@ point, sae_b200_jumprelu_backward, on two calls in a row: the second call runs
 on the array exactly as the first call left it. The file is named so that
 pytest collects it last.
 """
-import ctypes
-
-import numpy as np
 import pytest
 import torch
-
-REL_TOL = 2e-2   # the suite's bf16 tolerance; the two entry points run the same kernels
 
 
 def _lib():
     from sae_b200 import _lib as L
     L.load()
     return L
-
-
-def _rel(a, b):
-    a = a.double().cpu()
-    b = b.double().cpu()
-    return float((a - b).norm() / b.norm().clamp(min=1e-30))
 
 
 def _inputs(n_tokens, n_features, seed):
@@ -63,8 +52,11 @@ def _run(L, static, pre, log_thr, gf, gg, eps=0.2):
 @pytest.mark.gpu
 def test_static_scratch_matches_workspace_entry_point_twice():
     L = _lib()
-    # Two calls in a row; the second is smaller, so it also runs over partial
-    # sums the first call left in the shared array.
+    # Two calls in a row; the second is smaller (3 slabs x 384 features cover
+    # fewer slots than the first call's 12 x 1024), so it runs over partial
+    # sums the first call left in the shared array. Both entry points run the
+    # same two kernels in the same order, so every output must match bit for
+    # bit: a stale partial sum would show up as a difference.
     for n, F, seed in ((3000, 1024, 1), (700, 384, 2)):
         pre, log_thr, gf, gg = _inputs(n, F, seed)
         got_pre, got_lt = _run(L, True, pre, log_thr, gf, gg)
@@ -73,7 +65,7 @@ def test_static_scratch_matches_workspace_entry_point_twice():
         assert L.device_status() == 0
         assert torch.equal(got_pre, ref_pre)
         assert ref_lt.abs().max() > 0
-        assert _rel(got_lt, ref_lt) < REL_TOL
+        assert torch.equal(got_lt, ref_lt)
 
 
 def test_static_scratch_rejects_oversize_without_touching_the_device():
@@ -87,3 +79,23 @@ def test_static_scratch_rejects_oversize_without_touching_the_device():
                0.2, fake, fake, None)
     assert err.value.code == L.SAE_ERR_UNSUPPORTED_SHAPE
     assert "at most" in str(err.value)
+
+
+@pytest.mark.parametrize("static", [True, False])
+def test_more_token_slabs_than_grid_rows_are_refused(static):
+    """A small dictionary with a huge token count fits the static array
+    (65536 slabs x 8 features) but not CUDA's 65535 grid rows: both entry
+    points refuse it with SAE_ERR_UNSUPPORTED_SHAPE before any CUDA call."""
+    L = _lib()
+    n, F = 65536 * 256, 8
+    assert ((n + 255) // 256) * F <= L.JUMPRELU_BWD_STATIC_FLOATS
+    fake = 1 << 20
+    with pytest.raises(L.SaeB200Error) as err:
+        if static:
+            L.call("sae_b200_jumprelu_backward_static", fake, L.DTYPE_BF16, fake, n, F, fake,
+                   fake, 0.2, fake, fake, None)
+        else:
+            L.call("sae_b200_jumprelu_backward", fake, L.DTYPE_BF16, fake, n, F, fake, fake, 0.2,
+                   fake, fake, fake, 1 << 40, None)
+    assert err.value.code == L.SAE_ERR_UNSUPPORTED_SHAPE
+    assert "slabs" in str(err.value)
