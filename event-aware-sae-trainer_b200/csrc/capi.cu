@@ -21,6 +21,9 @@
 #include "aux_kernels.cuh"
 #include "peer_kernels.cuh"
 #include "tile_gemm.cuh"
+#include "gemm_kernels.cuh"
+
+#include <type_traits>
 
 using namespace sae;
 
@@ -334,17 +337,29 @@ int aux_tmap(CUtensorMap* m, const bf16* aux, int64_t F, int64_t B, uint32_t box
   return make_tmap(m, aux, B, F, box_tokens, TILE_M, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+// Epilogues that bounds-check their rows (kRowGuard) take any row count on
+// the paired kernel: rows past F are TMA zero fill and never stored.
+template <class E, class = void>
+struct RowGuard : std::false_type {};
+template <class E>
+struct RowGuard<E, std::void_t<decltype(E::kRowGuard)>> : std::bool_constant<E::kRowGuard> {};
+
+// w_pitch / t_pitch: row pitch of the operands in elements (0: d, dense rows).
+// The contraction runs over ceil(d / TILE_K) slabs; TMA zero-fills past d.
 template <class Epi>
 int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64_t d,
                      const Epi& e, bool use_tc, cudaStream_t stream, int timer = -1,
-                     const bf16* aux = nullptr) {
+                     const bf16* aux = nullptr, int64_t w_pitch = 0, int64_t t_pitch = 0) {
   const int m_tiles = static_cast<int>((F + TILE_M - 1) / TILE_M);
   const int n_tiles = static_cast<int>((B + TILE_N - 1) / TILE_N);
+  const int k_blocks = static_cast<int>((d + TILE_K - 1) / TILE_K);
   if (use_tc) {
     constexpr size_t smem = TcConfig<Epi::kAux>::SMEM;
     CUtensorMap tm_w, tm_t, tm_aux;
-    SAE_TRY(make_tmap(&tm_w, w, F, d, TILE_M));
-    SAE_TRY(make_tmap(&tm_t, tok, B, d, TILE_N));
+    SAE_TRY(make_tmap(&tm_w, w, F, d, TILE_M, TILE_K, CU_TENSOR_MAP_SWIZZLE_128B,
+                      static_cast<uint64_t>(w_pitch)));
+    SAE_TRY(make_tmap(&tm_t, tok, B, d, TILE_N, TILE_K, CU_TENSOR_MAP_SWIZZLE_128B,
+                      static_cast<uint64_t>(t_pitch)));
     if (Epi::kAux != AUX_NONE) {
       if (aux == nullptr) return fail(SAE_ERR_INVALID_ARGUMENT, "tile GEMM side tensor is NULL");
       SAE_TRY(aux_tmap<Epi>(&tm_aux, aux, F, B, TILE_N));
@@ -356,7 +371,7 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
       return fail(SAE_ERR_CUDA, "no usable current device");
-    if (F % (2 * TILE_M) == 0 && pair_mode_enabled()) {
+    if ((F % (2 * TILE_M) == 0 || RowGuard<Epi>::value) && pair_mode_enabled()) {
       // Paired CTAs: one 256-feature x 256-token tile per cluster of two.
       constexpr size_t smem2 = Tc2Config<Epi::kAux>::SMEM;
       static std::once_flag attr2_once[kMaxDevices];
@@ -384,16 +399,17 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
       if (max_clusters > 0) {
         // Each CTA of the pair loads half of the 256-token slab.
         CUtensorMap tm_t_half, tm_aux2 = tm_aux;
-        SAE_TRY(make_tmap(&tm_t_half, tok, B, d, TILE_N / 2));
+        SAE_TRY(make_tmap(&tm_t_half, tok, B, d, TILE_N / 2, TILE_K, CU_TENSOR_MAP_SWIZZLE_128B,
+                          static_cast<uint64_t>(t_pitch)));
         // Side-tile stores go out in 128-token slabs.
         if (Epi::kAux == AUX_STORE)
           SAE_TRY(aux_tmap<Epi>(&tm_aux2, aux, F, B, TC2_STORE_ROWS));
-        const int m_pairs = static_cast<int>(F / (2 * TILE_M));
+        const int m_pairs = static_cast<int>((F + 2 * TILE_M - 1) / (2 * TILE_M));
         const int total_pairs = m_pairs * n_tiles;
         const int clusters = std::min(total_pairs, max_clusters);
         if (timer >= 0) timer_begin(timer, stream);
         tc2_tile_gemm<Epi><<<2 * clusters, TC2_THREADS, smem2, stream>>>(
-            tm_w, tm_t_half, tm_aux2, m_pairs, n_tiles, static_cast<int>(d / TILE_K), e);
+            tm_w, tm_t_half, tm_aux2, m_pairs, n_tiles, k_blocks, e);
         const int rc = check_launch("tc2_tile_gemm");
         if (timer >= 0) timer_end(timer, stream);
         return rc;
@@ -407,8 +423,8 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
     const int total = m_tiles * n_tiles;
     const int grid = std::min(total, device_info().sm_count);
     if (timer >= 0) timer_begin(timer, stream);
-    tc_tile_gemm<Epi><<<grid, TC_THREADS, smem, stream>>>(
-        tm_w, tm_t, tm_aux, m_tiles, n_tiles, static_cast<int>(d / TILE_K), e);
+    tc_tile_gemm<Epi><<<grid, TC_THREADS, smem, stream>>>(tm_w, tm_t, tm_aux, m_tiles, n_tiles,
+                                                          k_blocks, e);
     const int rc = check_launch("tc_tile_gemm");
     if (timer >= 0) timer_end(timer, stream);
     return rc;
@@ -422,10 +438,76 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
   return rc;
 }
 
+// C = alpha * A B^T + beta * C (+ bias) on the tcgen05 tile GEMM. A [M, K] and
+// B [N, K] bf16, K-major, rows lda / ldb elements apart (multiples of 8, bases
+// 16-byte aligned); C row-major with rows ldc apart, fp32 or bf16.
+int tc_store_gemm(int64_t M, int64_t N, int64_t K, const bf16* A, int64_t lda, const bf16* B,
+                  int64_t ldb, void* C, int64_t ldc, int c_bf16, float alpha, float beta,
+                  const float* bias, int bias_per_row, cudaStream_t stream, int timer = -1) {
+  StoreEpi e{};
+  e.c = C;
+  e.ldc = ldc;
+  e.rows = M;
+  e.cols = N;
+  e.alpha = alpha;
+  e.beta = beta;
+  e.bias = bias;
+  e.bias_per_row = bias_per_row;
+  e.c_bf16 = c_bf16;
+  const int64_t eb = c_bf16 ? 2 : 4;
+  e.vec = (aligned16(C) && (ldc * eb) % 16 == 0) ? 1 : 0;
+  return launch_tile_gemm(A, B, M, N, K, e, true, stream, timer, nullptr, lda, ldb);
+}
+
+int transpose_bf16(const bf16* src, int64_t rows, int64_t cols, int64_t lds, bf16* dst,
+                   int64_t ldd, cudaStream_t stream);
+
+// SAE_B200_GEMM_SIMT=1 keeps sae_b200_gemm on CUDA cores.
+bool gemm_simt_forced() {
+  static const bool on = [] {
+    const char* v = std::getenv("SAE_B200_GEMM_SIMT");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+
+// Products the tile GEMM takes: bf16 operands stored K-major (contiguous
+// contraction dimension, 16-byte aligned bases and row pitches), an output
+// with one unit stride, and sizes worth a persistent tensor-core launch.
+bool gemm_tc_eligible(int64_t M, int64_t N, int64_t K, const void* A, int a_dtype, int64_t sam,
+                      int64_t sak, const void* B, int b_dtype, int64_t sbn, int64_t sbk,
+                      int64_t scm, int64_t scn) {
+  if (gemm_simt_forced() || device_info().major != 10) return false;
+  if (a_dtype != SAE_DTYPE_BF16 || b_dtype != SAE_DTYPE_BF16) return false;
+  if (M < TILE_M || N < TILE_M || K < TILE_K) return false;
+  if (M > (int64_t(1) << 31) - 1 - TILE_N || N > (int64_t(1) << 31) - 1 - TILE_N) return false;
+  if (sak != 1 || sbk != 1 || sam < K || sbn < K || sam % 8 != 0 || sbn % 8 != 0) return false;
+  if (!aligned16(A) || !aligned16(B)) return false;
+  return scn == 1 || scm == 1;
+}
+
 int grid_for(int64_t n, int threads, int per_sm = 8) {
   const int64_t want = (n + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(std::max(1, device_info().sm_count)) * per_sm;
   return static_cast<int>(std::max<int64_t>(1, std::min(want, cap)));
+}
+
+int transpose_bf16(const bf16* src, int64_t rows, int64_t cols, int64_t lds, bf16* dst,
+                   int64_t ldd, cudaStream_t stream) {
+  const int vec = (aligned16(src) && aligned16(dst) && lds % 8 == 0 && ldd % 8 == 0) ? 1 : 0;
+  const int64_t tiles = ((rows + TP_TILE - 1) / TP_TILE) * ((cols + TP_TILE - 1) / TP_TILE);
+  const int grid = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>(tiles, int64_t(device_info().sm_count) * 8)));
+  transpose_bf16_kernel<<<grid, 256, 0, stream>>>(src, rows, cols, lds, dst, ldd, vec);
+  return check_launch("transpose_bf16_kernel");
+}
+
+// Scratch of the dense weight-gradient path: the dense [F, ldp] bf16 operand
+// (dpre, then the gated pre), and, on the tensor-core path, xc^T and go^T
+// ([d, ldp] bf16 each: the tokens become the contraction's K-major dimension).
+size_t dense_scratch_need(int64_t B, int64_t d, int64_t F, bool tc) {
+  const size_t ldp = static_cast<size_t>(pre_pitch(B));
+  return (static_cast<size_t>(F) * ldp + (tc ? 2 * static_cast<size_t>(d) * ldp : 0)) * 2;
 }
 
 int vec_threads(int64_t d) {
@@ -1132,8 +1214,8 @@ int sae_b200_shard_finish_forward(const SaeB200Model* model, const void* x, int 
 // summed across GPUs, with the go sum and the accumulated value counted once.
 static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
                            const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
-                           SaeB200StepStats* stats, bf16* dense_scratch, cudaStream_t stream,
-                           int bdec_owner = 1) {
+                           SaeB200StepStats* stats, bf16* dense_scratch,
+                           size_t dense_scratch_bytes, cudaStream_t stream, int bdec_owner = 1) {
   SAE_TRY(check_model(model, true));
   SAE_TRY(check_cfg(cfg));
   SAE_TRY(check_fused_shape(model));
@@ -1148,6 +1230,12 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
   const int64_t B = cfg->n_tokens, d = model->d_in, F = model->n_features;
   const Layout L = make_layout(B, d, F, cfg->csr_capacity);
   SAE_TRY(check_ws(L, workspace, workspace_bytes));
+  // the dense weight gradients run on the tcgen05 tile GEMM unless the caller
+  // asked for CUDA cores (or the device is not an sm_100)
+  const bool dense_tc = !cfg->force_simt && device_info().major == 10;
+  if (dense_scratch != nullptr && dense_scratch_bytes < dense_scratch_need(B, d, F, dense_tc))
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "dense_scratch has %zu bytes, needs %zu",
+                dense_scratch_bytes, dense_scratch_need(B, d, F, dense_tc));
   const Ws w = carve(workspace, L);
   const int n_tiles = static_cast<int>((B + TILE_N - 1) / TILE_N);
   const int acc = cfg->accumulate ? 1 : 0;
@@ -1236,10 +1324,28 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
 #undef SAE_SCATTER
     return check_launch("scatter_weight_grads_kernel");
   }
-  // dense fallback: dW_enc = dpre^T xc, dW_dec = acts^T go
+  // dense fallback: dW_enc = dpre^T xc, dW_dec = acts^T go, contractions over
+  // the tokens. dense_scratch holds [F, ldp] (feature-major, like pre), whose
+  // rows are already K-major; xc and go [B, d] are transposed to [d, ldp].
+  if (dense_tc) {
+    const int64_t ldp = pre_pitch(B);
+    bf16* xcT = dense_scratch + static_cast<size_t>(F) * ldp;
+    bf16* goT = xcT + static_cast<size_t>(d) * ldp;
+    SAE_TRY(transpose_bf16(w.xc, B, d, d, xcT, ldp, stream));
+    SAE_TRY(tc_store_gemm(F, d, B, dense_scratch, ldp, xcT, ldp, grads->W_enc, d, 0, 1.f,
+                          acc ? 1.f : 0.f, nullptr, 0, stream));
+    if (g_wdec != nullptr) {
+      gated_pre_kernel<<<grid_for(B * F, 256), 256, 0, stream>>>(w.pre, w.theta, B, F, ldp,
+                                                                 dense_scratch);
+      SAE_TRY(check_launch("gated_pre_kernel"));
+      SAE_TRY(transpose_bf16(w.go, B, d, d, goT, ldp, stream));
+      SAE_TRY(tc_store_gemm(F, d, B, dense_scratch, ldp, goT, ldp, g_wdec, d, 0, 1.f,
+                            acc ? 1.f : 0.f, nullptr, 0, stream));
+    }
+    return SAE_OK;
+  }
   {
     dim3 grid(static_cast<unsigned>((d + GG_T - 1) / GG_T), static_cast<unsigned>((F + GG_T - 1) / GG_T));
-    // dense_scratch holds [F, ldp] (feature-major, like pre)
     const int64_t ldp = pre_pitch(B);
     gemm_generic_kernel<bf16, bf16, float><<<grid, 256, 0, stream>>>(
         F, d, B, 1.f, dense_scratch, ldp, 1, w.xc, 1, d, acc ? 1.f : 0.f, grads->W_enc, d, 1,
@@ -1261,7 +1367,7 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
 int sae_b200_train_backward(const SaeB200Model* model, const SaeB200Grads* grads,
                             const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
                             SaeB200StepStats* stats, void* stream) {
-  return backward_common(model, grads, cfg, workspace, workspace_bytes, stats, nullptr,
+  return backward_common(model, grads, cfg, workspace, workspace_bytes, stats, nullptr, 0,
                          static_cast<cudaStream_t>(stream));
 }
 
@@ -1287,26 +1393,35 @@ int sae_b200_store_full_pre(const SaeB200Model* model, const SaeB200StepConfig* 
                                   tc_eligible(c.d, c.F, cfg->force_simt), stream);
 }
 
+int sae_b200_dense_scratch_bytes(int64_t n_tokens, int64_t d_in, int64_t n_features,
+                                 size_t* bytes_out) {
+  if (bytes_out == nullptr || n_tokens <= 0 || d_in <= 0 || n_features <= 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid dense_scratch_bytes arguments");
+  *bytes_out = dense_scratch_need(n_tokens, d_in, n_features, true);
+  return SAE_OK;
+}
+
 int sae_b200_train_backward_dense(const SaeB200Model* model, const SaeB200Grads* grads,
                                   const SaeB200StepConfig* cfg, void* workspace,
                                   size_t workspace_bytes, SaeB200StepStats* stats,
-                                  void* dense_scratch, void* stream) {
+                                  void* dense_scratch, size_t dense_scratch_bytes, void* stream) {
   if (dense_scratch == nullptr || !aligned16(dense_scratch))
     return fail(SAE_ERR_INVALID_ARGUMENT, "dense_scratch must be a 16-byte aligned buffer");
   return backward_common(model, grads, cfg, workspace, workspace_bytes, stats,
-                         static_cast<bf16*>(dense_scratch), static_cast<cudaStream_t>(stream));
+                         static_cast<bf16*>(dense_scratch), dense_scratch_bytes,
+                         static_cast<cudaStream_t>(stream));
 }
 
 int sae_b200_shard_backward(const SaeB200Model* model, const SaeB200Grads* grads,
                             const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
                             SaeB200StepStats* stats, int shard_rank, void* dense_scratch,
-                            void* stream) {
+                            size_t dense_scratch_bytes, void* stream) {
   if (shard_rank < 0) return fail(SAE_ERR_INVALID_ARGUMENT, "shard_rank must be >= 0");
   if (dense_scratch != nullptr && !aligned16(dense_scratch))
     return fail(SAE_ERR_MISALIGNED, "dense_scratch must be 16-byte aligned");
   return backward_common(model, grads, cfg, workspace, workspace_bytes, stats,
-                         static_cast<bf16*>(dense_scratch), static_cast<cudaStream_t>(stream),
-                         shard_rank == 0 ? 1 : 0);
+                         static_cast<bf16*>(dense_scratch), dense_scratch_bytes,
+                         static_cast<cudaStream_t>(stream), shard_rank == 0 ? 1 : 0);
 }
 
 int sae_b200_grad_norm(const SaeB200Model* model, const SaeB200Grads* grads, float max_norm,
@@ -1716,6 +1831,19 @@ int sae_b200_gemm(int64_t M, int64_t N, int64_t K, float alpha, const void* A, i
   if (M <= 0 || N <= 0 || K < 0 || A == nullptr || B == nullptr || C == nullptr)
     return fail(SAE_ERR_INVALID_ARGUMENT, "invalid gemm arguments");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (a_dtype < 0 || a_dtype > 1 || b_dtype < 0 || b_dtype > 1 || c_dtype < 0 || c_dtype > 1)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "gemm dtype must be F32 or BF16");
+  // bf16 operands with the contraction dimension contiguous go to the tcgen05
+  // tile GEMM: rows of the tile are the output's contiguous-row dimension
+  // (C^T = B A^T when C is column-major).
+  if (gemm_tc_eligible(M, N, K, A, a_dtype, sam, sak, B, b_dtype, sbn, sbk, scm, scn)) {
+    if (scn == 1)
+      return tc_store_gemm(M, N, K, static_cast<const bf16*>(A), sam,
+                           static_cast<const bf16*>(B), sbn, C, scm, c_dtype == SAE_DTYPE_BF16,
+                           alpha, beta, bias_n, 0, stream);
+    return tc_store_gemm(N, M, K, static_cast<const bf16*>(B), sbn, static_cast<const bf16*>(A),
+                         sam, C, scn, c_dtype == SAE_DTYPE_BF16, alpha, beta, bias_n, 1, stream);
+  }
   dim3 grid(static_cast<unsigned>((N + GG_T - 1) / GG_T), static_cast<unsigned>((M + GG_T - 1) / GG_T));
   if (grid.y > 65535) return fail(SAE_ERR_UNSUPPORTED_SHAPE, "gemm: M too large");
   const int code = a_dtype * 4 + b_dtype * 2 + c_dtype;
@@ -1725,8 +1853,6 @@ int sae_b200_gemm(int64_t M, int64_t N, int64_t K, float alpha, const void* A, i
         M, N, K, alpha, static_cast<const TA*>(A), sam, sak, static_cast<const TB*>(B), sbn, \
         sbk, beta, static_cast<TC*>(C), scm, scn, bias_n);                                   \
     break;
-  if (a_dtype < 0 || a_dtype > 1 || b_dtype < 0 || b_dtype > 1 || c_dtype < 0 || c_dtype > 1)
-    return fail(SAE_ERR_INVALID_ARGUMENT, "gemm dtype must be F32 or BF16");
   switch (code) {
     SAE_GEMM_CASE(0, float, float, float)
     SAE_GEMM_CASE(1, float, float, bf16)
@@ -1739,6 +1865,15 @@ int sae_b200_gemm(int64_t M, int64_t N, int64_t K, float alpha, const void* A, i
   }
 #undef SAE_GEMM_CASE
   return check_launch("gemm_generic_kernel");
+}
+
+int sae_b200_transpose(const void* src, int dtype, int64_t rows, int64_t cols, int64_t lds,
+                       void* dst, int64_t ldd, void* stream_) {
+  if (src == nullptr || dst == nullptr || rows <= 0 || cols <= 0 || lds < cols || ldd < rows)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "invalid transpose arguments");
+  if (dtype != SAE_DTYPE_BF16) return fail(SAE_ERR_INVALID_ARGUMENT, "transpose takes bf16");
+  return transpose_bf16(static_cast<const bf16*>(src), rows, cols, lds, static_cast<bf16*>(dst),
+                        ldd, static_cast<cudaStream_t>(stream_));
 }
 
 int sae_b200_column_sum(const void* X, int x_dtype, int64_t rows, int64_t cols, float alpha,

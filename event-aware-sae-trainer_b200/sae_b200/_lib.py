@@ -160,9 +160,10 @@ _SIGNATURES = {
          c_void_p], c_int),
     "sae_b200_store_full_pre": (
         [POINTER(Model), POINTER(StepConfig), c_void_p, c_size_t, c_void_p], c_int),
+    "sae_b200_dense_scratch_bytes": ([c_int64, c_int64, c_int64, POINTER(c_size_t)], c_int),
     "sae_b200_train_backward_dense": (
         [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
-         c_void_p, c_void_p], c_int),
+         c_void_p, c_size_t, c_void_p], c_int),
     "sae_b200_encode_decode": (
         [POINTER(Model), c_void_p, c_int, c_int64, c_void_p, c_size_t, c_void_p, c_void_p,
          c_void_p, c_void_p], c_int),
@@ -193,7 +194,7 @@ _SIGNATURES = {
          c_void_p, c_void_p, c_void_p], c_int),
     "sae_b200_shard_backward": (
         [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_void_p, c_int,
-         c_void_p, c_void_p], c_int),
+         c_void_p, c_size_t, c_void_p], c_int),
     "sae_b200_grad_sumsq": (
         [POINTER(Model), POINTER(Grads), c_void_p, c_size_t, c_void_p, c_void_p], c_int),
     "sae_b200_clip_from_sumsq": ([c_void_p, c_float, c_void_p, c_void_p], c_int),
@@ -219,6 +220,8 @@ _SIGNATURES = {
     "sae_b200_gemm": (
         [c_int64, c_int64, c_int64, c_float, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int,
          c_int64, c_int64, c_float, c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p], c_int),
+    "sae_b200_transpose": (
+        [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p], c_int),
     "sae_b200_column_sum": (
         [c_void_p, c_int, c_int64, c_int64, c_float, c_float, c_void_p, c_void_p], c_int),
     "sae_b200_renorm_rows": ([c_void_p, c_int64, c_int64, c_void_p, c_void_p], c_int),
@@ -292,6 +295,13 @@ def aux_workspace_bytes(max_tokens: int, d_in: int, n_features: int, max_dead: i
     out = c_size_t(0)
     call("sae_b200_aux_workspace_bytes", max_tokens, d_in, n_features, max_dead, k,
          ctypes.byref(out))
+    return out.value
+
+
+def dense_scratch_bytes(n_tokens: int, d_in: int, n_features: int) -> int:
+    """Bytes of the caller's scratch for the dense weight-gradient backward."""
+    out = c_size_t(0)
+    call("sae_b200_dense_scratch_bytes", n_tokens, d_in, n_features, ctypes.byref(out))
     return out.value
 
 

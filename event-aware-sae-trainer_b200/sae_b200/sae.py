@@ -61,8 +61,31 @@ def _autocast_bf16(device: torch.device) -> bool:
             and torch.get_autocast_dtype("cuda") == torch.bfloat16)
 
 
+_GEMM_SIMT = os.environ.get("SAE_B200_GEMM_SIMT", "0") == "1"
+
+
+def _k_major(T: torch.Tensor, s_outer: int, s_k: int, n_outer: int, K: int):
+    """A bf16 GEMM operand with its contraction dimension contiguous, as
+    (tensor, outer stride, k stride): operands stored the other way round
+    ([K, n_outer] rows s_k apart) are transposed by the library into a fresh
+    [n_outer, K] buffer whose rows are padded to 16 bytes."""
+    if s_k == 1 or s_outer != 1:
+        return T, s_outer, s_k
+    kp = (K + 7) // 8 * 8
+    out = torch.empty(n_outer, kp, device=T.device, dtype=torch.bfloat16)
+    L.call("sae_b200_transpose", L.ptr(T), L.DTYPE_BF16, K, n_outer, s_k, L.ptr(out), kp,
+           _stream())
+    return out, kp, 1
+
+
 def gemm(M, N, K, A, sam, sak, B, sbn, sbk, C, scm, scn, *, alpha=1.0, beta=0.0, bias=None):
-    """C = alpha A B^T + beta C (+ bias) on CUDA cores, arbitrary strides (elements)."""
+    """C = alpha A B^T + beta C (+ bias), arbitrary strides (elements). bf16
+    products large enough for the tensor cores get K-major operands (see
+    _k_major) and run on the tcgen05 tile GEMM; the rest on CUDA cores."""
+    if (not _GEMM_SIMT and A.dtype == torch.bfloat16 and B.dtype == torch.bfloat16
+            and M >= 128 and N >= 128 and K >= 64 and (scn == 1 or scm == 1)):
+        A, sam, sak = _k_major(A, sam, sak, M, K)
+        B, sbn, sbk = _k_major(B, sbn, sbk, N, K)
     L.call("sae_b200_gemm", M, N, K, alpha, L.ptr(A), _dt_code(A), sam, sak, L.ptr(B),
            _dt_code(B), sbn, sbk, beta, L.ptr(C), _dt_code(C), scm, scn, L.ptr(bias), _stream())
 

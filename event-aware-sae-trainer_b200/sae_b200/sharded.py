@@ -274,7 +274,7 @@ class ShardedFusedStep(FusedStep):
             sae._sparse_decode_calls += 1
         L.call("sae_b200_shard_backward", ctypes.byref(model), ctypes.byref(grads),
                ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), self.rank,
-               L.ptr(scratch), stream)
+               L.ptr(scratch), 0 if scratch is None else scratch.numel(), stream)
         self._allreduce(self.g_b_dec)                          # b_dec gradient
         if after_backward is not None:
             after_backward()

@@ -292,11 +292,12 @@ class FusedStep:
         return x.contiguous()
 
     def _dense_scratch_for(self, n_tokens: int) -> torch.Tensor:
-        """bf16 [F, ldp] buffer of the dense weight-gradient path (allocated on
-        the first microbatch whose active set overflows the CSR)."""
-        need = L.pre_pitch(n_tokens) * self.sae.n_features
+        """Scratch of the dense weight-gradient path: the bf16 [F, ldp] dense
+        operand plus the transposed xc and go (allocated on the first
+        microbatch whose active set overflows the CSR)."""
+        need = L.dense_scratch_bytes(n_tokens, self.sae.d_in, self.sae.n_features)
         if self._dense_scratch is None or self._dense_scratch.numel() < need:
-            self._dense_scratch = torch.empty(need, device=self.device, dtype=torch.bfloat16)
+            self._dense_scratch = torch.empty(need, device=self.device, dtype=torch.uint8)
         return self._dense_scratch
 
     def read_stats(self) -> dict:
@@ -385,9 +386,10 @@ class FusedStep:
                 L.call("sae_b200_store_full_pre", ctypes.byref(model), ctypes.byref(cfg),
                        L.ptr(self.ws), self.ws_bytes, stream)
                 cfg.pre_entries_only = 0
+            scratch = self._dense_scratch_for(n)
             L.call("sae_b200_train_backward_dense", ctypes.byref(model), ctypes.byref(grads),
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
-                   L.ptr(self._dense_scratch_for(n)), stream)
+                   L.ptr(scratch), scratch.numel(), stream)
             redone = True
         else:
             sae._sparse_decode_calls += 1

@@ -209,12 +209,19 @@ int sae_b200_store_full_pre(const SaeB200Model* model, const SaeB200StepConfig* 
                             void* workspace, size_t workspace_bytes, void* stream);
 
 /* Same gradients without the capacity limit, for microbatches whose active
- * set overflowed csr_capacity. dense_scratch: bf16 device buffer of
- * n_features * sae_b200_pre_pitch(n_tokens) elements owned by the caller. */
+ * set overflowed csr_capacity (the reference's dense autograd: dW_enc = dpre^T xc,
+ * _EncoderPreBias.backward 592-607; dW_dec = acts^T go, decode 922-925). The two
+ * weight-gradient contractions over the tokens run on the tcgen05 tile GEMM
+ * (CUDA cores when cfg->force_simt is set). dense_scratch: device buffer owned
+ * by the caller, 16-byte aligned, of at least sae_b200_dense_scratch_bytes()
+ * bytes (the dense [F, ldp] operand and the transposed xc and go [d, ldp]);
+ * smaller buffers return SAE_ERR_WORKSPACE_TOO_SMALL. */
+int sae_b200_dense_scratch_bytes(int64_t n_tokens, int64_t d_in, int64_t n_features,
+                                 size_t* bytes_out);
 int sae_b200_train_backward_dense(const SaeB200Model* model, const SaeB200Grads* grads,
                                   const SaeB200StepConfig* cfg, void* workspace,
                                   size_t workspace_bytes, SaeB200StepStats* stats,
-                                  void* dense_scratch, void* stream);
+                                  void* dense_scratch, size_t dense_scratch_bytes, void* stream);
 
 /* Global gradient norm and clip coefficient (torch.nn.utils.clip_grad_norm_,
  * called at sae_trainer_rolling.py:3049). Writes stats->grad_norm and
@@ -350,7 +357,7 @@ int sae_b200_shard_finish_forward(const SaeB200Model* model, const void* x, int 
 int sae_b200_shard_backward(const SaeB200Model* model, const SaeB200Grads* grads,
                             const SaeB200StepConfig* cfg, void* workspace, size_t workspace_bytes,
                             SaeB200StepStats* stats, int shard_rank, void* dense_scratch,
-                            void* stream);
+                            size_t dense_scratch_bytes, void* stream);
 /* *sumsq_out (device float) = sum of squares of the non-NULL gradients. */
 int sae_b200_grad_sumsq(const SaeB200Model* model, const SaeB200Grads* grads, void* workspace,
                         size_t workspace_bytes, float* sumsq_out, void* stream);
@@ -421,13 +428,28 @@ int sae_b200_jumprelu_backward_static(const void* pre, int pre_dtype, const floa
                                       const float* grad_feat, const float* grad_gate, float eps,
                                       void* grad_pre_out, float* grad_log_threshold, void* stream);
 
-/* General strided product on CUDA cores: C = alpha * A B^T + beta * C (+ bias[n]).
+/* General strided product: C = alpha * A B^T + beta * C (+ bias[n]).
  * A[m, k] at A + m*sam + k*sak; B[n, k] at B + n*sbn + k*sbk; C[m, n] at
- * C + m*scm + n*scn (strides in elements). beta == 0 never reads C. */
+ * C + m*scm + n*scn (strides in elements). beta == 0 never reads C.
+ * bf16 A and B stored K-major (sak == sbk == 1, 16-byte aligned bases, sam and
+ * sbn multiples of 8), M, N >= 128, K >= 64 and an output with scn == 1 or
+ * scm == 1 run on the tcgen05 tile GEMM (fp32 accumulate); everything else, and
+ * every call while SAE_B200_GEMM_SIMT=1 is set in the environment, on CUDA cores
+ * in fp32. The module API's dense products under bf16 autocast: decode
+ * (sae_trainer_rolling.py:922-925) and the weight / input gradients of the
+ * decoder and encoder (592-607). */
 int sae_b200_gemm(int64_t M, int64_t N, int64_t K, float alpha, const void* A, int a_dtype,
                   int64_t sam, int64_t sak, const void* B, int b_dtype, int64_t sbn,
                   int64_t sbk, float beta, void* C, int c_dtype, int64_t scm, int64_t scn,
                   const float* bias_n, void* stream);
+
+/* dst[c, r] = src[r, c] for a bf16 [rows, cols] matrix with rows lds apart into
+ * [cols, rows] with rows ldd apart (elements): puts an operand whose
+ * contraction dimension is outermost into the K-major layout sae_b200_gemm
+ * feeds to the tensor cores. No counterpart in the reference (cuBLAS takes
+ * either layout). */
+int sae_b200_transpose(const void* src, int dtype, int64_t rows, int64_t cols, int64_t lds,
+                       void* dst, int64_t ldd, void* stream);
 
 /* out[c] = beta * out[c] + alpha * sum_r X[r, c]  (X row-major [rows, cols]). */
 int sae_b200_column_sum(const void* X, int x_dtype, int64_t rows, int64_t cols, float alpha,

@@ -80,9 +80,17 @@ def test_full_pre_store_and_pre_flag_are_checked_without_a_device():
     m = L.Model(1536, 49152, 256, 256, 256, 256, 256, 256, 256)
     g = L.Grads(256, 256, 256, 256, 256)
     rc = lib.sae_b200_train_backward_dense(ctypes.byref(m), ctypes.byref(g), ctypes.byref(entries),
-                                           256, 1 << 30, 256, 256, None)
+                                           256, 1 << 40, 256, 256, 1 << 40, None)
     assert rc == L.SAE_ERR_INVALID_ARGUMENT
     assert b"pre_entries_only" in lib.sae_b200_last_error()
+    # a dense scratch below sae_b200_dense_scratch_bytes is refused before any launch
+    full = L.StepConfig(16, 1024, 0.0, 0.0, 0.0, 0.1, 1, 0, 1, 0, 0, 0)
+    need = L.dense_scratch_bytes(16, 1536, 49152)
+    assert need >= 49152 * L.pre_pitch(16) * 2
+    rc = lib.sae_b200_train_backward_dense(ctypes.byref(m), ctypes.byref(g), ctypes.byref(full),
+                                           256, 1 << 40, 256, 256, 1024, None)
+    assert rc == L.SAE_ERR_WORKSPACE_TOO_SMALL
+    assert b"dense_scratch" in lib.sae_b200_last_error()
 
 
 def test_norm_from_backward_partials_is_checked_without_a_device():

@@ -168,6 +168,26 @@ def test_sampled_and_gemm_backward_agree_at_full_size(setup):
     del fs2
 
 
+def test_dense_fallback_at_full_size(setup):
+    """A microbatch whose entries overflow the CSR takes the dense weight-
+    gradient path: dW_enc = dpre^T xc and dW_dec = acts^T go as two tcgen05
+    GEMMs contracting over the 32768 tokens. Same gradients as the sampled
+    backward (2e-3 relative: the weight gradients are summed in another order
+    and grad_feat may differ by one bf16 ulp)."""
+    import sae_b200
+    sae, x, g = setup["sae"], setup["x"], setup["grads"]
+    fs4 = sae_b200.FusedStep(sae, setup["fs"].opt, max_tokens=B, csr_capacity=4096)
+    st4 = fs4.microbatch(x, lambda_l0=1e-3, al_mu=1e-2, target_l0=50)
+    torch.cuda.synchronize()
+    assert fs4.dense_fallbacks == 1
+    assert st4["nnz"] == setup["st"]["nnz"]
+    for k, t in (("W_enc", fs4.g_W_enc), ("b_enc", fs4.g_b_enc), ("W_dec_fm", fs4.g_W_dec_fm),
+                 ("b_dec", fs4.g_b_dec), ("log_threshold", fs4.g_log_thr)):
+        a, b = t.double(), g[k].double()
+        assert float((a - b).norm() / b.norm()) < 2e-3, k
+    del fs4
+
+
 def test_entries_only_pre_store_is_bit_identical_at_full_size(setup):
     """The default forward stores pre only where an entry is; at the full
     workload its statistics and gradients equal the full store's bit for bit."""

@@ -217,20 +217,21 @@ def test_microbatch_accumulation_matches_oracle(n, grad_feat):
 
 def test_dense_fallback_matches_sparse_path():
     """An active set larger than the workspace's CSR capacity takes the dense
-    weight-gradient path; the result must match the sampled and the GEMM
-    sparse paths."""
+    weight-gradient path (tcgen05 weight-gradient GEMMs, or CUDA cores with
+    force_simt); the result must match the sampled and the GEMM sparse paths."""
     g = load_golden("super_f32_tiles")
     cfg = oracle_cfg(g)
     x = torch.from_numpy(g["x0"].astype(np.float32)).cuda()
     res = []
-    for cap, mode in ((None, "sampled"), (16, "sampled"), (None, "gemm")):
-        sae, opt, fs = build(g, csr_capacity=cap, grad_feat=mode)
+    for cap, mode, simt in ((None, "sampled", False), (16, "sampled", False),
+                            (None, "gemm", False), (16, "sampled", True)):
+        sae, opt, fs = build(g, csr_capacity=cap, grad_feat=mode, force_simt=simt)
         fs.microbatch(x, lambda_l0=cfg.lambda_l0, al_mu=cfg.al_mu, target_l0=cfg.target_l0)
         torch.cuda.synchronize()
         res.append((fs.dense_fallbacks, fs.g_W_enc.clone(), fs.g_W_dec_fm.clone(),
                     fs.g_b_dec.clone(), fs.g_log_thr.clone()))
-    assert res[0][0] == 0 and res[1][0] == 1 and res[2][0] == 0
-    for other in (res[1], res[2]):
+    assert res[0][0] == 0 and res[1][0] == 1 and res[2][0] == 0 and res[3][0] == 1
+    for other in (res[1], res[2], res[3]):
         for a, b in zip(res[0][1:], other[1:]):
             # the sampled dot products and the tensor-core GEMM sum in different
             # orders: grad_feat may differ by one bf16 ulp on a few entries
