@@ -166,95 +166,129 @@ class ClockSampler:
                 "samples": len(self.rows), "source": src}
 
 
-# ------------------------------------------------------------- CPU oracle
-_CPU_DICT = {}
+# ------------------------------------------------------------- CPU reference
+def host_threads() -> int:
+    """Cores this process may run on (its affinity set)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
 
 
-def cpu_reference_step_time(tokens: int, seed: int = 0, opt_features: int = 0):
-    """Time the oracle's restatement of the reference CPU step (fp32) on a
-    bounded sample: one microbatch of `tokens` tokens fwd+bwd, plus the clip
-    norm and Adam + renorm over all parameters. Returns (t_microbatch, t_adam,
-    l0). opt_features > 0 times the clip norm and Adam + renorm on the first
-    opt_features features only (their W_enc rows, W_dec columns, b_enc and
-    thresholds, plus b_dec) and scales the time by the parameter count: both
-    are elementwise or per-row passes over memory, so their time is linear in
-    the parameters."""
-    import numpy as np
+CPU_SAMPLE_TOKENS = 2048
+
+
+class CpuReferenceSampler:
+    """The reference trainer's fp32 CPU step (oracle/torch_step.py: its torch-
+    operator restatement, pinned to the reference's own outputs) on a bounded
+    sample of the 32768-token workload, timed on the host cores.
+
+    One sample = 1/k of one optimizer step (k = 32768 / S): the forward and
+    backward of one S-token microbatch over the whole dictionary (exact
+    gradient accumulation makes the step k such microbatches) plus the clip
+    norm, Adam and both renorms over 1/k of the features (those are passes
+    over the parameters, linear in their count). A sample's tokens/s is S over
+    its measured time: nothing is extrapolated. All host threads are used
+    (torchrun sets OMP_NUM_THREADS=1, so the count is set explicitly), and the
+    thresholds are calibrated so that the mean L0 is ~50, as on the GPU."""
+
+    def __init__(self, sample_tokens: int = 0, seed: int = 0):
+        import torch
+
+        from oracle import sae_oracle as O
+        from oracle.torch_step import TorchReferenceStep
+        self.threads = host_threads()
+        torch.set_num_threads(self.threads)
+        self.S = int(sample_tokens or CPU_SAMPLE_TOKENS)
+        self.k = TOKENS // self.S
+        self.xs = [torch.from_numpy(O.superposition_batch(self.S, D_IN, N_FEAT, K_TARGET, NORM_MU,
+                                                          NORM_SIGMA, seed=seed + i))
+                   for i in range(2)]
+        self.ref = TorchReferenceStep(D_IN, N_FEAT, seed=0, lr=LR, ste_bandwidth=0.2,
+                                      lambda_l0=LAMBDA, al_mu=MU, target_l0=K_TARGET)
+        with torch.no_grad():
+            self.ref.b_dec.copy_(self.xs[0].mean(0))
+            pre = torch.addmm(self.ref.b_enc, self.xs[0][:256] - self.ref.b_dec,
+                              self.ref.W_enc.t())
+            q = torch.quantile(pre.flatten(), 1.0 - K_TARGET / N_FEAT).item()
+            self.ref.log_threshold.fill_(math.log(max(q, 1e-6)))
+        self.ref.microbatch(self.xs[0], self.k, True)          # gradients exist for the slice
+        self.opt_slice = self.ref.slice_features(N_FEAT // self.k)
+        self.description = (
+            f"per step: 1/{self.k} of the 32768-token optimizer step, timed as is: one "
+            f"{self.S}-token fwd+bwd microbatch over all {N_FEAT} features + clip norm, Adam and "
+            f"both renorms over {N_FEAT // self.k} features; the reference's fp32 CPU step "
+            "restated with torch CPU operators (oracle/torch_step.py, pinned to the reference's "
+            f"own outputs), {self.threads} threads, thresholds calibrated to L0~{K_TARGET}")
+
+    def sample(self, i: int):
+        """(seconds, l0) of one sample."""
+        t0 = time.perf_counter()
+        out = self.ref.microbatch(self.xs[i % 2], self.k, True)
+        self.opt_slice.optimizer_step()
+        return time.perf_counter() - t0, out["l0"]
+
+
+CFG1 = dict(d=256, F=8192, tokens=4096)
+
+
+def cpu_cfg1_full_step(steps: int = 3, warmup: int = 1):
+    """One full, unscaled step of the CPU benchmark configuration (d=256,
+    F=8192, one 4096-token microbatch, log_threshold = log 0.05, b_dec =
+    mean(x)) with the same torch restatement: (tokens/s, ms per step, l0)."""
+    import torch
 
     from oracle import sae_oracle as O
-    d, F = D_IN, N_FEAT
-    x = O.superposition_batch(tokens, d, 4096, K_TARGET, NORM_MU, NORM_SIGMA, seed=seed)
-    if _CPU_DICT.get((F, d)) is None:     # one random unit-row dictionary per process
-        W = np.random.default_rng(0).standard_normal((F, d)).astype(np.float32)
-        W /= np.linalg.norm(W, axis=1, keepdims=True)
-        _CPU_DICT[(F, d)] = W
-    W = _CPU_DICT[(F, d)].copy()
-    p = O.Params(W, np.zeros(F, np.float32), W.T.copy(), x.mean(0).astype(np.float32),
-                 np.full(F, math.log(4.7), np.float32))
-    cfg = O.StepConfig(lambda_l0=LAMBDA, al_mu=MU, target_l0=K_TARGET, ste_bandwidth=0.2,
-                       accum_steps=TOKENS // tokens, lr=(LR,) * 4)
-    t0 = time.perf_counter()
-    fw = O.forward(x, p, cfg, "fp32")
-    g = O.backward(x, p, fw, cfg, "fp32")
-    t_mb = time.perf_counter() - t0
-    scale = 1.0
-    if 0 < opt_features < F:
-        fs = opt_features
-        p = O.Params(p.W_enc[:fs].copy(), p.b_enc[:fs].copy(), p.W_dec[:, :fs].copy(), p.b_dec,
-                     p.log_threshold[:fs].copy())
-        g = O.Grads(g.W_enc[:fs].copy(), g.b_enc[:fs].copy(), g.W_dec[:, :fs].copy(), g.b_dec,
-                    g.log_threshold[:fs].copy())
-        scale = (2 * F * d + 2 * F + d) / (2 * fs * d + 2 * fs + d)
-    st = O.AdamState.zeros_like(p)
-    t1 = time.perf_counter()
-    norm, clip = O.clip_coef(g, 1.0)
-    O.adam_step(p, g, st, cfg, clip)
-    t2 = time.perf_counter()
-    return t_mb, (t2 - t1) * scale, float(fw.l0)
-
-
-def cpu_threads():
-    try:
-        import threadpoolctl
-        info = threadpoolctl.threadpool_info()
-        n = max((i.get("num_threads", 1) for i in info), default=1)
-        return int(n)
-    except Exception:
-        return os.cpu_count() or 1
+    from oracle.torch_step import TorchReferenceStep
+    torch.set_num_threads(host_threads())
+    d, F, n = CFG1["d"], CFG1["F"], CFG1["tokens"]
+    x = torch.from_numpy(O.superposition_batch(n, d, F, 50, math.log(16.0), 0.3, seed=0))
+    ref = TorchReferenceStep(d, F, seed=0, lr=1e-4, ste_bandwidth=0.2, lambda_l0=1e-3,
+                             al_mu=1e-2, target_l0=50)
+    with torch.no_grad():
+        ref.b_dec.copy_(x.mean(0))
+        ref.log_threshold.fill_(math.log(0.05))
+    times, l0 = [], None
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        out = ref.step([x])
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+        l0 = out["l0"]
+    t = statistics.mean(times)
+    return n / t, t * 1e3, l0
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    sample = 1024
-    opt_features = N_FEAT // 16
-    times = []
-    l0 = None
+    sampler = CpuReferenceSampler()
+    times, l0s = [], []
     for i in range(args.warmup + args.steps):
-        t_mb, t_adam, l0 = cpu_reference_step_time(sample, seed=i, opt_features=opt_features)
+        t, l0 = sampler.sample(i)
         if i >= args.warmup:
-            times.append((TOKENS // sample) * t_mb + t_adam)
+            times.append(t)
+            l0s.append(l0)
     step_s = statistics.mean(times)
-    value = TOKENS / step_s
-    cores = cpu_threads()
+    value = sampler.S / step_s
+    c1_tok_s, c1_ms, c1_l0 = cpu_cfg1_full_step()
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "d_in": D_IN, "n_features": N_FEAT,
-                   "tokens_per_step": TOKENS, "cpu_sample_tokens": sample},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": (f"per step: one {sample}-token fwd+bwd microbatch (x"
-                                    f"{TOKENS // sample} for the 32768-token step, exact "
-                                    "gradient accumulation) + clip norm and Adam/renorm timed "
-                                    f"on {opt_features} of the {N_FEAT} features and scaled "
-                                    "by the parameter count to all 151M params; oracle "
-                                    "restatement of the reference fp32 CPU path")},
+                   "tokens_per_step": TOKENS, "cpu_sample_tokens": sampler.S,
+                   "sample_fraction_of_step": 1.0 / sampler.k, "l0_measured": statistics.mean(l0s)},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": sampler.threads,
+                         "kind": "port", "sample": sampler.description, "extrapolated": False},
+        "cfg1_full_step": {"workload": "d_in=256 F=8192, one 4096-token microbatch, "
+                                       "log_threshold = log 0.05 (one full unscaled "
+                                       "fwd+bwd+clip+Adam+renorm step)",
+                           "tokens_per_s": c1_tok_s, "ms_per_step": c1_ms, "l0": c1_l0},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "l0_sample": l0,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -725,15 +759,13 @@ def run_b200(args):
             "device_status": status,
         }
         if args.cpu_baseline and world == 1 and not sharded:
-            t_mb, t_adam, _ = cpu_reference_step_time(2048, opt_features=N_FEAT // 16)
-            cpu_step = (TOKENS // 2048) * t_mb + t_adam
+            sampler = CpuReferenceSampler()
+            times = [sampler.sample(i)[0] for i in range(4)][1:]   # one warm-up sample
+            cpu_s = statistics.mean(times)
             line["cpu_baseline"] = {
-                "value": TOKENS / cpu_step, "unit": "tokens/s", "cores": cpu_threads(),
-                "kind": "port",
-                "sample": ("one 2048-token fwd+bwd microbatch (x16 for the 32768-token step) + "
-                           f"clip norm and Adam/renorm timed on {N_FEAT // 16} of the {N_FEAT} "
-                           "features and scaled by the parameter count to all 151M params; "
-                           "oracle restatement of the reference fp32 CPU path")}
+                "value": sampler.S / cpu_s, "unit": "tokens/s", "cores": sampler.threads,
+                "kind": "port", "sample": sampler.description + f"; mean of {len(times)} samples",
+                "extrapolated": False}
         print(json.dumps(line), flush=True)
     if sharded:
         fs.close()

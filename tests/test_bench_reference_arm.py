@@ -1,8 +1,9 @@
-"""The reference arm of bench.py (`--impl reference`) on the CPU: the oracle's
-restatement of the reference fp32 step, timed on the host cores, printed as
-one JSON line with the same metric, unit and direction as the B200 arm plus
-its `cpu_baseline` and a zero-copy `e2e`. Shrunk to d=64, F=512 here so that
-it runs in seconds; the line's shape does not depend on the sizes."""
+"""The reference arm of bench.py (`--impl reference`) on the CPU: the torch
+restatement of the reference's fp32 step (oracle/torch_step.py), timed on the
+host cores on a bounded sample, printed as one JSON line with the same metric,
+unit and direction as the B200 arm plus its `cpu_baseline`, a full unscaled
+step of the CPU benchmark configuration, and a zero-copy `e2e`. Shrunk here so
+that it runs in seconds; the line's shape does not depend on the sizes."""
 import argparse
 import json
 
@@ -15,7 +16,8 @@ def _shrink(monkeypatch):
     monkeypatch.setattr(bench, "D_IN", 64)
     monkeypatch.setattr(bench, "N_FEAT", 512)
     monkeypatch.setattr(bench, "TOKENS", 4096)
-    monkeypatch.setattr(bench, "_CPU_DICT", {})
+    monkeypatch.setattr(bench, "CPU_SAMPLE_TOKENS", 256)
+    monkeypatch.setattr(bench, "CFG1", dict(d=32, F=256, tokens=512))
 
 
 def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
@@ -29,10 +31,15 @@ def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
     assert line["metric"] == bench.METRIC and line["unit"] == "tokens/s"
     assert line["higher_is_better"] is True and line["steps"] == 2 and line["warmup"] == 1
     assert line["value"] > 0
-    assert line["ms_per_step"] == pytest.approx(bench.TOKENS / line["value"] * 1e3, rel=1e-9)
+    # the value is the sample's own tokens over its own measured time
+    assert line["ms_per_step"] == pytest.approx(256 / line["value"] * 1e3, rel=1e-9)
+    assert line["config"]["sample_fraction_of_step"] == pytest.approx(256 / 4096)
     cb = line["cpu_baseline"]
-    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == line["value"]
-    assert "32 of the 512 features" in cb["sample"]
+    assert cb["kind"] == "port" and cb["cores"] == bench.host_threads()
+    assert cb["value"] == line["value"] and cb["extrapolated"] is False
+    assert "over 32 features" in cb["sample"]
+    c1 = line["cfg1_full_step"]
+    assert c1["tokens_per_s"] > 0 and c1["ms_per_step"] > 0
     assert line["e2e"] == {"value": line["value"], "unit": "tokens/s",
                            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
@@ -44,22 +51,16 @@ def test_reference_arm_runs_on_rank_zero_only(monkeypatch, capsys):
     assert capsys.readouterr().out == ""
 
 
-def test_sliced_optimizer_timing_scales_to_the_whole_parameter_count(monkeypatch):
-    """opt_features times the clip norm and Adam on a feature slice; the
-    returned time is scaled by P / P_slice (P = 2 F d + 2 F + d)."""
+def test_sampler_uses_every_host_thread_and_calibrates_l0(monkeypatch):
+    """torchrun sets OMP_NUM_THREADS=1; the sampler sets torch's thread count
+    to the process's whole affinity set anyway, and its thresholds put the
+    mean L0 near the target."""
+    import torch
     _shrink(monkeypatch)
-    calls = []
-    real = bench.time.perf_counter
-    ticks = iter(range(1000))
-
-    def fake_clock():
-        calls.append(1)
-        return float(next(ticks))
-
-    monkeypatch.setattr(bench.time, "perf_counter", fake_clock)
-    t_mb, t_opt, l0 = bench.cpu_reference_step_time(256, seed=0, opt_features=32)
-    monkeypatch.setattr(bench.time, "perf_counter", real)
-    F, d, fs = 512, 64, 32
-    assert t_mb == 1.0
-    assert t_opt == (2 * F * d + 2 * F + d) / (2 * fs * d + 2 * fs + d)
-    assert l0 >= 0
+    monkeypatch.setattr(bench, "K_TARGET", 16)
+    torch.set_num_threads(1)
+    s = bench.CpuReferenceSampler(sample_tokens=256)
+    assert s.threads == bench.host_threads() == torch.get_num_threads()
+    t, l0 = s.sample(0)
+    assert t > 0
+    assert 4 <= l0 <= 64

@@ -162,3 +162,42 @@ def test_cfg1_summary_matches_reference():
     assert _rel(res.grads.W_dec[:, rows].T, g["grad_W_dec_rows"]) < 1e-3
     assert _rel(res.params.W_enc[rows], g["p1_W_enc_rows"]) < 1e-5
     assert _rel(res.params.W_dec[:, rows].T, g["p1_W_dec_rows"]) < 1e-5
+
+
+def test_torch_cpu_step_matches_reference_cfg1():
+    """oracle/torch_step.py -- the torch-operator restatement that the CPU
+    baseline times -- against the reference's own fp32 step at the CPU
+    benchmark configuration (init bit-identical, same tolerances as the numpy
+    restatement above)."""
+    torch = pytest.importorskip("torch")
+    from oracle.torch_step import TorchReferenceStep
+
+    g = load_golden("cfg1_f32")
+    d, F = int(g["d"]), int(g["F"])
+    x = O.superposition_batch(4096, d, 8192, 50, math.log(16.0), 0.3, seed=0)
+    ref = TorchReferenceStep(d, F, seed=0, lr=float(g["lr"]), ste_bandwidth=float(g["eps"]),
+                             lambda_l0=float(g["lam"]), al_mu=float(g["mu"]),
+                             target_l0=float(g["target"]))
+    with torch.no_grad():
+        ref.b_dec.copy_(torch.from_numpy(x.mean(0)))
+        ref.log_threshold.fill_(math.log(0.05))
+    names = ("W_enc", "b_enc", "W_dec", "b_dec", "log_threshold")
+    for k, p in zip(names, ref.params()):
+        assert float(p.detach().double().sum()) == pytest.approx(float(g[f"p0_{k}_sum"]),
+                                                                 rel=1e-6, abs=1e-6), k
+    out = ref.step([torch.from_numpy(x)])
+    rows = g["rows"]
+    assert out["l0"] == pytest.approx(float(g["l0"][0]), rel=1e-6)
+    assert out["recon_loss"] == pytest.approx(float(g["recon"][0]), rel=1e-5)
+    assert out["grad_norm"] == pytest.approx(float(g["grad_norm"]), rel=1e-4)
+    grads = dict(zip(names, (p.grad.numpy() for p in ref.params())))
+    p1 = dict(zip(names, (p.detach().numpy() for p in ref.params())))
+    # the gradients were clipped in place by clip_grad_norm_: undo the scale
+    clip = min(1.0, 1.0 / (float(g["grad_norm"]) + 1e-6))
+    for k in ("b_enc", "b_dec", "log_threshold"):
+        assert _rel(grads[k] / clip, g[f"grad_{k}"]) < 1e-3, k
+        assert _rel(p1[k], g[f"p1_{k}"]) < 1e-5, k
+    assert _rel(grads["W_enc"][rows] / clip, g["grad_W_enc_rows"]) < 1e-3
+    assert _rel(grads["W_dec"][:, rows].T / clip, g["grad_W_dec_rows"]) < 1e-3
+    assert _rel(p1["W_enc"][rows], g["p1_W_enc_rows"]) < 1e-5
+    assert _rel(p1["W_dec"][:, rows].T, g["p1_W_dec_rows"]) < 1e-5
