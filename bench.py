@@ -583,8 +583,12 @@ def run_b200(args):
     d_stop = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     a_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     a_stop = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    for e in k_start + k_stop + d_start + d_stop + a_start + a_stop:
+    x_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    x_stop = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    for e in k_start + k_stop + d_start + d_stop + a_start + a_stop + x_start + x_stop:
         e.record()
+    if sharded:
+        fs.timing = {}       # per-phase events of the timed steps (forward, backward, ...)
     barrier()
     launches0 = L.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -596,15 +600,22 @@ def run_b200(args):
             L.set_kernel_timer(L.KERNEL_GRAD_GEMM, k_start[2 * i + 1], k_stop[2 * i + 1])
             L.set_kernel_timer(L.KERNEL_DECODE, d_start[i], d_stop[i])
             L.set_kernel_timer(L.KERNEL_ADAM, a_start[i], a_stop[i])
+            L.set_kernel_timer(L.KERNEL_EXCHANGE, x_start[i], x_stop[i])
             stats.append(step(i, pool[(args.warmup + i) % POOL_BATCHES]))
         ev1.record()
         barrier()
-    L.set_kernel_timer(L.KERNEL_ENCODER_GEMM)
-    L.set_kernel_timer(L.KERNEL_GRAD_GEMM)
-    L.set_kernel_timer(L.KERNEL_DECODE)
-    L.set_kernel_timer(L.KERNEL_ADAM)
+    for k in (L.KERNEL_ENCODER_GEMM, L.KERNEL_GRAD_GEMM, L.KERNEL_DECODE, L.KERNEL_ADAM,
+              L.KERNEL_EXCHANGE):
+        L.set_kernel_timer(k)
+    phases = None
+    if sharded:
+        phases = {k: statistics.mean(a.elapsed_time(b) for a, b in v)
+                  for k, v in fs.timing.items()}
+        fs.timing = None
     launches = (L.launch_count() - launches0)
     dec_ms = statistics.mean(d_start[i].elapsed_time(d_stop[i]) for i in range(n_ev))
+    xch_ms = (statistics.mean(x_start[i].elapsed_time(x_stop[i]) for i in range(n_ev))
+              if sharded and world > 1 and args.exchange == "p2p" else None)
     adam_ms = statistics.mean(a_start[i].elapsed_time(a_stop[i]) for i in range(n_ev))
     # mean entry counts of the timed microbatches (active, and active + in-band)
     nnz_mean = statistics.mean(s["nnz"] for s in stats)
@@ -746,6 +757,17 @@ def run_b200(args):
                         "hbm_peak_source": f"hbm_gbs ({peaks['src']})"} |
                        {"step_dense_tflops": step_flop / (ms / 1e3) / 1e12},
             "clocks": clock,
+            "phases_ms": (None if phases is None else
+                          {**{k: round(v, 4) for k, v in phases.items()},
+                           "encoder_gemm": round(enc_ms, 4), "decode_partial": round(dec_ms, 4),
+                           "exchange_p2p": None if xch_ms is None else round(xch_ms, 4),
+                           "sampled_backward": round(grad_ms, 4),
+                           "note": ("CUDA events on rank 0: forward = encoder + decode "
+                                    "partial + exchange + loss terms; backward = this "
+                                    "shard's sampled backward; bdec_allreduce, norm "
+                                    "(sum of squares + its all-reduce + clip) and adam as "
+                                    "named; the step's remainder is host time (the one "
+                                    "stats read-back per microbatch)")}),
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": (tokens if sharded else world * tokens) * d * 2,
                     "d2h_bytes_per_step": world * 2 * 64,

@@ -31,8 +31,9 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<int64_t> g_launches{0};
-cudaEvent_t g_timer_start[4] = {nullptr, nullptr, nullptr, nullptr};
-cudaEvent_t g_timer_stop[4] = {nullptr, nullptr, nullptr, nullptr};
+constexpr int kTimers = 6;
+cudaEvent_t g_timer_start[kTimers] = {};
+cudaEvent_t g_timer_stop[kTimers] = {};
 
 void timer_begin(int which, cudaStream_t s) {
   if (g_timer_start[which] != nullptr) cudaEventRecord(g_timer_start[which], s);
@@ -568,8 +569,7 @@ int64_t sae_b200_launch_count(void) { return g_launches.load(); }
 int64_t sae_b200_pre_pitch(int64_t n_tokens) { return pre_pitch(n_tokens); }
 
 int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event) {
-  if (kernel != SAE_KERNEL_ENCODER_GEMM && kernel != SAE_KERNEL_GRAD_GEMM &&
-      kernel != SAE_KERNEL_DECODE && kernel != SAE_KERNEL_ADAM)
+  if (kernel < 0 || kernel >= kTimers)
     return fail(SAE_ERR_INVALID_ARGUMENT, "unknown kernel id %d", kernel);
   if ((start_event == nullptr) != (stop_event == nullptr))
     return fail(SAE_ERR_INVALID_ARGUMENT, "set both timer events or neither");
@@ -1153,6 +1153,7 @@ int sae_b200_shard_forward_p2p(const SaeB200Model* model, const void* x, int x_d
   a.tok_sqerr_off = c.L.tok_sqerr;
   a.tok_cnt_off = c.L.tok_cnt;
   a.gosum_off = c.L.gosum_part;
+  timer_begin(SAE_KERNEL_EXCHANGE, stream);
   peer_barrier_kernel<<<1, 32, 0, stream>>>(a, 0);
   SAE_TRY(check_launch("peer_barrier_kernel"));
   const int64_t lo = c.B * peers->rank / peers->world;
@@ -1168,7 +1169,9 @@ int sae_b200_shard_forward_p2p(const SaeB200Model* model, const void* x, int x_d
                                                         c.go_scale, lo, hi);
   SAE_TRY(check_launch("exchange_reduce_kernel"));
   peer_barrier_kernel<<<1, 32, 0, stream>>>(a, 1);
-  SAE_TRY(check_launch("peer_barrier_kernel"));
+  const int rc = check_launch("peer_barrier_kernel");
+  timer_end(SAE_KERNEL_EXCHANGE, stream);
+  SAE_TRY(rc);
   return forward_stats(cfg, c, stats, stream);
 }
 
@@ -1333,7 +1336,7 @@ static int backward_common(const SaeB200Model* model, const SaeB200Grads* grads,
     bf16* goT = xcT + static_cast<size_t>(d) * ldp;
     SAE_TRY(transpose_bf16(w.xc, B, d, d, xcT, ldp, stream));
     SAE_TRY(tc_store_gemm(F, d, B, dense_scratch, ldp, xcT, ldp, grads->W_enc, d, 0, 1.f,
-                          acc ? 1.f : 0.f, nullptr, 0, stream));
+                          acc ? 1.f : 0.f, nullptr, 0, stream, SAE_KERNEL_DENSE_WGRAD));
     if (g_wdec != nullptr) {
       gated_pre_kernel<<<grid_for(B * F, 256), 256, 0, stream>>>(w.pre, w.theta, B, F, ldp,
                                                                  dense_scratch);
@@ -1488,6 +1491,40 @@ int sae_b200_grad_norm_sampled(const SaeB200Model* model, const SaeB200Grads* gr
   SAE_TRY(check_launch("grad_sumsq_rows_kernel"));
   grad_norm_final_kernel<<<1, 1024, 0, stream>>>(part, NORM_GRID, max_norm, stats);
   return check_launch("grad_norm_final_kernel");
+}
+
+int sae_b200_grad_sumsq_sampled(const SaeB200Model* model, const SaeB200Grads* grads,
+                                const SaeB200StepConfig* cfg, const void* workspace,
+                                size_t workspace_bytes, void* norm_workspace,
+                                size_t norm_workspace_bytes, float* sumsq_out, void* stream_) {
+  SAE_TRY(check_model(model, false));
+  SAE_TRY(check_cfg(cfg));
+  if (grads == nullptr || sumsq_out == nullptr)
+    return fail(SAE_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (cfg->grad_feat_gemm != 0)
+    return fail(SAE_ERR_INVALID_ARGUMENT,
+                "grad_sumsq_sampled follows the sampled backward (grad_feat_gemm = 0) only");
+  if (norm_workspace == nullptr || norm_workspace_bytes < NORM_GRID * sizeof(float))
+    return fail(SAE_ERR_WORKSPACE_TOO_SMALL, "grad_sumsq_sampled needs %zu workspace bytes",
+                NORM_GRID * sizeof(float));
+  const int64_t d = model->d_in, F = model->n_features;
+  const Layout L = make_layout(cfg->n_tokens, d, F, cfg->csr_capacity);
+  SAE_TRY(check_ws(L, const_cast<void*>(workspace), workspace_bytes));
+  const Ws w = carve(const_cast<void*>(workspace), L);
+  GradList gl{};
+  gl.p[0] = grads->b_dec;   // NULL on the shards that do not count the replicated b_dec
+  gl.n[0] = d;
+  if (!cfg->train_decoder && grads->W_dec_fm != nullptr) {   // not covered by the rows
+    gl.p[1] = grads->W_dec_fm;
+    gl.n[1] = F * d;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  float* part = static_cast<float*>(norm_workspace);
+  grad_sumsq_rows_kernel<<<NORM_GRID, 512, 0, stream>>>(
+      w.row_sumsq, F, sampled_threads(static_cast<int>(d)) / 32, gl, part);
+  SAE_TRY(check_launch("grad_sumsq_rows_kernel"));
+  sum_parts_kernel<<<1, 1024, 0, stream>>>(part, NORM_GRID, sumsq_out);
+  return check_launch("sum_parts_kernel");
 }
 
 int sae_b200_grad_sumsq(const SaeB200Model* model, const SaeB200Grads* grads, void* workspace,

@@ -195,6 +195,9 @@ _SIGNATURES = {
     "sae_b200_shard_backward": (
         [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_void_p, c_int,
          c_void_p, c_size_t, c_void_p], c_int),
+    "sae_b200_grad_sumsq_sampled": (
+        [POINTER(Model), POINTER(Grads), POINTER(StepConfig), c_void_p, c_size_t, c_void_p,
+         c_size_t, c_void_p, c_void_p], c_int),
     "sae_b200_grad_sumsq": (
         [POINTER(Model), POINTER(Grads), c_void_p, c_size_t, c_void_p, c_void_p], c_int),
     "sae_b200_clip_from_sumsq": ([c_void_p, c_float, c_void_p, c_void_p], c_int),
@@ -265,6 +268,8 @@ KERNEL_ENCODER_GEMM = 0
 KERNEL_GRAD_GEMM = 1
 KERNEL_DECODE = 2
 KERNEL_ADAM = 3
+KERNEL_EXCHANGE = 4
+KERNEL_DENSE_WGRAD = 5
 
 
 def pre_pitch(n_tokens: int) -> int:

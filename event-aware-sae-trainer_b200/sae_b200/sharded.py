@@ -195,6 +195,8 @@ class ShardedFusedStep(FusedStep):
         else:
             self.rank, self.world = 0, 1
         self._custom_allreduce = allreduce
+        # per-phase timing: None (off) or a dict phase -> [(start, stop) events]
+        self.timing = None
         self.sumsq = torch.zeros(1, device=self.device, dtype=torch.float32)
         self.peers = None
         if exchange == "p2p" and self.world > 1 and allreduce is None:
@@ -220,10 +222,28 @@ class ShardedFusedStep(FusedStep):
         elif self.world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
+    def _mark(self) -> Optional[torch.cuda.Event]:
+        """A timing event on the current stream when per-phase timing is on."""
+        if self.timing is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def _phase(self, name: str, start, stop) -> None:
+        if self.timing is not None and start is not None:
+            self.timing.setdefault(name, []).append((start, stop))
+
     def microbatch(self, x: torch.Tensor, *, accum_steps: int = 1, first: bool = True,
                    lambda_l0: float = 0.0, al_mu: float = 0.0, target_l0: float = 0.0,
                    x_hat_out: Optional[torch.Tensor] = None,
                    after_backward: Optional[Callable[[], None]] = None) -> dict:
+        """FusedStep.microbatch on this shard. Every rank takes the same
+        collective steps whatever its own CSR does: the sampled backward is
+        queued before the host reads the forward's statistics (it leaves the
+        gradients untouched if this shard's entries overflowed the CSR), the
+        overflowed shard then redoes its backward on the dense path, and only
+        after that do the ranks all-reduce the b_dec gradient."""
         sae = self.sae
         if self._aux is not None:
             raise NotImplementedError("the dead-feature aux loss needs a top-k over the whole "
@@ -236,6 +256,7 @@ class ShardedFusedStep(FusedStep):
         model = sae._model_struct(need_shadows=True)
         stream = _stream()
         dt = L.DTYPE_BF16 if x.dtype == torch.bfloat16 else L.DTYPE_F32
+        t0 = self._mark()
         if self.peers is not None:
             if x_hat_out is not None:
                 raise ValueError("x_hat_out is not available with the peer exchange")
@@ -244,10 +265,6 @@ class ShardedFusedStep(FusedStep):
             L.call("sae_b200_shard_forward_p2p", ctypes.byref(model), L.ptr(x), dt,
                    ctypes.byref(cfg), ctypes.byref(peers), L.ptr(self.stats), L.ptr(self.fired),
                    stream)
-            st = self.read_stats()
-            if L.device_status() != 0:
-                raise L.SaeB200Error(L.SAE_ERR_DEVICE_TIMEOUT,
-                                     "a peer exchange barrier timed out (a rank stopped)")
         else:
             ex = self.exchange[:n * (sae.d_in + 1)]
             L.call("sae_b200_shard_forward", ctypes.byref(model), L.ptr(x), dt,
@@ -257,10 +274,22 @@ class ShardedFusedStep(FusedStep):
             L.call("sae_b200_shard_finish_forward", ctypes.byref(model), L.ptr(x), dt,
                    ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
                    L.ptr(ex), L.ptr(x_hat_out), stream)
-            st = self.read_stats()
-        self.nnz_last = st["nnz"]
+        t1 = self._mark()
+        pending = self._copy_stats(0)
         grads = self._grads_struct()
-        scratch = None
+        sampled = self.grad_feat == "sampled"
+        if sampled:
+            # ahead of the read; a no-op if this shard's CSR overflowed
+            L.call("sae_b200_shard_backward", ctypes.byref(model), ctypes.byref(grads),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
+                   self.rank, None, 0, stream)
+        t2 = self._mark()
+        st = self._wait_stats(pending)
+        if self.peers is not None and L.device_status() != 0:
+            raise L.SaeB200Error(L.SAE_ERR_DEVICE_TIMEOUT,
+                                 "a peer exchange barrier timed out (a rank stopped)")
+        self.nnz_last = st["nnz"]
+        rows_valid = sampled and not st["csr_overflow"]
         if st["csr_overflow"]:
             self.dense_fallbacks += 1
             scratch = self._dense_scratch_for(n)
@@ -270,25 +299,55 @@ class ShardedFusedStep(FusedStep):
                 L.call("sae_b200_store_full_pre", ctypes.byref(model), ctypes.byref(cfg),
                        L.ptr(self.ws), self.ws_bytes, stream)
                 cfg.pre_entries_only = 0
+            L.call("sae_b200_shard_backward", ctypes.byref(model), ctypes.byref(grads),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
+                   self.rank, L.ptr(scratch), scratch.numel(), stream)
         else:
             sae._sparse_decode_calls += 1
-        L.call("sae_b200_shard_backward", ctypes.byref(model), ctypes.byref(grads),
-               ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats), self.rank,
-               L.ptr(scratch), 0 if scratch is None else scratch.numel(), stream)
+            if not sampled:
+                L.call("sae_b200_shard_backward", ctypes.byref(model), ctypes.byref(grads),
+                       ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.stats),
+                       self.rank, None, 0, stream)
+        t3 = self._mark()
         self._allreduce(self.g_b_dec)                          # b_dec gradient
+        t4 = self._mark()
+        self._phase("forward", t0, t1)
+        self._phase("backward", t1, t2 if not st["csr_overflow"] and sampled else t3)
+        self._phase("bdec_allreduce", t3, t4)
         if after_backward is not None:
-            after_backward()
+            self._rows_cfg = cfg if rows_valid else None
+            try:
+                after_backward()
+            finally:
+                self._rows_cfg = None
         self._bind_grads()
         return st
 
     def grad_norm(self, max_norm: float = 1.0) -> None:
+        """clip_grad_norm_ over the whole dictionary: this shard's sum of
+        squares (from the sampled backward's per-feature partials when that
+        backward ran to completion, else a pass over the gradients; the
+        replicated b_dec counted on rank 0 only), summed over the ranks."""
+        t0 = self._mark()
         model = self.sae._model_struct(need_shadows=False)
         grads = self._grads_struct()
         if self.rank != 0:
             grads.b_dec = 0          # the replicated b_dec gradient counts once
         stream = _stream()
-        L.call("sae_b200_grad_sumsq", ctypes.byref(model), ctypes.byref(grads),
-               L.ptr(self.norm_ws), self.norm_ws.numel(), L.ptr(self.sumsq), stream)
+        cfg = getattr(self, "_rows_cfg", None)
+        if cfg is not None:
+            L.call("sae_b200_grad_sumsq_sampled", ctypes.byref(model), ctypes.byref(grads),
+                   ctypes.byref(cfg), L.ptr(self.ws), self.ws_bytes, L.ptr(self.norm_ws),
+                   self.norm_ws.numel(), L.ptr(self.sumsq), stream)
+        else:
+            L.call("sae_b200_grad_sumsq", ctypes.byref(model), ctypes.byref(grads),
+                   L.ptr(self.norm_ws), self.norm_ws.numel(), L.ptr(self.sumsq), stream)
         self._allreduce(self.sumsq)                            # clip_grad_norm_ sum
         L.call("sae_b200_clip_from_sumsq", L.ptr(self.sumsq), float(max_norm),
                L.ptr(self.stats), stream)
+        self._phase("norm", t0, self._mark())
+
+    def optimizer_step(self, wenc_factor: float = 1.0) -> None:
+        t0 = self._mark()
+        super().optimizer_step(wenc_factor)
+        self._phase("adam", t0, self._mark())

@@ -142,12 +142,16 @@ int64_t sae_b200_launch_count(void);
  * (cudaEvent_t handles owned by the caller; NULL, NULL clears it).
  * kernel: SAE_KERNEL_ENCODER_GEMM (tile GEMM of the forwards),
  * SAE_KERNEL_GRAD_GEMM (tile GEMM of the backwards, or the sampled backward),
- * SAE_KERNEL_DECODE (gathered decode of the forwards) or SAE_KERNEL_ADAM (all
- * launches of one sae_b200_adam_step). */
+ * SAE_KERNEL_DECODE (gathered decode of the forwards), SAE_KERNEL_ADAM (all
+ * launches of one sae_b200_adam_step), SAE_KERNEL_EXCHANGE or
+ * SAE_KERNEL_DENSE_WGRAD (below). */
 #define SAE_KERNEL_ENCODER_GEMM 0
 #define SAE_KERNEL_GRAD_GEMM 1
 #define SAE_KERNEL_DECODE 2   /* the gathered decode of every forward */
 #define SAE_KERNEL_ADAM 3     /* one optimizer update (Adam + renorm + bf16 copies) */
+#define SAE_KERNEL_EXCHANGE 4 /* the NVLink peer exchange of sae_b200_shard_forward_p2p
+                                 (both flag barriers and the cross-shard sum) */
+#define SAE_KERNEL_DENSE_WGRAD 5 /* the dW_enc tile GEMM of the dense backward */
 int sae_b200_set_kernel_timer(int kernel, void* start_event, void* stop_event);
 
 /* Bytes of scratch the training step needs for up to max_tokens tokens. */
@@ -359,6 +363,16 @@ int sae_b200_shard_backward(const SaeB200Model* model, const SaeB200Grads* grads
                             SaeB200StepStats* stats, int shard_rank, void* dense_scratch,
                             size_t dense_scratch_bytes, void* stream);
 /* *sumsq_out (device float) = sum of squares of the non-NULL gradients. */
+/* The same shard sum of squares straight after a sampled sae_b200_shard_backward
+ * that did not overflow (and after the b_dec all-reduce): from the backward's
+ * per-feature partials of the W_enc, W_dec, b_enc and log_threshold gradient
+ * rows plus grads->b_dec (pass NULL on the ranks that do not count the
+ * replicated b_dec), without another pass over the gradients. cfg, workspace:
+ * those of the backward; norm_workspace: SAE_GRAD_NORM_WORKSPACE_BYTES. */
+int sae_b200_grad_sumsq_sampled(const SaeB200Model* model, const SaeB200Grads* grads,
+                                const SaeB200StepConfig* cfg, const void* workspace,
+                                size_t workspace_bytes, void* norm_workspace,
+                                size_t norm_workspace_bytes, float* sumsq_out, void* stream);
 int sae_b200_grad_sumsq(const SaeB200Model* model, const SaeB200Grads* grads, void* workspace,
                         size_t workspace_bytes, float* sumsq_out, void* stream);
 /* stats->grad_norm = sqrt(*sumsq), stats->clip_coef = min(1, max_norm/(norm+1e-6))
