@@ -14,15 +14,17 @@ the fused decoder/encoder renormalisation, with the loop's stats read-back
 before the optimizer step.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
-                    [--workload atlas|sharded]
+                    [--workload atlas|sharded|inference] [--layers 35]
 
 Under torchrun every rank trains its own SAE (one layer per GPU, the atlas
 layout): no data-path collective, weak scaling; the timing is the max over
-ranks. `--workload sharded` instead trains one wide SAE (d_in = 4096,
-F = 131072, K = 64, LogNormal(log 80, 0.4) norms) with its dictionary split
-over the ranks and three all-reduces per step (strong scaling).
-`--impl reference` times the oracle's CPU restatement of the reference step on
-this host's cores (rank 0 only).
+ranks. `--layers 35` runs the 35-layer atlas configuration instead (layers
+round-robin over the GPUs, K timed steps per layer). `--workload sharded`
+trains one wide SAE (d_in = 4096, F = 131072, K = 64, LogNormal(log 80, 0.4)
+norms) with its dictionary split over the ranks and three cross-rank sums per
+step (strong scaling), with a per-phase time breakdown. `--impl reference`
+times the reference's fp32 CPU step (its torch-operator restatement in
+oracle/torch_step.py) on a bounded sample on this host's cores (rank 0 only).
 """
 from __future__ import annotations
 
@@ -797,6 +799,141 @@ def run_b200(args):
     return 0
 
 
+ATLAS_POOL_BATCHES = 16   # per-layer activation pool: 16 shards x 32768 tokens
+
+
+def run_atlas_layers(args):
+    """The 35-layer atlas configuration: independent SAEs (d=1536, F=49152,
+    K=50), layer l with its own seed-derived pool of 16 x 32768 tokens whose
+    norms are LogNormal(log(20 + 3 l), 0.4), placed round-robin on the GPUs
+    (layer l on rank l mod N, sae_b200.atlas) and trained one after another on
+    each GPU, as the reference's atlas loop trains them one after another
+    (run_atlas_rolling, sae_trainer_rolling.py:4040-4180). Per layer: set-up
+    (pool, init, threshold calibration; untimed), W warm-up steps, K timed
+    steps on device-resident batches (value), then K steps fed from pinned
+    host memory (e2e). A rank's time is the sum of its layers' timed regions;
+    the job's is the slowest rank's, so the 35 / ceil(35 / N) bound of the
+    round-robin placement shows in the value."""
+    import torch
+    import torch.distributed as dist
+
+    import sae_b200
+    from sae_b200 import _lib as L
+    from sae_b200 import atlas
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=600))
+    d, F, tokens, k = D_IN, N_FEAT, TOKENS, K_TARGET
+    mine = atlas.layers_for_rank(args.layers, world, rank)
+    side = torch.cuda.Stream(device=dev)
+    per_layer = []
+    launches0 = L.launch_count()
+    with ClockSampler(local) as clocks:
+        for layer in mine:
+            norm_mu = math.log(20.0 + 3.0 * layer)
+            pool = [sae_b200.superposition_batch(tokens, d, F, k, norm_mu, 0.4,
+                                                 seed=100_000 * (layer + 1) + i, device=dev)
+                    for i in range(ATLAS_POOL_BATCHES)]
+            sae = sae_b200.make_shard_sae(d, F, 0, 1, seed=layer, device=dev)
+            sae.ste_bandwidth = 0.2
+            calibrate(sae, pool, k, F)
+            opt = sae_b200.B200Adam(sae_b200.reference_param_groups(sae, LR), lr=LR,
+                                    betas=(0.9, 0.999), sae=sae, renorm=True)
+            fs = sae_b200.FusedStep(sae, opt, max_tokens=tokens)
+
+            def step(x):
+                out = fs.step(x, lambda_l0=LAMBDA, al_mu=MU, target_l0=k)
+                threshold_nudge(sae, out["l0"], k)
+                return out
+
+            for i in range(args.warmup):
+                step(pool[i % ATLAS_POOL_BATCHES])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            outs = [step(pool[(args.warmup + i) % ATLAS_POOL_BATCHES]) for i in range(args.steps)]
+            e1.record()
+            torch.cuda.synchronize()
+            dev_ms = e0.elapsed_time(e1)
+            # the same K steps fed from pinned host memory, double-buffered on a side stream
+            host = [b.cpu().pin_memory() for b in pool]
+            bufs = [torch.empty_like(pool[0]) for _ in range(2)]
+            ready = [torch.cuda.Event() for _ in range(2)]
+
+            def h2d(j, src):
+                with torch.cuda.stream(side):
+                    side.wait_stream(torch.cuda.current_stream())
+                    bufs[j].copy_(src, non_blocking=True)
+                    ready[j].record(side)
+
+            torch.cuda.synchronize()
+            h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            h0.record()
+            h2d(0, host[0])
+            for i in range(args.steps):
+                j = i % 2
+                torch.cuda.current_stream().wait_event(ready[j])
+                if i + 1 < args.steps:
+                    h2d(1 - j, host[(i + 1) % ATLAS_POOL_BATCHES])
+                step(bufs[j])
+            h1.record()
+            torch.cuda.synchronize()
+            per_layer.append({"layer": layer, "device_ms": dev_ms, "e2e_ms": h0.elapsed_time(h1),
+                              "l0": statistics.mean(o["l0"] for o in outs)})
+            del fs, opt, sae, pool, host, bufs
+            torch.cuda.empty_cache()
+    launches = L.launch_count() - launches0
+    status = L.device_status()
+    rank_ms = sum(p["device_ms"] for p in per_layer)
+    rank_e2e_ms = sum(p["e2e_ms"] for p in per_layer)
+    job_ms = atlas.max_over_ranks(rank_ms, device=dev)
+    job_e2e_ms = atlas.max_over_ranks(rank_e2e_ms, device=dev)
+    job_tokens = args.layers * args.steps * tokens
+    busiest = -(-args.layers // world)
+    if rank == 0:
+        value = job_tokens / (job_ms / 1e3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": job_ms / (busiest * args.steps), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "bf16",
+            "data": "synthetic superposition activations (seeded per layer, on device)",
+            "config": {"workload": (f"{args.layers}-layer atlas: independent d_in={d} F={F} "
+                                    f"K={k} SAEs, 32768-token microbatches, per-layer pools "
+                                    f"of {ATLAS_POOL_BATCHES} x 32768 tokens with norms "
+                                    "LogNormal(log(20 + 3 layer), 0.4), round-robin over "
+                                    "the GPUs, trained layer after layer on each GPU"),
+                       "layers": args.layers, "steps_per_layer": args.steps,
+                       "layers_on_busiest_gpu": busiest,
+                       "ideal_speedup": atlas.ideal_speedup(args.layers, world),
+                       "parallelism": f"atlas: layer l on GPU l mod {world}, no collective",
+                       "timed": "per layer, the K steps only (set-up and warm-up untimed); "
+                                "a rank's time is the sum over its layers, the job's the "
+                                "slowest rank's",
+                       "rank0_layers": per_layer},
+            "clocks": clocks.summary(),
+            "e2e": {"value": job_tokens / (job_e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": world * tokens * d * 2,
+                    "d2h_bytes_per_step": world * 2 * 64,
+                    "note": "every step's batch copied from pinned host memory on a side "
+                            "stream overlapped with the previous step; stats read back "
+                            "every step"},
+            "gpu_launches": int(launches),
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -815,6 +952,10 @@ def main():
                     help="atlas workload: also run the dead-feature aux loss with this fraction "
                          "of the dictionary marked dead (the trainer turns it on after 250 "
                          "silent steps)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="atlas workload: train this many independent layer SAEs (35 for the "
+                         "atlas configuration) round-robin over the GPUs, --steps timed steps "
+                         "each, instead of one SAE per GPU")
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per step (default: the workload's); smaller values are for "
                          "profiler captures, not for the reported metric")
@@ -829,6 +970,10 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.layers > 0:
+        if args.workload != "atlas":
+            ap.error("--layers applies to the atlas workload")
+        return run_atlas_layers(args)
     if args.workload == "inference":
         return run_inference(args)
     return run_b200(args)
