@@ -15,6 +15,7 @@ from .data import superposition_batch  # noqa: F401
 from .feed import DeviceActivationPool  # noqa: F401
 from .sae import sae_from_tensors  # noqa: F401
 from .sharded import ShardedFusedStep, make_shard_sae, shard_range, shard_sae  # noqa: F401
+from . import revival  # noqa: F401
 
 __all__ = ["B200JumpReLUSAE", "make_sae", "install", "B200Adam", "FusedStep",
            "reference_param_groups", "superposition_batch", "SaeB200Error", "load_library",
