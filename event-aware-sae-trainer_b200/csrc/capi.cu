@@ -19,6 +19,7 @@
 #include "sae_b200.h"
 #include "step_kernels.cuh"
 #include "aux_kernels.cuh"
+#include "sampled_ring.cuh"
 #include "peer_kernels.cuh"
 #include "tile_gemm.cuh"
 #include "gemm_kernels.cuh"
@@ -298,6 +299,47 @@ int sampled_threads(int d) {
   return (nvec / U + 31) / 32 * 32;
 }
 
+// SAE_B200_SAMPLED=plain selects the register-staged sampled backward instead
+// of the shared-memory ring (same results); SAE_B200_RING_SLOTS overrides the
+// ring's slot count (4..32).
+bool sampled_ring_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SAE_B200_SAMPLED");
+    return !(v != nullptr && std::strcmp(v, "plain") == 0);
+  }();
+  return on;
+}
+
+int ring_slots(int d) {
+  const char* v = std::getenv("SAE_B200_RING_SLOTS");
+  int r = v != nullptr ? std::atoi(v) : (48 * 1024) / (4 * d);
+  return std::max(4, std::min(32, r));
+}
+
+// Ring variant launch: the dynamic shared-memory limit is raised once per
+// device and instantiation.
+template <int C, int U, int MT, int MB>
+int launch_ring(int grid, int bthr, int R, int d, cudaStream_t stream, const int* offs,
+                const int* tok, const uint32_t* val, const bf16* go, const bf16* xc,
+                const bf16* w_dec, const float* theta, int n_seg, int n_tokens, float eps,
+                int accumulate, float* g_wdec, float* g_wenc, float* g_logthr, float* g_benc,
+                float* db_enc, int* counter, const SaeB200StepStats* stats, const int* seg_rows,
+                int honor_overflow, float* row_sumsq) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(SAE_ERR_CUDA, "no usable current device");
+  static std::once_flag once[kMaxDevices];
+  std::call_once(once[dev], [] {
+    cudaFuncSetAttribute(sampled_backward_ring_kernel<C, U, MT, MB>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  const size_t smem = ring_smem_bytes(d, R);
+  sampled_backward_ring_kernel<C, U, MT, MB><<<grid, bthr, smem, stream>>>(
+      offs, tok, val, go, xc, w_dec, theta, n_seg, n_tokens, d, eps, accumulate, g_wdec, g_wenc,
+      g_logthr, g_benc, db_enc, counter, stats, seg_rows, honor_overflow, row_sumsq, R);
+  return SAE_OK;
+}
+
 void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const bf16* go,
                     const bf16* xc, const bf16* w_dec, const float* theta, int n_seg,
                     int n_tokens, int d, float eps, int accumulate, float* g_wdec, float* g_wenc,
@@ -308,6 +350,30 @@ void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const 
   const int U = (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
   const int bthr = sampled_threads(d);
   const int per_sm = bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1);
+  if (sampled_ring_enabled()) {
+    const int R = ring_slots(d);
+    // blocks per SM as the shared memory allows (at most the register bound)
+    // (228 KB of shared memory per SM; 1 KB reserved per block, ~1 KB static)
+    const int fit = std::max(1, static_cast<int>((228 * 1024) / (ring_smem_bytes(d, R) + 2048)));
+    const int grid = device_info().sm_count * std::min(per_sm, fit);
+#define SAE_RING(CC, UU, MT, MB)                                                             \
+  launch_ring<CC, UU, MT, MB>(grid, bthr, R, d, stream, offs, tok, val, go, xc, w_dec, theta, \
+                              n_seg, n_tokens, eps, accumulate, g_wdec, g_wenc, g_logthr,     \
+                              g_benc, db_enc, counter, stats, seg_rows, honor_overflow,       \
+                              row_sumsq)
+    if (U == 1) {
+      if (bthr <= 192) SAE_RING(2, 1, 192, 4);
+      else if (bthr <= 256) SAE_RING(4, 1, 256, 2);
+      else if (bthr <= 512) SAE_RING(4, 1, 512, 1);
+      else SAE_RING(4, 1, 1024, 1);
+    } else {
+      if (bthr <= 192) SAE_RING(2, 2, 192, 2);
+      else if (bthr <= 256) SAE_RING(2, 2, 256, 2);
+      else SAE_RING(2, 2, 512, 1);
+    }
+#undef SAE_RING
+    return;
+  }
   const int grid = device_info().sm_count * per_sm * 2;
 #define SAE_SAMPLED(CC, UU, MT, MB)                                                            \
   sampled_backward_kernel<CC, UU, MT, MB><<<grid, bthr, 0, stream>>>(                         \
