@@ -538,10 +538,15 @@ def run_b200(args):
         F = F_total
         torch.manual_seed(1000 + rank)
         sae = sae_b200.make_sae(d, F, seed=rank).to(dev)
-    pool = [sae_b200.superposition_batch(tokens, d, F_total, k_target, wl["norm_mu"],
+    gen_k = k_target
+    if args.l0:
+        # an L0 other than the workload's (e.g. early training, before the
+        # controller has brought L0 down): the thresholds are calibrated to it
+        k_target = args.l0
+    pool = [sae_b200.superposition_batch(tokens, d, F_total, gen_k, wl["norm_mu"],
                                          wl["norm_sigma"], seed=data_seed + 7 * i, device=dev)
             for i in range(POOL_BATCHES)]
-    sae.ste_bandwidth = 0.2
+    sae.ste_bandwidth = args.ste_bandwidth
     thr = calibrate(sae, pool, k_target, F_total)
     opt = sae_b200.B200Adam(sae_b200.reference_param_groups(sae, wl["lr"]), lr=wl["lr"],
                             betas=(0.9, 0.999), sae=sae, renorm=True)
@@ -709,6 +714,8 @@ def run_b200(args):
                                        if sharded else
                                        f"atlas: {world} independent SAE(s), one per GPU"),
                        "l0_target": k_target, "l0_measured": l0_timed,
+                       "ste_bandwidth": args.ste_bandwidth,
+                       "entries_per_token": pairs_mean / tokens,
                        "aux_loss": ({"dead_fraction": args.aux_dead, "k": aux_k}
                                     if aux_dead is not None else None),
                        "threshold_calibrated": thr,
@@ -952,6 +959,12 @@ def main():
                     help="atlas workload: also run the dead-feature aux loss with this fraction "
                          "of the dictionary marked dead (the trainer turns it on after 250 "
                          "silent steps)")
+    ap.add_argument("--ste-bandwidth", type=float, default=0.2,
+                    help="STE band half-width epsilon (the scheduler adapts it up to 0.5); "
+                         "the sampled backward's work grows with the band's population")
+    ap.add_argument("--l0", type=float, default=0.0,
+                    help="calibrate the thresholds to this mean L0 instead of the workload's "
+                         "(e.g. an early-training state); not the metric's configuration")
     ap.add_argument("--layers", type=int, default=0,
                     help="atlas workload: train this many independent layer SAEs (35 for the "
                          "atlas configuration) round-robin over the GPUs, --steps timed steps "
