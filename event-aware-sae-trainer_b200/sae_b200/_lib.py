@@ -282,7 +282,11 @@ def launch_count() -> int:
 
 
 def set_kernel_timer(kernel: int, start_event=None, stop_event=None) -> None:
-    """Record torch.cuda.Event pairs around the chosen tile GEMM's launches."""
+    """Record torch.cuda.Event pairs around the chosen kernel's launches."""
+    for ev in (start_event, stop_event):
+        # torch creates the CUDA event on its first record: make sure it exists
+        if ev is not None and ev.cuda_event == 0:
+            ev.record()
     s = 0 if start_event is None else start_event.cuda_event
     e = 0 if stop_event is None else stop_event.cuda_event
     call("sae_b200_set_kernel_timer", kernel, s, e)

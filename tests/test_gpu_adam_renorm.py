@@ -9,7 +9,9 @@ gradient dampening factor, torch.optim.Adam over the trainer's four groups
 The reference here is exactly that torch sequence on the reference layout
 (W_dec.weight [d, F] contiguous), on the GPU in fp32. Both sides compute in
 fp32 with the same operation order up to the order of the two gradient
-scalings, so the parameters agree to 1e-5 relative after one and three steps.
+scalings and the summation order of the clip norm (1e-5 relative), so the
+parameters agree to 1e-5 relative after one and three steps and the second
+moments, which square the clipped gradient, to 3e-5.
 Both row widths are covered: d=64 (one warp per row) and d=1536 (the wide-row
 kernel of the benchmark shape).
 """
@@ -86,7 +88,10 @@ def test_fused_adam_renorm_matches_torch(d, F, clip):
                 st_b = bopt.state[p]
                 st_t = tadam.state[plain[k]]
                 torch.testing.assert_close(st_b["exp_avg"], st_t["exp_avg"], rtol=1e-5, atol=1e-8)
-                torch.testing.assert_close(st_b["exp_avg_sq"], st_t["exp_avg_sq"], rtol=1e-5,
+                # the two clip coefficients come from fp32 sums of squares taken in
+                # different orders (they agree to 1e-5 relative, asserted above):
+                # exp_avg_sq holds the clipped gradient squared, so twice that
+                torch.testing.assert_close(st_b["exp_avg_sq"], st_t["exp_avg_sq"], rtol=3e-5,
                                            atol=1e-12)
             # the bf16 tensor-core copies are the rounded fp32 masters
             assert torch.equal(sae._shadow_enc, sae.W_enc.weight.detach().to(torch.bfloat16))
