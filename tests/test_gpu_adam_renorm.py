@@ -87,7 +87,7 @@ def test_fused_adam_renorm_matches_torch(d, F, clip):
                             (sae.W_enc.weight, sae.W_dec.weight)):
                 st_b = bopt.state[p]
                 st_t = tadam.state[plain[k]]
-                torch.testing.assert_close(st_b["exp_avg"], st_t["exp_avg"], rtol=1e-5, atol=1e-8)
+                torch.testing.assert_close(st_b["exp_avg"], st_t["exp_avg"], rtol=2e-5, atol=1e-8)
                 # the two clip coefficients come from fp32 sums of squares taken in
                 # different orders (they agree to 1e-5 relative, asserted above):
                 # exp_avg_sq holds the clipped gradient squared, so twice that
