@@ -283,6 +283,17 @@ bool pair_mode_enabled() {
   return on;
 }
 
+// Feature tiles (pairs) per rasterisation group of the tile GEMMs;
+// SAE_B200_GROUP_M overrides the default (1..1024).
+int raster_group() {
+  static const int g = [] {
+    const char* v = std::getenv("SAE_B200_GROUP_M");
+    const int x = v != nullptr ? std::atoi(v) : TC_GROUP_M;
+    return std::max(1, std::min(1024, x));
+  }();
+  return g;
+}
+
 bool tc_eligible(int64_t d, int64_t F, int force_simt) {
   if (force_simt) return false;
   const DeviceInfo di = device_info();
@@ -476,7 +487,7 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
         const int clusters = std::min(total_pairs, max_clusters);
         if (timer >= 0) timer_begin(timer, stream);
         tc2_tile_gemm<Epi><<<2 * clusters, TC2_THREADS, smem2, stream>>>(
-            tm_w, tm_t_half, tm_aux2, m_pairs, n_tiles, k_blocks, e);
+            tm_w, tm_t_half, tm_aux2, m_pairs, n_tiles, k_blocks, raster_group(), e);
         const int rc = check_launch("tc2_tile_gemm");
         if (timer >= 0) timer_end(timer, stream);
         return rc;
@@ -491,7 +502,7 @@ int launch_tile_gemm(const bf16* w, const bf16* tok, int64_t F, int64_t B, int64
     const int grid = std::min(total, device_info().sm_count);
     if (timer >= 0) timer_begin(timer, stream);
     tc_tile_gemm<Epi><<<grid, TC_THREADS, smem, stream>>>(tm_w, tm_t, tm_aux, m_tiles, n_tiles,
-                                                          k_blocks, e);
+                                                          k_blocks, raster_group(), e);
     const int rc = check_launch("tc_tile_gemm");
     if (timer >= 0) timer_end(timer, stream);
     return rc;

@@ -38,7 +38,7 @@ constexpr int TC_A_BYTES = TILE_M * TILE_K * 2;   // 16 KiB
 constexpr int TC_B_BYTES = TILE_N * TILE_K * 2;   // 32 KiB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_THREADS = 192;   // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
-constexpr int TC_GROUP_M = 16;    // feature tiles per rasterisation group
+constexpr int TC_GROUP_M = 16;    // default feature tiles (pairs) per rasterisation group
 constexpr int TC_BARRIER_BYTES = 256;
 constexpr uint32_t TC_TMEM_COLS = 2 * TILE_N;     // two fp32 accumulators
 
@@ -124,15 +124,16 @@ struct TileCoord {
   int m, n;
 };
 
-// Tiles are visited in groups of TC_GROUP_M feature tiles; inside a group the
+// Tiles are visited in groups of group_m feature tiles; inside a group the
 // feature tile varies fastest, so the CTAs running at any moment share a few
-// token slabs and a few weight slabs in L2.
-__device__ __forceinline__ TileCoord tile_coord(int t, int m_tiles, int n_tiles) {
-  const int per_group = TC_GROUP_M * n_tiles;
+// token slabs and a few weight slabs in L2. The token operand is streamed
+// once per group, the weight operand about once in all.
+__device__ __forceinline__ TileCoord tile_coord(int t, int m_tiles, int n_tiles, int group_m) {
+  const int per_group = group_m * n_tiles;
   const int g = t / per_group;
   const int r = t - g * per_group;
-  const int m0 = g * TC_GROUP_M;
-  const int gm = min(TC_GROUP_M, m_tiles - m0);
+  const int m0 = g * group_m;
+  const int gm = min(group_m, m_tiles - m0);
   TileCoord c;
   c.m = m0 + r % gm;
   c.n = r / gm;
@@ -153,7 +154,7 @@ template <class Epi>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_tile_gemm(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_t,
                  const __grid_constant__ CUtensorMap tm_aux, int m_tiles, int n_tiles,
-                 int k_blocks, const Epi epi) {
+                 int k_blocks, int group_m, const Epi epi) {
   constexpr int AUX = Epi::kAux;
   constexpr int STAGES = TcConfig<AUX>::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t aux_parity = 0;
       int kit = 0, it = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
-        const TileCoord tc = tile_coord(t, m_tiles, n_tiles);
+        const TileCoord tc = tile_coord(t, m_tiles, n_tiles, group_m);
         for (int kb = 0; kb < k_blocks; ++kb, ++kit) {
           const int s = kit % STAGES;
           const uint32_t ph = (kit / STAGES) & 1;
@@ -321,7 +322,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!mbar_wait(&acc_full[acc], aph, abort_flag)) break;
       if (AUX == AUX_LOAD && !mbar_wait(aux_full, it & 1, abort_flag)) break;
       tc_fence_after();
-      const TileCoord tc = tile_coord(t, m_tiles, n_tiles);
+      const TileCoord tc = tile_coord(t, m_tiles, n_tiles, group_m);
       Epi e = epi;
       e.begin_tile(tc.m, tc.n, row, q, lane, AUX == AUX_NONE ? nullptr : s_aux);
       const uint32_t t_row =
@@ -491,7 +492,7 @@ template <class Epi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
     tc2_tile_gemm(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_t,
                   const __grid_constant__ CUtensorMap tm_aux, int m_pairs, int n_tiles,
-                  int k_blocks, const Epi epi) {
+                  int k_blocks, int group_m, const Epi epi) {
   constexpr int AUX = Epi::kAux;
   constexpr int STAGES = Tc2Config<AUX>::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -561,7 +562,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
       bool ok = true;
       int kit = 0;
       for (int t = pair; t < total && ok; t += pairs) {
-        const TileCoord tc = tile_coord(t, m_pairs, n_tiles);
+        const TileCoord tc = tile_coord(t, m_pairs, n_tiles, group_m);
         const int f0 = (2 * tc.m + static_cast<int>(rank)) * TILE_M;
         const int t0 = tc.n * TILE_N + static_cast<int>(rank) * (TILE_N / 2);
         for (int kb = 0; kb < k_blocks; ++kb, ++kit) {
@@ -589,7 +590,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
       bool aux_issued = false;
       int it = 0;
       for (int t = pair; t < total; t += pairs, ++it) {
-        const TileCoord tc = tile_coord(t, m_pairs, n_tiles);
+        const TileCoord tc = tile_coord(t, m_pairs, n_tiles, group_m);
         const int f0 = (2 * tc.m + static_cast<int>(rank)) * TILE_M;
         const uint32_t ph = it & 1;
         if (!mbar_wait(aux_empty, ph ^ 1, abort_flag)) break;
@@ -670,7 +671,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC2_THREADS, 1)
       if (!mbar_wait(&acc_full[acc], aph, abort_flag)) break;
       if (AUX == AUX_LOAD && !mbar_wait(aux_full, it & 1, abort_flag)) break;
       tc_fence_after();
-      const TileCoord tc = tile_coord(t, m_pairs, n_tiles);
+      const TileCoord tc = tile_coord(t, m_pairs, n_tiles, group_m);
       const int m_tile = 2 * tc.m + static_cast<int>(rank);
       Epi e = epi;
       e.begin_tile(m_tile, tc.n, row, q, lane, AUX == AUX_NONE ? nullptr : s_aux);
