@@ -310,13 +310,14 @@ int sampled_threads(int d) {
   return (nvec / U + 31) / 32 * 32;
 }
 
-// SAE_B200_SAMPLED=plain selects the register-staged sampled backward instead
-// of the shared-memory ring (same results); SAE_B200_RING_SLOTS overrides the
-// ring's slot count (4..32).
+// SAE_B200_SAMPLED=ring selects the shared-memory ring variant of the sampled
+// backward instead of the register-staged kernel (same results; measured
+// slower at the benchmark shape: 3.7 ms against 2.0 ms, issue-bound on its
+// barrier waits); SAE_B200_RING_SLOTS overrides its slot count (4..32).
 bool sampled_ring_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("SAE_B200_SAMPLED");
-    return !(v != nullptr && std::strcmp(v, "plain") == 0);
+    return v != nullptr && std::strcmp(v, "ring") == 0;
   }();
   return on;
 }
