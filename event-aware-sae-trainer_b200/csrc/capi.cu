@@ -304,10 +304,20 @@ bool tc_eligible(int64_t d, int64_t F, int force_simt) {
 // block of d / (8 U) threads (U = 2 for wide rows: more features in flight
 // per SM). seg_rows maps segments to feature rows (the aux backward).
 // Threads per block of the sampled backward at row width d (a multiple of 32).
-int sampled_threads(int d) {
+// 16-byte column vectors per thread (U) of the sampled backward: 2 for wide
+// rows (more features in flight per SM). SAE_B200_SAMPLED_U=1|2 overrides it.
+int sampled_u(int d) {
+  static const int forced = [] {
+    const char* v = std::getenv("SAE_B200_SAMPLED_U");
+    return v != nullptr ? std::atoi(v) : 0;
+  }();
   const int nvec = d / 8;
-  const int U = (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
-  return (nvec / U + 31) / 32 * 32;
+  if ((forced == 1 || forced == 2) && nvec % forced == 0) return forced;
+  return (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
+}
+
+int sampled_threads(int d) {
+  return (d / 8 / sampled_u(d) + 31) / 32 * 32;
 }
 
 // SAE_B200_SAMPLED=ring selects the shared-memory ring variant of the sampled
@@ -358,10 +368,9 @@ void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const 
                     float* g_logthr, float* g_benc, float* db_enc, int* counter,
                     const SaeB200StepStats* stats, const int* seg_rows, int honor_overflow,
                     cudaStream_t stream, float* row_sumsq = nullptr) {
-  const int nvec = d / 8;
-  const int U = (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
+  const int U = sampled_u(d);
   const int bthr = sampled_threads(d);
-  const int per_sm = bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1);
+  const int per_sm = bthr <= 96 ? 5 : (bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1));
   if (sampled_ring_enabled()) {
     const int R = ring_slots(d);
     // blocks per SM as the shared memory allows (at most the register bound)
@@ -397,7 +406,8 @@ void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const 
     else if (bthr <= 512) SAE_SAMPLED(4, 1, 512, 1);
     else SAE_SAMPLED(4, 1, 1024, 1);
   } else {
-    if (bthr <= 192) SAE_SAMPLED(2, 2, 192, 2);
+    if (bthr <= 96) SAE_SAMPLED(2, 2, 96, 5);
+    else if (bthr <= 192) SAE_SAMPLED(2, 2, 192, 2);
     else if (bthr <= 256) SAE_SAMPLED(2, 2, 256, 2);
     else SAE_SAMPLED(2, 2, 512, 1);
   }

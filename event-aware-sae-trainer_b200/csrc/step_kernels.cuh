@@ -28,6 +28,18 @@ __device__ __forceinline__ void unpack8(const uint4 u, float (&f)[8]) {
   }
 }
 
+// Two independent fp32 FMAs in one instruction (sm_100 fma.rn.f32x2):
+// (d0, d1) = (a0 * b0 + d0, a1 * b1 + d1), each rounded like fmaf.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0,
+                                     float b1) {
+  uint64_t d, a, b;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(d0), "f"(d1));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   const uint32_t l = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
   const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
@@ -777,15 +789,17 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
       float part[C];
 #pragma unroll
       for (int r = 0; r < C; ++r) {
-        float a = 0.f;
+        // even and odd columns in the two halves of packed FMAs
+        float a0 = 0.f, a1 = 0.f;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           float g8[8];
           unpack8(gu[r][u], g8);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) a = fmaf(g8[j], wf[8 * u + j], a);
+          for (int j = 0; j < 8; j += 2)
+            fma2(a0, a1, g8[j], g8[j + 1], wf[8 * u + j], wf[8 * u + j + 1]);
         }
-        part[r] = a;
+        part[r] = a0 + a1;
       }
       const float q = warp_sum_c<C>(part, lane);
       constexpr int kStride = 32 / C;
@@ -805,9 +819,9 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
               unpack8(gu[r][u], g8);
               unpack8(xu[r][u], x8);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                ad[8 * u + j] = fmaf(p, g8[j], ad[8 * u + j]);
-                ae[8 * u + j] = fmaf(gfv, x8[j], ae[8 * u + j]);
+              for (int j = 0; j < 8; j += 2) {
+                fma2(ad[8 * u + j], ad[8 * u + j + 1], p, p, g8[j], g8[j + 1]);
+                fma2(ae[8 * u + j], ae[8 * u + j + 1], gfv, gfv, x8[j], x8[j + 1]);
               }
             }
             db += gfv;
@@ -991,7 +1005,7 @@ __global__ void __launch_bounds__(1024)
             unpack8(u[r], wf);
             const float a = s_v[i + r * G];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+            for (int j = 0; j < 8; j += 2) fma2(acc[j], acc[j + 1], a, a, wf[j], wf[j + 1]);
           }
         }
         for (; i < n; i += G) {
@@ -999,7 +1013,7 @@ __global__ void __launch_bounds__(1024)
           unpack8(__ldg(wcol + static_cast<size_t>(s_f[i]) * nvec), wf);
           const float a = s_v[i];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+          for (int j = 0; j < 8; j += 2) fma2(acc[j], acc[j + 1], a, a, wf[j], wf[j + 1]);
         }
       }
     }
