@@ -19,7 +19,6 @@
 #include "sae_b200.h"
 #include "step_kernels.cuh"
 #include "aux_kernels.cuh"
-#include "sampled_ring.cuh"
 #include "peer_kernels.cuh"
 #include "tile_gemm.cuh"
 #include "gemm_kernels.cuh"
@@ -304,8 +303,11 @@ bool tc_eligible(int64_t d, int64_t F, int force_simt) {
 // block of d / (8 U) threads (U = 2 for wide rows: more features in flight
 // per SM). seg_rows maps segments to feature rows (the aux backward).
 // Threads per block of the sampled backward at row width d (a multiple of 32).
-// 16-byte column vectors per thread (U) of the sampled backward: 2 for wide
-// rows (more features in flight per SM). SAE_B200_SAMPLED_U=1|2 overrides it.
+// 16-byte column vectors per thread (U) of the sampled backward: 2 from
+// d = 1024 up (at d = 1536: 3 warps per feature instead of 6, which halves the
+// per-warp work of every entry -- the butterfly, the partial sums, the flag
+// logic -- measured 1.5-1.6 ms against 2.0-2.1 ms per 32768-token step).
+// SAE_B200_SAMPLED_U=1|2 overrides it.
 int sampled_u(int d) {
   static const int forced = [] {
     const char* v = std::getenv("SAE_B200_SAMPLED_U");
@@ -313,53 +315,21 @@ int sampled_u(int d) {
   }();
   const int nvec = d / 8;
   if ((forced == 1 || forced == 2) && nvec % forced == 0) return forced;
-  return (nvec % 2 == 0 && nvec / 2 >= 128) ? 2 : 1;
+  return (nvec % 2 == 0 && nvec / 2 >= 64) ? 2 : 1;
+}
+
+// Entries per chunk (one block barrier each) of the sampled backward at 96
+// threads: SAE_B200_SAMPLED_C=4 selects 4 instead of 2.
+int sampled_chunk() {
+  static const int c = [] {
+    const char* v = std::getenv("SAE_B200_SAMPLED_C");
+    return (v != nullptr && std::atoi(v) == 4) ? 4 : 2;
+  }();
+  return c;
 }
 
 int sampled_threads(int d) {
   return (d / 8 / sampled_u(d) + 31) / 32 * 32;
-}
-
-// SAE_B200_SAMPLED=ring selects the shared-memory ring variant of the sampled
-// backward instead of the register-staged kernel (same results; measured
-// slower at the benchmark shape: 3.7 ms against 2.0 ms, issue-bound on its
-// barrier waits); SAE_B200_RING_SLOTS overrides its slot count (4..32).
-bool sampled_ring_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("SAE_B200_SAMPLED");
-    return v != nullptr && std::strcmp(v, "ring") == 0;
-  }();
-  return on;
-}
-
-int ring_slots(int d) {
-  const char* v = std::getenv("SAE_B200_RING_SLOTS");
-  int r = v != nullptr ? std::atoi(v) : (48 * 1024) / (4 * d);
-  return std::max(4, std::min(32, r));
-}
-
-// Ring variant launch: the dynamic shared-memory limit is raised once per
-// device and instantiation.
-template <int C, int U, int MT, int MB>
-int launch_ring(int grid, int bthr, int R, int d, cudaStream_t stream, const int* offs,
-                const int* tok, const uint32_t* val, const bf16* go, const bf16* xc,
-                const bf16* w_dec, const float* theta, int n_seg, int n_tokens, float eps,
-                int accumulate, float* g_wdec, float* g_wenc, float* g_logthr, float* g_benc,
-                float* db_enc, int* counter, const SaeB200StepStats* stats, const int* seg_rows,
-                int honor_overflow, float* row_sumsq) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return fail(SAE_ERR_CUDA, "no usable current device");
-  static std::once_flag once[kMaxDevices];
-  std::call_once(once[dev], [] {
-    cudaFuncSetAttribute(sampled_backward_ring_kernel<C, U, MT, MB>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  });
-  const size_t smem = ring_smem_bytes(d, R);
-  sampled_backward_ring_kernel<C, U, MT, MB><<<grid, bthr, smem, stream>>>(
-      offs, tok, val, go, xc, w_dec, theta, n_seg, n_tokens, d, eps, accumulate, g_wdec, g_wenc,
-      g_logthr, g_benc, db_enc, counter, stats, seg_rows, honor_overflow, row_sumsq, R);
-  return SAE_OK;
 }
 
 void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const bf16* go,
@@ -371,30 +341,6 @@ void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const 
   const int U = sampled_u(d);
   const int bthr = sampled_threads(d);
   const int per_sm = bthr <= 96 ? 5 : (bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1));
-  if (sampled_ring_enabled()) {
-    const int R = ring_slots(d);
-    // blocks per SM as the shared memory allows (at most the register bound)
-    // (228 KB of shared memory per SM; 1 KB reserved per block, ~1 KB static)
-    const int fit = std::max(1, static_cast<int>((228 * 1024) / (ring_smem_bytes(d, R) + 2048)));
-    const int grid = device_info().sm_count * std::min(per_sm, fit);
-#define SAE_RING(CC, UU, MT, MB)                                                             \
-  launch_ring<CC, UU, MT, MB>(grid, bthr, R, d, stream, offs, tok, val, go, xc, w_dec, theta, \
-                              n_seg, n_tokens, eps, accumulate, g_wdec, g_wenc, g_logthr,     \
-                              g_benc, db_enc, counter, stats, seg_rows, honor_overflow,       \
-                              row_sumsq)
-    if (U == 1) {
-      if (bthr <= 192) SAE_RING(2, 1, 192, 4);
-      else if (bthr <= 256) SAE_RING(4, 1, 256, 2);
-      else if (bthr <= 512) SAE_RING(4, 1, 512, 1);
-      else SAE_RING(4, 1, 1024, 1);
-    } else {
-      if (bthr <= 192) SAE_RING(2, 2, 192, 2);
-      else if (bthr <= 256) SAE_RING(2, 2, 256, 2);
-      else SAE_RING(2, 2, 512, 1);
-    }
-#undef SAE_RING
-    return;
-  }
   const int grid = device_info().sm_count * per_sm * 2;
 #define SAE_SAMPLED(CC, UU, MT, MB)                                                            \
   sampled_backward_kernel<CC, UU, MT, MB><<<grid, bthr, 0, stream>>>(                         \
@@ -406,7 +352,8 @@ void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const 
     else if (bthr <= 512) SAE_SAMPLED(4, 1, 512, 1);
     else SAE_SAMPLED(4, 1, 1024, 1);
   } else {
-    if (bthr <= 96) SAE_SAMPLED(2, 2, 96, 5);
+    if (bthr <= 96 && sampled_chunk() == 4) SAE_SAMPLED(4, 2, 96, 4);
+    else if (bthr <= 96) SAE_SAMPLED(2, 2, 96, 5);
     else if (bthr <= 192) SAE_SAMPLED(2, 2, 192, 2);
     else if (bthr <= 256) SAE_SAMPLED(2, 2, 256, 2);
     else SAE_SAMPLED(2, 2, 512, 1);
@@ -824,12 +771,23 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
 
 // Gathered decode; partial != NULL writes the shard's decoder sums and counts
 // instead of the residual (dictionary-sharded step).
+// Row groups per token of the decode (blocks of G x V threads):
+// SAE_B200_DECODE_G=1|2|4 overrides the default.
+int decode_groups(int V) {
+  static const int forced = [] {
+    const char* v = std::getenv("SAE_B200_DECODE_G");
+    return v != nullptr ? std::atoi(v) : 0;
+  }();
+  if ((forced == 1 || forced == 2 || forced == 4) && forced * V <= 1024) return forced;
+  return std::min(4, std::max(1, 512 / V));
+}
+
 int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const ForwardCtx& c,
                    float* x_hat_out, float* partial, cudaStream_t stream) {
   const int64_t B = c.B, d = c.d, F = c.F;
   const Ws& w = c.w;
   const int V = vec_threads(d);
-  const int G = std::min(4, std::max(1, 512 / V));   // row groups per token
+  const int G = decode_groups(V);   // row groups per token
   const size_t dyn = static_cast<size_t>(G - 1) * V * 2 * sizeof(float4);
   // Tokens' active counts are heavy-tailed: blocks take tokens in order of
   // decreasing count, round robin (a fixed, data-determined assignment, so the
