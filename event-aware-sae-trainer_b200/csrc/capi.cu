@@ -814,20 +814,6 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
   token_count_kernel<<<grid_for(B * 32, 256), 256, 0, stream>>>(w.mask, B, c.mask_words,
                                                                w.order_k0, w.order_v0);
   SAE_TRY(check_launch("token_count_kernel"));
-  // token-major active lists (in the CSR arrays, which the backward fills
-  // only later): offsets from the counts, then one warp per token
-  const bool lists = decode_lists_enabled() && c.cap > 0;
-  if (lists) {
-    size_t scan_bytes = w.order_tmp_bytes;
-    if (cub::DeviceScan::ExclusiveSum(w.order_tmp, scan_bytes, w.order_k0, w.tok_offs,
-                                      static_cast<int>(B), stream) != cudaSuccess)
-      return fail(SAE_ERR_CUDA, "decode list offset scan failed");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    token_list_kernel<<<grid_for(B * 32, 256), 256, 0, stream>>>(
-        w.mask, w.pre, B, c.mask_words, static_cast<int>(pre_pitch(B)), w.order_k0, w.tok_offs,
-        c.cap, w.csr_tok, reinterpret_cast<float*>(w.csr_val));
-    SAE_TRY(check_launch("token_list_kernel"));
-  }
   size_t tmp_bytes = w.order_tmp_bytes;
   if (cub::DeviceRadixSort::SortPairsDescending(w.order_tmp, tmp_bytes, w.order_k0, w.order_k1,
                                                 w.order_v0, w.order_v1, static_cast<int>(B), 0,
@@ -842,6 +828,20 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
       w.gosum_part, partial, w.order_v1, lists ? w.order_k0 : nullptr, w.tok_offs,          \
       lists ? w.csr_tok : nullptr, reinterpret_cast<const float*>(w.csr_val), c.cap)
   timer_begin(SAE_KERNEL_DECODE, stream);
+  // token-major active lists (in the CSR arrays, which the backward fills
+  // only later): offsets from the counts, then one warp per token
+  const bool lists = decode_lists_enabled() && c.cap > 0;
+  if (lists) {
+    size_t scan_bytes = w.order_tmp_bytes;
+    if (cub::DeviceScan::ExclusiveSum(w.order_tmp, scan_bytes, w.order_k0, w.tok_offs,
+                                      static_cast<int>(B), stream) != cudaSuccess)
+      return fail(SAE_ERR_CUDA, "decode list offset scan failed");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    token_list_kernel<<<grid_for(B * 32, 256), 256, 0, stream>>>(
+        w.mask, w.pre, B, c.mask_words, static_cast<int>(pre_pitch(B)), w.order_k0, w.tok_offs,
+        c.cap, w.csr_tok, reinterpret_cast<float*>(w.csr_val));
+    SAE_TRY(check_launch("token_list_kernel"));
+  }
   if (x_dtype == SAE_DTYPE_BF16) {
     if (G >= 4) SAE_DECODE(bf16, 4);
     else if (G == 2 || G == 3) SAE_DECODE(bf16, 2);
