@@ -679,7 +679,7 @@ def run_b200(args):
         enc_tf = gemm_flop / (enc_ms / 1e3) / 1e12
         grad_tf = gemm_flop / (grad_ms / 1e3) / 1e12
         traffic_scale = (d * F) / (D_IN * N_FEAT) * (tokens / TOKENS)
-        gemm_bwd = args.grad_feat == "gemm"
+        gemm_bwd = fs.grad_feat == "gemm"   # the backward in effect at the end ("auto" may switch)
         entries = fs.pre_store == "entries" and not gemm_bwd and aux_dead is None
         dom_ms, dom_tf, dom_name, dom_traffic = (
             (enc_ms, enc_tf, "encoder tile GEMM (tcgen05 cta_group::2) + JumpReLU epilogue",
@@ -975,7 +975,7 @@ def main():
     ap.add_argument("--pre-store", choices=["entries", "full"], default="entries",
                     help="encoder stores pre only in the 32-token words holding a backward "
                          "entry (default), or all of it")
-    ap.add_argument("--grad-feat", choices=["sampled", "gemm"], default="sampled",
+    ap.add_argument("--grad-feat", choices=["sampled", "gemm", "auto"], default="sampled",
                     help="backward: grad_feat on the active + in-band entries only (default), "
                          "or the dense tcgen05 grad_feat GEMM")
     args = ap.parse_args()

@@ -321,6 +321,7 @@ class ShardedFusedStep(FusedStep):
             finally:
                 self._rows_cfg = None
         self._bind_grads()
+        self._auto_update(st, n)
         return st
 
     def grad_norm(self, max_norm: float = 1.0) -> None:

@@ -173,7 +173,8 @@ class FusedStep:
 
     def __init__(self, sae: B200JumpReLUSAE, optimizer: B200Adam, max_tokens: int,
                  csr_capacity: Optional[int] = None, force_simt: bool = False,
-                 grad_feat: str = "sampled", pre_store: str = "entries"):
+                 grad_feat: str = "sampled", pre_store: str = "entries",
+                 auto_threshold: float = 280.0):
         _require_cuda(sae.W_enc.weight)
         if not isinstance(optimizer, B200Adam) or optimizer.sae is not sae:
             raise TypeError("FusedStep needs the B200Adam built over the same SAE")
@@ -182,11 +183,17 @@ class FusedStep:
         self.max_tokens = int(max_tokens)
         self.csr_capacity = int(csr_capacity or _csr_capacity_default(self.max_tokens))
         self.force_simt = bool(force_simt)
-        if grad_feat not in ("sampled", "gemm"):
-            raise ValueError("grad_feat must be 'sampled' or 'gemm'")
+        if grad_feat not in ("sampled", "gemm", "auto"):
+            raise ValueError("grad_feat must be 'sampled', 'gemm' or 'auto'")
         # "sampled": grad_feat = go . W_dec[f] only where the backward uses it
-        # (active entries and the STE band); "gemm": the dense tcgen05 product.
-        self.grad_feat = grad_feat
+        # (active entries and the STE band); "gemm": the dense tcgen05 product;
+        # "auto": sampled while the entries per token stay under auto_threshold
+        # (the sampled cost grows with them, the GEMM's does not), the GEMM
+        # above it, decided from the previous microbatch's statistics.
+        self.grad_feat_mode = grad_feat
+        self.grad_feat = "sampled" if grad_feat == "auto" else grad_feat
+        self.auto_threshold = float(auto_threshold)
+        self._band_ratio = 1.0    # entries / active entries of the last sampled microbatch
         if pre_store not in ("entries", "full"):
             raise ValueError("pre_store must be 'entries' or 'full'")
         # "entries": the encoder stores pre only in the 32-token words that hold
@@ -403,7 +410,22 @@ class FusedStep:
         if redone and after_backward is not None:
             after_backward()
         self._bind_grads()
+        self._auto_update(st, n)
         return st
+
+    def _auto_update(self, st: dict, n_tokens: int) -> None:
+        """grad_feat="auto": pick the next microbatch's backward from this one's
+        entry count (sampled entries per token; in GEMM mode the active count
+        scaled by the last sampled microbatch's entries-per-active ratio), with
+        a 20% hysteresis so that it does not flip back and forth."""
+        if self.grad_feat_mode != "auto" or st["csr_overflow"] or n_tokens <= 0:
+            return
+        if self.grad_feat == "sampled":
+            self._band_ratio = st["csr_pairs"] / max(1, st["nnz"])
+            if st["csr_pairs"] / n_tokens > self.auto_threshold:
+                self.grad_feat = "gemm"
+        elif st["nnz"] * self._band_ratio / n_tokens < 0.8 * self.auto_threshold:
+            self.grad_feat = "sampled"
 
     def grad_norm(self, max_norm: float = 1.0) -> None:
         """Global L2 norm of all gradients + clip coefficient, on the device.
