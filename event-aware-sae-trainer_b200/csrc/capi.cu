@@ -93,8 +93,8 @@ DeviceInfo device_info() {
 struct Layout {
   size_t theta, xc, pre, sbits, mask, tile_cnt, col_tot, col_act, col_offs, go, tok_sqerr,
       tok_cnt, gosum_part, thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part,
-      row_sumsq, order_k0, order_k1, order_v0, order_v1, order_tmp, order_tmp_bytes, tok_offs,
-      counters, total;
+      row_sumsq, order_k0, order_k1, order_v0, order_v1, order_tmp, order_tmp_bytes, counters,
+      total;
 };
 
 // Row pitch (tokens) of the feature-major pre-activations: whole 64-token
@@ -164,12 +164,8 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   size_t scan_bytes = 0;   // the same scratch serves the CSR offset scan
   cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int*>(nullptr),
                                 static_cast<int*>(nullptr), static_cast<int>(F + 1));
-  size_t tok_scan_bytes = 0;   // and the decode list's per-token offsets
-  cub::DeviceScan::ExclusiveSum(nullptr, tok_scan_bytes, static_cast<int*>(nullptr),
-                                static_cast<int*>(nullptr), static_cast<int>(B));
-  L.order_tmp_bytes = std::max(sort_bytes, std::max(scan_bytes, tok_scan_bytes));
+  L.order_tmp_bytes = std::max(sort_bytes, scan_bytes);
   L.order_tmp = take(L.order_tmp_bytes);
-  L.tok_offs = take(B * 4);
   L.counters = take(256);
   L.total = off;
   return L;
@@ -200,7 +196,6 @@ struct Ws {
   int *order_k0, *order_k1, *order_v0, *order_v1;
   void* order_tmp;
   size_t order_tmp_bytes;
-  int* tok_offs;
   int* counters;
 };
 
@@ -234,7 +229,6 @@ Ws carve(void* base, const Layout& L) {
   w.order_v1 = reinterpret_cast<int*>(at(L.order_v1));
   w.order_tmp = at(L.order_tmp);
   w.order_tmp_bytes = L.order_tmp_bytes;
-  w.tok_offs = reinterpret_cast<int*>(at(L.tok_offs));
   w.counters = reinterpret_cast<int*>(at(L.counters));
   return w;
 }
@@ -325,15 +319,6 @@ int sampled_u(int d) {
   return (nvec % 2 == 0 && nvec / 2 >= 64) ? 2 : 1;
 }
 
-// Entries per chunk (one block barrier each) of the sampled backward at 96
-// threads: SAE_B200_SAMPLED_C=4 selects 4 instead of 2.
-int sampled_chunk() {
-  static const int c = [] {
-    const char* v = std::getenv("SAE_B200_SAMPLED_C");
-    return (v != nullptr && std::atoi(v) == 4) ? 4 : 2;
-  }();
-  return c;
-}
 
 int sampled_threads(int d) {
   return (d / 8 / sampled_u(d) + 31) / 32 * 32;
@@ -359,8 +344,7 @@ void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const 
     else if (bthr <= 512) SAE_SAMPLED(4, 1, 512, 1);
     else SAE_SAMPLED(4, 1, 1024, 1);
   } else {
-    if (bthr <= 96 && sampled_chunk() == 4) SAE_SAMPLED(4, 2, 96, 4);
-    else if (bthr <= 96) SAE_SAMPLED(2, 2, 96, 5);
+    if (bthr <= 96) SAE_SAMPLED(2, 2, 96, 5);
     else if (bthr <= 192) SAE_SAMPLED(2, 2, 192, 2);
     else if (bthr <= 256) SAE_SAMPLED(2, 2, 256, 2);
     else SAE_SAMPLED(2, 2, 512, 1);
@@ -661,7 +645,6 @@ namespace {
 
 struct ForwardCtx {
   int64_t B, d, F;
-  int64_t cap;   // CSR entries the workspace holds
   Layout L;
   Ws w;
   int mask_words, n_tiles;
@@ -685,7 +668,6 @@ int forward_checks(const SaeB200Model* model, const void* x, int x_dtype,
   c->B = cfg->n_tokens;
   c->d = model->d_in;
   c->F = model->n_features;
-  c->cap = cfg->csr_capacity;
   c->L = make_layout(c->B, c->d, c->F, cfg->csr_capacity);
   SAE_TRY(check_ws(c->L, workspace, workspace_bytes));
   c->w = carve(workspace, c->L);
@@ -780,16 +762,6 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
 
 // Gathered decode; partial != NULL writes the shard's decoder sums and counts
 // instead of the residual (dictionary-sharded step).
-// SAE_B200_DECODE_LIST=1: the decode reads token-major active lists built by
-// token_list_kernel instead of scanning each token's mask row itself.
-bool decode_lists_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("SAE_B200_DECODE_LIST");
-    return v != nullptr && v[0] == '1';
-  }();
-  return on;
-}
-
 // Row groups per token of the decode (blocks of G x V threads):
 // SAE_B200_DECODE_G=1|2|4 overrides the default.
 int decode_groups(int V) {
@@ -825,23 +797,8 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
       w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,             \
       static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), c.mask_words, \
       static_cast<int>(pre_pitch(B)), c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt,  \
-      w.gosum_part, partial, w.order_v1, lists ? w.order_k0 : nullptr, w.tok_offs,          \
-      lists ? w.csr_tok : nullptr, reinterpret_cast<const float*>(w.csr_val), c.cap)
+      w.gosum_part, partial, w.order_v1)
   timer_begin(SAE_KERNEL_DECODE, stream);
-  // token-major active lists (in the CSR arrays, which the backward fills
-  // only later): offsets from the counts, then one warp per token
-  const bool lists = decode_lists_enabled() && c.cap > 0;
-  if (lists) {
-    size_t scan_bytes = w.order_tmp_bytes;
-    if (cub::DeviceScan::ExclusiveSum(w.order_tmp, scan_bytes, w.order_k0, w.tok_offs,
-                                      static_cast<int>(B), stream) != cudaSuccess)
-      return fail(SAE_ERR_CUDA, "decode list offset scan failed");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    token_list_kernel<<<grid_for(B * 32, 256), 256, 0, stream>>>(
-        w.mask, w.pre, B, c.mask_words, static_cast<int>(pre_pitch(B)), w.order_k0, w.tok_offs,
-        c.cap, w.csr_tok, reinterpret_cast<float*>(w.csr_val));
-    SAE_TRY(check_launch("token_list_kernel"));
-  }
   if (x_dtype == SAE_DTYPE_BF16) {
     if (G >= 4) SAE_DECODE(bf16, 4);
     else if (G == 2 || G == 3) SAE_DECODE(bf16, 2);
@@ -1464,7 +1421,6 @@ int sae_b200_store_full_pre(const SaeB200Model* model, const SaeB200StepConfig* 
   c.B = cfg->n_tokens;
   c.d = model->d_in;
   c.F = model->n_features;
-  c.cap = cfg->csr_capacity;
   c.L = make_layout(c.B, c.d, c.F, cfg->csr_capacity);
   SAE_TRY(check_ws(c.L, workspace, workspace_bytes));
   c.w = carve(workspace, c.L);

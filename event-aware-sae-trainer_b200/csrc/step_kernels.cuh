@@ -939,11 +939,7 @@ __global__ void __launch_bounds__(1024)
                   int mask_words, int ldp, float go_scale, bf16* __restrict__ go,
                   float* __restrict__ x_hat, float* __restrict__ tok_sqerr,
                   int* __restrict__ tok_cnt, float* __restrict__ gosum_part,
-                  float* __restrict__ partial, const int* __restrict__ order,
-                  const int* __restrict__ list_cnt = nullptr,
-                  const int* __restrict__ list_offs = nullptr,
-                  const int* __restrict__ list_f = nullptr,
-                  const float* __restrict__ list_v = nullptr, int64_t list_cap = 0) {
+                  float* __restrict__ partial, const int* __restrict__ order) {
   __shared__ int s_f[DECODE_LIST_CAP];
   __shared__ float s_v[DECODE_LIST_CAP];
   __shared__ int s_itmp[33];
@@ -966,18 +962,10 @@ __global__ void __launch_bounds__(1024)
   for (int64_t k = blockIdx.x; k < n_tokens; k += gridDim.x) {
     const int64_t b = order != nullptr ? order[k] : k;
     const uint32_t* mrow = mask + b * mask_words;
-    // the token's list from token_list_kernel when it has one (uniform per block)
-    const int l_off = list_f != nullptr ? list_offs[b] : 0;
-    const int l_n = list_f != nullptr ? list_cnt[b] : 0;
-    const bool from_list = list_f != nullptr && static_cast<int64_t>(l_off) + l_n <= list_cap;
     int mine = 0;
-    int total = 0, my_off = 0;
-    if (from_list) {
-      total = l_n;
-    } else {
-      for (int w = w0; w < w1; ++w) mine += __popc(mrow[w]);
-      my_off = block_excl_scan(mine, s_itmp, total);
-    }
+    for (int w = w0; w < w1; ++w) mine += __popc(mrow[w]);
+    int total = 0;
+    const int my_off = block_excl_scan(mine, s_itmp, total);
 
     float acc[8];
 #pragma unroll
@@ -985,13 +973,7 @@ __global__ void __launch_bounds__(1024)
 
     for (int win = 0; win < total; win += DECODE_LIST_CAP) {
       __syncthreads();
-      if (from_list) {
-        const int n_w = min(DECODE_LIST_CAP, total - win);
-        for (int i = tid; i < n_w; i += blockDim.x) {
-          s_f[i] = list_f[l_off + win + i];
-          s_v[i] = list_v[l_off + win + i];
-        }
-      } else if (my_off < win + DECODE_LIST_CAP && my_off + mine > win) {
+      if (my_off < win + DECODE_LIST_CAP && my_off + mine > win) {
         int rank = my_off;
         for (int w = w0; w < w1; ++w) {
           uint32_t bits = mrow[w];
@@ -1108,60 +1090,6 @@ __global__ void __launch_bounds__(256)
     if (lane == 0) {
       counts[b] = c;
       ids[b] = static_cast<int>(b);
-    }
-  }
-}
-
-// Token-major active lists for the decode: one warp per token writes the
-// token's active features in increasing order, then their pre-activations,
-// at list[offs[b], offs[b] + counts[b]) (offs: exclusive scan of counts).
-// Tokens whose list would end past `cap` are skipped; the decode scans their
-// mask rows itself. Each lane prefetches LW mask words per round.
-constexpr int TL_WORDS = 8;
-__global__ void __launch_bounds__(256)
-    token_list_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
-                      int64_t n_tokens, int mask_words, int ldp, const int* __restrict__ counts,
-                      const int* __restrict__ offs, int64_t cap, int* __restrict__ list_f,
-                      float* __restrict__ list_v) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t b = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-       b < n_tokens; b += warps) {
-    const int off = offs[b], n = counts[b];
-    if (n == 0 || static_cast<int64_t>(off) + n > cap) continue;   // uniform per warp
-    const uint32_t* row = mask + b * mask_words;
-    int pos = off;
-    for (int w0 = 0; w0 < mask_words; w0 += 32 * TL_WORDS) {
-      uint32_t bits[TL_WORDS];
-#pragma unroll
-      for (int q = 0; q < TL_WORDS; ++q) {
-        const int w = w0 + 32 * q + lane;
-        bits[q] = w < mask_words ? row[w] : 0u;
-      }
-#pragma unroll
-      for (int q = 0; q < TL_WORDS; ++q) {
-        const int c = __popc(bits[q]);
-        int incl = c;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        int my = pos + incl - c;
-        const int fbase = (w0 + 32 * q + lane) * 32;
-        uint32_t m = bits[q];
-        while (m) {
-          const int bit = __ffs(m) - 1;
-          m &= m - 1;
-          list_f[my++] = fbase + bit;
-        }
-        pos += __shfl_sync(0xffffffffu, incl, 31);
-      }
-    }
-    __syncwarp();
-    for (int j = lane; j < n; j += 32) {
-      const int f = list_f[off + j];
-      list_v[off + j] = __bfloat162float(pre[static_cast<size_t>(f) * ldp + b]);
     }
   }
 }
