@@ -519,6 +519,7 @@ def run_b200(args):
     wl = WORKLOADS[args.workload]
     d, F_total, tokens, k_target = wl["d"], wl["F"], wl["tokens"], wl["k"]
     tokens = args.tokens or tokens
+    F_total = args.features or F_total
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -972,6 +973,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per step (default: the workload's); smaller values are for "
                          "profiler captures, not for the reported metric")
+    ap.add_argument("--features", type=int, default=0,
+                    help="dictionary size (default: the workload's); other values are for "
+                         "profiler captures of a small case, not for the reported metric")
     ap.add_argument("--pre-store", choices=["entries", "full"], default="entries",
                     help="encoder stores pre only in the 32-token words holding a backward "
                          "entry (default), or all of it")
