@@ -315,7 +315,7 @@ int sampled_u(int d) {
     return v != nullptr ? std::atoi(v) : 0;
   }();
   const int nvec = d / 8;
-  if ((forced == 1 || forced == 2) && nvec % forced == 0) return forced;
+  if ((forced == 1 || forced == 2 || forced == 3) && nvec % forced == 0) return forced;
   return (nvec % 2 == 0 && nvec / 2 >= 64) ? 2 : 1;
 }
 
@@ -332,13 +332,16 @@ void launch_sampled(const int* offs, const int* tok, const uint32_t* val, const 
                     cudaStream_t stream, float* row_sumsq = nullptr) {
   const int U = sampled_u(d);
   const int bthr = sampled_threads(d);
-  const int per_sm = bthr <= 96 ? 5 : (bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1));
+  const int per_sm = bthr <= 64 ? 6 : bthr <= 96 ? 5 : (bthr <= 192 ? 4 : (bthr <= 256 ? 2 : 1));
   const int grid = device_info().sm_count * per_sm * 2;
 #define SAE_SAMPLED(CC, UU, MT, MB)                                                            \
   sampled_backward_kernel<CC, UU, MT, MB><<<grid, bthr, 0, stream>>>(                         \
       offs, tok, val, go, xc, w_dec, theta, n_seg, n_tokens, d, eps, accumulate, g_wdec,       \
       g_wenc, g_logthr, g_benc, db_enc, counter, stats, seg_rows, honor_overflow, row_sumsq)
-  if (U == 1) {
+  if (U == 3) {
+    if (bthr <= 64) SAE_SAMPLED(2, 3, 64, 6);
+    else SAE_SAMPLED(2, 3, 192, 2);
+  } else if (U == 1) {
     if (bthr <= 192) SAE_SAMPLED(2, 1, 192, 4);
     else if (bthr <= 256) SAE_SAMPLED(4, 1, 256, 2);
     else if (bthr <= 512) SAE_SAMPLED(4, 1, 512, 1);
@@ -762,6 +765,16 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
 
 // Gathered decode; partial != NULL writes the shard's decoder sums and counts
 // instead of the residual (dictionary-sharded step).
+// SAE_B200_DECODE_R4=1: the decode gathers 4 rows per batch per thread and
+// is compiled for 4 resident 384-thread blocks per SM (more tokens in flight).
+bool decode_small_batches() {
+  static const bool on = [] {
+    const char* v = std::getenv("SAE_B200_DECODE_R4");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+
 // Row groups per token of the decode (blocks of G x V threads):
 // SAE_B200_DECODE_G=1|2|4 overrides the default.
 int decode_groups(int V) {
@@ -798,8 +811,17 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
       static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), c.mask_words, \
       static_cast<int>(pre_pitch(B)), c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt,  \
       w.gosum_part, partial, w.order_v1)
+#define SAE_DECODE_SMALL(XT)                                                                 \
+  decode_kernel<XT, 2, 4, 4><<<DECODE_GRID, V * 2, dyn, stream>>>(                          \
+      w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,             \
+      static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), c.mask_words, \
+      static_cast<int>(pre_pitch(B)), c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt,  \
+      w.gosum_part, partial, w.order_v1)
   timer_begin(SAE_KERNEL_DECODE, stream);
-  if (x_dtype == SAE_DTYPE_BF16) {
+  if (G == 2 && V * G <= 384 && decode_small_batches()) {
+    if (x_dtype == SAE_DTYPE_BF16) SAE_DECODE_SMALL(bf16);
+    else SAE_DECODE_SMALL(float);
+  } else if (x_dtype == SAE_DTYPE_BF16) {
     if (G >= 4) SAE_DECODE(bf16, 4);
     else if (G == 2 || G == 3) SAE_DECODE(bf16, 2);
     else SAE_DECODE(bf16, 1);
@@ -809,6 +831,7 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
     else SAE_DECODE(float, 1);
   }
 #undef SAE_DECODE
+#undef SAE_DECODE_SMALL
   const int rc = check_launch("decode_kernel");
   timer_end(SAE_KERNEL_DECODE, stream);
   return rc;

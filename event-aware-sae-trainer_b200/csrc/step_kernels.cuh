@@ -931,8 +931,11 @@ __device__ __forceinline__ float residual8(const float (&acc)[8], const XT* __re
 // partial[b * d + c] and its active count to partial[n_tokens * d + b] (as a
 // float); the shards' partials are summed across GPUs and residual_kernel
 // finishes the forward.
-template <typename XT, int G>
-__global__ void __launch_bounds__(1024)
+// RB: decoder rows gathered per batch by each thread (the same rows in the
+// same order whatever RB, so the sums are identical); MINB: blocks per SM the
+// register allocation must allow (1: the default 1024-thread bound).
+template <typename XT, int G, int RB = 8, int MINB = 1>
+__global__ void __launch_bounds__(MINB > 1 ? 384 : 1024, MINB)
     decode_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
                   const bf16* __restrict__ w_dec, const float* __restrict__ b_dec,
                   const XT* __restrict__ x, int64_t n_tokens, int d, int n_features,
@@ -994,13 +997,13 @@ __global__ void __launch_bounds__(1024)
       if (has) {
         const uint4* wcol = reinterpret_cast<const uint4*>(w_dec) + col;
         int i = g;
-        for (; i + 7 * G < n; i += 8 * G) {
-          uint4 u[8];
+        for (; i + (RB - 1) * G < n; i += RB * G) {
+          uint4 u[RB];
 #pragma unroll
-          for (int r = 0; r < 8; ++r)
+          for (int r = 0; r < RB; ++r)
             u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r * G]) * nvec);
 #pragma unroll
-          for (int r = 0; r < 8; ++r) {
+          for (int r = 0; r < RB; ++r) {
             float wf[8];
             unpack8(u[r], wf);
             const float a = s_v[i + r * G];
