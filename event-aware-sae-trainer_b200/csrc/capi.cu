@@ -94,7 +94,7 @@ struct Layout {
   size_t theta, xc, pre, sbits, mask, tile_cnt, col_tot, col_act, col_offs, go, tok_sqerr,
       tok_cnt, gosum_part, thr_part, dbenc_part, db_enc, gemv_part, csr_tok, csr_val, sumsq_part,
       row_sumsq, order_k0, order_k1, order_v0, order_v1, order_tmp, order_tmp_bytes, counters,
-      total;
+      cut, total;
 };
 
 // Row pitch (tokens) of the feature-major pre-activations: whole 64-token
@@ -167,6 +167,7 @@ Layout make_layout(int64_t B, int64_t d, int64_t F, int64_t cap) {
   L.order_tmp_bytes = std::max(sort_bytes, scan_bytes);
   L.order_tmp = take(L.order_tmp_bytes);
   L.counters = take(256);
+  L.cut = take(F * 8);   // per-feature gate cut values (float2)
   L.total = off;
   return L;
 }
@@ -197,6 +198,7 @@ struct Ws {
   void* order_tmp;
   size_t order_tmp_bytes;
   int* counters;
+  float2* cut;
 };
 
 Ws carve(void* base, const Layout& L) {
@@ -230,6 +232,7 @@ Ws carve(void* base, const Layout& L) {
   w.order_tmp = at(L.order_tmp);
   w.order_tmp_bytes = L.order_tmp_bytes;
   w.counters = reinterpret_cast<int*>(at(L.counters));
+  w.cut = reinterpret_cast<float2*>(at(L.cut));
   return w;
 }
 
@@ -304,11 +307,13 @@ bool tc_eligible(int64_t d, int64_t F, int force_simt) {
 // block of d / (8 U) threads (U = 2 for wide rows: more features in flight
 // per SM). seg_rows maps segments to feature rows (the aux backward).
 // Threads per block of the sampled backward at row width d (a multiple of 32).
-// 16-byte column vectors per thread (U) of the sampled backward: 2 from
-// d = 1024 up (at d = 1536: 3 warps per feature instead of 6, which halves the
-// per-warp work of every entry -- the butterfly, the partial sums, the flag
-// logic -- measured 1.5-1.6 ms against 2.0-2.1 ms per 32768-token step).
-// SAE_B200_SAMPLED_U=1|2 overrides it.
+// 16-byte column vectors per thread (U) of the sampled backward. Fewer warps
+// per feature row mean less per-warp work per entry (the butterfly, the
+// partial sums, the flag logic): at d = 1536, U = 3 (2 warps) measured
+// 1.36 ms per 32768-token step against 1.51 ms for U = 2 (3 warps) and
+// 2.0-2.1 ms for U = 1 (6 warps). U = 3 where the row splits into whole warps
+// of 3 vectors, else 2 from d = 1024 up, else 1. SAE_B200_SAMPLED_U=1|2|3
+// overrides it.
 int sampled_u(int d) {
   static const int forced = [] {
     const char* v = std::getenv("SAE_B200_SAMPLED_U");
@@ -316,6 +321,7 @@ int sampled_u(int d) {
   }();
   const int nvec = d / 8;
   if ((forced == 1 || forced == 2 || forced == 3) && nvec % forced == 0) return forced;
+  if (nvec % 3 == 0 && (nvec / 3) % 32 == 0 && nvec / 3 >= 64) return 3;
   return (nvec % 2 == 0 && nvec / 2 >= 64) ? 2 : 1;
 }
 
@@ -688,10 +694,10 @@ int forward_checks(const SaeB200Model* model, const void* x, int x_dtype,
 // counts into tile_cnt instead).
 template <int PRE>
 int launch_encoder(const SaeB200Model* model, const ForwardCtx& c, uint32_t* sbits,
-                   int* act_sum, int* entry_sum, float eps, bool use_tc, cudaStream_t stream) {
+                   int* act_sum, int* entry_sum, bool use_tc, cudaStream_t stream) {
   const Ws& w = c.w;
   EncodeEpiT<PRE> e{};
-  e.theta = w.theta;
+  e.cut = w.cut;
   e.b_enc = model->b_enc;
   e.pre = w.pre;
   e.mask = w.mask;
@@ -699,7 +705,6 @@ int launch_encoder(const SaeB200Model* model, const ForwardCtx& c, uint32_t* sbi
   e.act_sum = act_sum;
   e.entry_sum = entry_sum;
   e.sbits = sbits;
-  e.eps = eps;
   e.n_tokens = static_cast<int>(c.B);
   e.n_features = static_cast<int>(c.F);
   e.mask_words = c.mask_words;
@@ -720,19 +725,20 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
     const int g = grid_for(std::max<int64_t>(F, B * d / 8), 256);
     if (x_dtype == SAE_DTYPE_BF16)
       prep_kernel<bf16><<<g, 256, 0, stream>>>(static_cast<const bf16*>(x), model->b_dec,
-                                               model->log_threshold, w.theta, w.xc, B,
+                                               model->log_threshold, model->b_enc,
+                                               cfg->ste_bandwidth, w.theta, w.cut, w.xc, B,
                                                static_cast<int>(d), static_cast<int>(F));
     else
       prep_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(x), model->b_dec,
-                                                model->log_threshold, w.theta, w.xc, B,
+                                                model->log_threshold, model->b_enc,
+                                                cfg->ste_bandwidth, w.theta, w.cut, w.xc, B,
                                                 static_cast<int>(d), static_cast<int>(F));
     SAE_TRY(check_launch("prep_kernel"));
   }
   // 2. encoder GEMM + JumpReLU epilogue
   const bool use_tc = tc_eligible(d, F, cfg->force_simt);
   if (!sampled) {
-    SAE_TRY(launch_encoder<PRE_FULL>(model, c, nullptr, nullptr, nullptr, cfg->ste_bandwidth,
-                                     use_tc, stream));
+    SAE_TRY(launch_encoder<PRE_FULL>(model, c, nullptr, nullptr, nullptr, use_tc, stream));
     // per-feature scans of the per-tile counts -> CSR offsets of the active
     // entries and each tile's start inside them (the GEMM backward's CSR fill)
     scan_columns_kernel<<<grid_for(F, 256), 256, 0, stream>>>(
@@ -747,11 +753,9 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
   if (cudaMemsetAsync(w.col_tot, 0, (2 * F + 1) * sizeof(int), stream) != cudaSuccess)
     return fail(SAE_ERR_CUDA, "count reset failed");
   if (cfg->pre_entries_only)
-    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, w.sbits, w.col_act, w.col_tot,
-                                        cfg->ste_bandwidth, use_tc, stream));
+    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, w.sbits, w.col_act, w.col_tot, use_tc, stream));
   else
-    SAE_TRY(launch_encoder<PRE_FULL>(model, c, w.sbits, w.col_act, w.col_tot,
-                                     cfg->ste_bandwidth, use_tc, stream));
+    SAE_TRY(launch_encoder<PRE_FULL>(model, c, w.sbits, w.col_act, w.col_tot, use_tc, stream));
   // 3. CSR offsets of the entries = exclusive scan of the totals
   size_t tmp_bytes = w.order_tmp_bytes;
   if (cub::DeviceScan::ExclusiveSum(w.order_tmp, tmp_bytes, w.col_tot, w.col_offs,
@@ -765,16 +769,6 @@ int forward_encode(const SaeB200Model* model, const void* x, int x_dtype,
 
 // Gathered decode; partial != NULL writes the shard's decoder sums and counts
 // instead of the residual (dictionary-sharded step).
-// SAE_B200_DECODE_R4=1: the decode gathers 4 rows per batch per thread and
-// is compiled for 4 resident 384-thread blocks per SM (more tokens in flight).
-bool decode_small_batches() {
-  static const bool on = [] {
-    const char* v = std::getenv("SAE_B200_DECODE_R4");
-    return v != nullptr && v[0] == '1';
-  }();
-  return on;
-}
-
 // Row groups per token of the decode (blocks of G x V threads):
 // SAE_B200_DECODE_G=1|2|4 overrides the default.
 int decode_groups(int V) {
@@ -811,17 +805,8 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
       static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), c.mask_words, \
       static_cast<int>(pre_pitch(B)), c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt,  \
       w.gosum_part, partial, w.order_v1)
-#define SAE_DECODE_SMALL(XT)                                                                 \
-  decode_kernel<XT, 2, 4, 4><<<DECODE_GRID, V * 2, dyn, stream>>>(                          \
-      w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,             \
-      static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), c.mask_words, \
-      static_cast<int>(pre_pitch(B)), c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt,  \
-      w.gosum_part, partial, w.order_v1)
   timer_begin(SAE_KERNEL_DECODE, stream);
-  if (G == 2 && V * G <= 384 && decode_small_batches()) {
-    if (x_dtype == SAE_DTYPE_BF16) SAE_DECODE_SMALL(bf16);
-    else SAE_DECODE_SMALL(float);
-  } else if (x_dtype == SAE_DTYPE_BF16) {
+  if (x_dtype == SAE_DTYPE_BF16) {
     if (G >= 4) SAE_DECODE(bf16, 4);
     else if (G == 2 || G == 3) SAE_DECODE(bf16, 2);
     else SAE_DECODE(bf16, 1);
@@ -831,7 +816,6 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
     else SAE_DECODE(float, 1);
   }
 #undef SAE_DECODE
-#undef SAE_DECODE_SMALL
   const int rc = check_launch("decode_kernel");
   timer_end(SAE_KERNEL_DECODE, stream);
   return rc;
@@ -883,16 +867,18 @@ int sae_b200_encode_decode(const SaeB200Model* model, const void* x, int x_dtype
     const int g = grid_for(std::max<int64_t>(F, B * d / 8), 256);
     if (x_dtype == SAE_DTYPE_BF16)
       prep_kernel<bf16><<<g, 256, 0, stream>>>(static_cast<const bf16*>(x), model->b_dec,
-                                               model->log_threshold, w.theta, w.xc, B,
+                                               model->log_threshold, model->b_enc,
+                                               0.f, w.theta, w.cut, w.xc, B,
                                                static_cast<int>(d), static_cast<int>(F));
     else
       prep_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(x), model->b_dec,
-                                                model->log_threshold, w.theta, w.xc, B,
+                                                model->log_threshold, model->b_enc,
+                                                0.f, w.theta, w.cut, w.xc, B,
                                                 static_cast<int>(d), static_cast<int>(F));
     SAE_TRY(check_launch("prep_kernel"));
     // pre is stored only in the 32-token words holding an active entry: the
     // decode reads it there and nowhere else
-    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, nullptr, nullptr, nullptr, 0.f,
+    SAE_TRY(launch_encoder<PRE_ENTRIES>(model, c, nullptr, nullptr, nullptr,
                                         tc_eligible(d, F, 0), stream));
   }
   if (fired != nullptr) {
@@ -1449,10 +1435,11 @@ int sae_b200_store_full_pre(const SaeB200Model* model, const SaeB200StepConfig* 
   c.w = carve(workspace, c.L);
   c.mask_words = static_cast<int>((c.F + 31) / 32);
   c.n_tiles = static_cast<int>((c.B + TILE_N - 1) / TILE_N);
-  // the forward's xc and thresholds are still in the workspace; the encoder
-  // writes pre in full, the mask again (same bits) and per-tile counts into
-  // scratch the sampled path does not use
-  return launch_encoder<PRE_FULL>(model, c, nullptr, nullptr, nullptr, cfg->ste_bandwidth,
+  // the forward's xc, thresholds and gate cut values (same cfg, same
+  // bandwidth) are still in the workspace; the encoder writes pre in full, the
+  // mask again (same bits) and per-tile counts into scratch the sampled path
+  // does not use
+  return launch_encoder<PRE_FULL>(model, c, nullptr, nullptr, nullptr,
                                   tc_eligible(c.d, c.F, cfg->force_simt), stream);
 }
 

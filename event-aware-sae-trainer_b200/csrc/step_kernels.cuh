@@ -110,13 +110,60 @@ __device__ __forceinline__ int block_excl_scan(int v, int* s_tmp, int& total) {
 // theta = exp(log_threshold) (the same expf the reference's CUDA exp uses),
 // xc = bf16(float(x) - b_dec): autocast's cast of the fp32 difference
 // (sae_trainer_rolling.py:586-588).
+// ------------------------------------------------- gate cut values
+// For a feature with threshold th and bf16-rounded bias b, the encoder gate of
+// an accumulator v is [bf16(v + b) > th] and its sampled-backward entry bit is
+// [bf16(v + b) - th > -eps] (fp32 add and subtract, round to nearest). Each
+// step rounds monotonically, so each predicate is [v >= cut] for the least
+// float cut that satisfies it. gate_cut finds cut by bisection over the
+// ordered float keys, evaluating the predicate with exactly those operations;
+// the encoder epilogue then reads each bit off the sign of fl(v - cut), which
+// is exact: a nonzero difference never rounds to zero, and v = cut gives +0.
+// A zero cut is returned as -0, so that fl(v + 0) keeps v's sign for v = -0.
+__device__ __forceinline__ uint32_t float_key(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+template <bool ENTRY>
+__device__ float gate_cut(float bias, float th, float neg_eps) {
+  auto pass = [&](float v) {
+    const float p = bf16_round(__fadd_rn(v, bias));
+    return ENTRY ? (__fsub_rn(p, th) > neg_eps) : (p > th);
+  };
+  const float inf = __int_as_float(0x7F800000);
+  if (!pass(inf)) return inf;     // no finite v passes
+  if (pass(-inf)) return -inf;    // every finite v passes
+  uint32_t lo = float_key(-inf), hi = float_key(inf);   // pass(lo) false, pass(hi) true
+  while (hi - lo > 1u) {
+    const uint32_t mid = lo + (hi - lo) / 2u;
+    if (pass(key_float(mid))) hi = mid;
+    else lo = mid;
+  }
+  const float c = key_float(hi);
+  return c == 0.f ? -0.f : c;
+}
+
+// theta = exp(log_threshold) and, when cut is set, each feature's gate cut
+// values (x: active, y: sampled-backward entry at bandwidth eps); xc = x - b_dec
+// in bf16.
 template <typename XT>
 __global__ void prep_kernel(const XT* __restrict__ x, const float* __restrict__ b_dec,
-                            const float* __restrict__ log_thr, float* __restrict__ theta,
+                            const float* __restrict__ log_thr, const float* __restrict__ b_enc,
+                            float eps, float* __restrict__ theta, float2* __restrict__ cut,
                             bf16* __restrict__ xc, int64_t n_tokens, int d, int n_features) {
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t f = tid; f < n_features; f += stride) theta[f] = expf(log_thr[f]);
+  for (int64_t f = tid; f < n_features; f += stride) {
+    const float th = expf(log_thr[f]);
+    theta[f] = th;
+    if (cut != nullptr) {
+      const float b = bf16_round(b_enc[f]);
+      cut[f] = make_float2(gate_cut<false>(b, th, -eps), gate_cut<true>(b, th, -eps));
+    }
+  }
   const int64_t nvec = n_tokens * (d / 8);
   const int dv = d / 8;
   auto one = [&](int64_t i, const float (&xv)[8]) {
@@ -184,7 +231,7 @@ template <int PRE>
 struct EncodeEpiT {
   static constexpr int kAux = PRE == PRE_FULL ? AUX_STORE : AUX_NONE;
   static constexpr bool kAuxFeatureMajor = true;
-  const float* theta;
+  const float2* cut;   // per feature: gate cut values (active, entry) of gate_cut
   const float* b_enc;
   bf16* pre;          // [F, ldp]
   uint32_t* mask;
@@ -199,11 +246,10 @@ struct EncodeEpiT {
   // are added to act_sum[f] / entry_sum[f] instead of stored per tile
   int* act_sum;
   int* entry_sum;
-  float eps;
   int n_tokens, n_features, mask_words, ldp;
   // per-thread tile state
   int f, n0, lane, word, row;
-  float th, bias;
+  float neg_cut_a, neg_cut_s, bias;
   int cnt, bcnt;
   bool row_ok;
   bf16* aux;
@@ -216,7 +262,10 @@ struct EncodeEpiT {
     lane = ln;
     aux = aux_tile;
     row_ok = f < n_features;
-    th = row_ok ? theta[f] : __int_as_float(0x7f800000);
+    const float2 ct = row_ok ? cut[f] : make_float2(__int_as_float(0x7f800000),
+                                                    __int_as_float(0x7f800000));
+    neg_cut_a = -ct.x;
+    neg_cut_s = -ct.y;
     bias = row_ok ? bf16_round(b_enc[f]) : 0.f;
     word = (m_tile * TILE_M + q * 32) >> 5;
   }
@@ -227,22 +276,39 @@ struct EncodeEpiT {
   __device__ __forceinline__ void chunk(int c, const float (&v)[32]) {
     const int t0 = n0 + c;
     const int nj = row_ok ? min(32, n_tokens - t0) : 0;
-    uint32_t pk[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float2 s = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), make_float2(bias, bias));
-      pk[i] = pack_bf2(s.x, s.y);
-    }
+    const uint32_t valid = nj >= 32 ? 0xFFFFFFFFu : (nj <= 0 ? 0u : (1u << nj) - 1u);
     // aw: this feature's gate bits over the chunk's 32 tokens; sword: its
-    // sampled-backward entries (active or in band: pre - theta > -eps)
-    uint32_t aw = 0, sword = 0;
-    const float neg_eps = -eps;
+    // sampled-backward entries (active or in band). Bit j is set where
+    // v[j] >= cut, i.e. where fl(v[j] - cut) has its sign bit clear; the sign
+    // bits are shifted in from token 15 (31) down, two chains per mask.
+    uint32_t na0 = 0u, na1 = 0u, ns0 = 0u, ns1 = 0u;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float p = (j & 1) ? bf_hi(pk[j >> 1]) : bf_lo(pk[j >> 1]);
-      aw |= ((j < nj) && (p > th)) ? (1u << j) : 0u;
-      sword |= ((j < nj) && __fsub_rn(p, th) > neg_eps) ? (1u << j) : 0u;
+    for (int k = 7; k >= 0; --k) {
+      const float2 lo = make_float2(v[2 * k], v[2 * k + 1]);
+      const float2 hi = make_float2(v[16 + 2 * k], v[17 + 2 * k]);
+      const float2 la = __fadd2_rn(lo, make_float2(neg_cut_a, neg_cut_a));
+      const float2 ha = __fadd2_rn(hi, make_float2(neg_cut_a, neg_cut_a));
+      const float2 ls = __fadd2_rn(lo, make_float2(neg_cut_s, neg_cut_s));
+      const float2 hs = __fadd2_rn(hi, make_float2(neg_cut_s, neg_cut_s));
+      na0 = __funnelshift_l(__float_as_uint(la.y), na0, 1);
+      na0 = __funnelshift_l(__float_as_uint(la.x), na0, 1);
+      na1 = __funnelshift_l(__float_as_uint(ha.y), na1, 1);
+      na1 = __funnelshift_l(__float_as_uint(ha.x), na1, 1);
+      ns0 = __funnelshift_l(__float_as_uint(ls.y), ns0, 1);
+      ns0 = __funnelshift_l(__float_as_uint(ls.x), ns0, 1);
+      ns1 = __funnelshift_l(__float_as_uint(hs.y), ns1, 1);
+      ns1 = __funnelshift_l(__float_as_uint(hs.x), ns1, 1);
     }
+    const uint32_t aw = ~((na1 << 16) | na0) & valid;
+    const uint32_t sword = ~((ns1 << 16) | ns0) & valid;
+    // the bf16 pre-activations, where they are stored
+    auto pack_pre = [&](uint32_t (&pk)[16]) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 s = __fadd2_rn(make_float2(v[2 * i], v[2 * i + 1]), make_float2(bias, bias));
+        pk[i] = pack_bf2(s.x, s.y);
+      }
+    };
     cnt += __popc(aw);
     // 32x32 bit transpose across the warp (lane = feature -> lane = token):
     // afterwards lane j holds the mask word of token t0 + j over the warp's
@@ -261,12 +327,16 @@ struct EncodeEpiT {
     }
     if (aux != nullptr) {
       // tokens past n_tokens are clipped by the TMA store
+      uint32_t pk[16];
+      pack_pre(pk);
       uint8_t* base = reinterpret_cast<uint8_t*>(aux);
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         *reinterpret_cast<uint4*>(base + aux_fm_offset(row, (c >> 3) + q)) =
             make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
     } else if (row_ok && (PRE == PRE_FULL || (aw | sword) != 0u)) {
+      uint32_t pk[16];
+      pack_pre(pk);
       bf16* dst = pre + static_cast<size_t>(f) * ldp + t0;
 #pragma unroll
       for (int q = 0; q < 4; ++q)
@@ -931,11 +1001,8 @@ __device__ __forceinline__ float residual8(const float (&acc)[8], const XT* __re
 // partial[b * d + c] and its active count to partial[n_tokens * d + b] (as a
 // float); the shards' partials are summed across GPUs and residual_kernel
 // finishes the forward.
-// RB: decoder rows gathered per batch by each thread (the same rows in the
-// same order whatever RB, so the sums are identical); MINB: blocks per SM the
-// register allocation must allow (1: the default 1024-thread bound).
-template <typename XT, int G, int RB = 8, int MINB = 1>
-__global__ void __launch_bounds__(MINB > 1 ? 384 : 1024, MINB)
+template <typename XT, int G, int RB = 8>
+__global__ void __launch_bounds__(1024)
     decode_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
                   const bf16* __restrict__ w_dec, const float* __restrict__ b_dec,
                   const XT* __restrict__ x, int64_t n_tokens, int d, int n_features,
