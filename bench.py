@@ -103,17 +103,29 @@ class ClockSampler:
                     pass
         return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
-    def _poll(self, nv, h):
+    def _sample(self, nv, h):
         bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
                 "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
                 "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
                 "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.rows.append((float(sm), float(smax), {k for k, b in bits.items() if r & b}))
+
+    def sample(self):
+        """One sample from the calling thread (e.g. once the timed work is
+        queued and the GPU is still running it)."""
+        if getattr(self, "nvml", None) is not None:
+            try:
+                self._sample(*self.nvml)
+            except Exception as e:
+                self.error = f"{type(e).__name__}: {e}"
+
+    def _poll(self, nv, h):
         try:
-            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
             while not self.stop.is_set():
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.rows.append((float(sm), float(smax), {k for k, b in bits.items() if r & b}))
+                self._sample(nv, h)
                 self.stop.wait(self.period)
         except Exception as e:      # reported in the summary
             self.error = f"{type(e).__name__}: {e}"
@@ -123,6 +135,11 @@ class ClockSampler:
         self.stop = threading.Event()
         try:
             nv, h = self._nvml_handle()
+            self.nvml = (nv, h)
+            # one sample from this thread as the region starts and one as it
+            # ends, so that a region shorter than the poll thread's first
+            # wake-up still has a record
+            self._sample(nv, h)
             self.thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
             self.thread.start()
             return self
@@ -140,6 +157,10 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.thread is not None:
+            try:
+                self._sample(*self.nvml)
+            except Exception as e:
+                self.error = f"{type(e).__name__}: {e}"
             self.stop.set()
             self.thread.join(timeout=5)
         if self.proc is not None:
@@ -385,6 +406,7 @@ def run_inference(args):
             L.set_kernel_timer(L.KERNEL_ENCODER_GEMM, ev[i][0], ev[i][1])
             L.set_kernel_timer(L.KERNEL_DECODE, ev[i][2], ev[i][3])
             step(pool[i % 2])
+        clocks.sample()
         t1.record()
         torch.cuda.synchronize()
     L.set_kernel_timer(L.KERNEL_ENCODER_GEMM)
@@ -626,6 +648,7 @@ def run_b200(args):
             L.set_kernel_timer(L.KERNEL_ADAM, a_start[i], a_stop[i])
             L.set_kernel_timer(L.KERNEL_EXCHANGE, x_start[i], x_stop[i])
             stats.append(step(i, pool[(args.warmup + i) % POOL_BATCHES]))
+        clocks.sample()
         ev1.record()
         barrier()
     for k in (L.KERNEL_ENCODER_GEMM, L.KERNEL_GRAD_GEMM, L.KERNEL_DECODE, L.KERNEL_ADAM,

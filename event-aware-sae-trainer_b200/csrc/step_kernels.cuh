@@ -959,23 +959,26 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
 // squared error per token, and the loss gradient go = -(scale * 2r) stored as
 // bf16 (what the decoder GEMMs see).
 //
-// Residual of 8 columns of one token given the fp32 decoder sum acc:
-// x_hat = bf16(acc) + b_dec, r = x - x_hat, go = -(scale * 2r) (bf16), and the
-// running per-column go sums. Returns the 8 columns' squared error.
+// 8 consecutive x values as fp32.
 template <typename XT>
-__device__ __forceinline__ float residual8(const float (&acc)[8], const XT* __restrict__ x,
-                                           const float* __restrict__ b_dec, size_t base, int c0,
-                                           float go_scale, bf16* __restrict__ go,
-                                           float* __restrict__ x_hat, float (&gsum)[8]) {
-  float xv[8];
+__device__ __forceinline__ void load_x8(const XT* x, float (&xv)[8]) {
   if constexpr (sizeof(XT) == 2) {
-    unpack8(*reinterpret_cast<const uint4*>(x + base), xv);
+    unpack8(*reinterpret_cast<const uint4*>(x), xv);
   } else {
-    const float4 a = *reinterpret_cast<const float4*>(x + base);
-    const float4 c = *reinterpret_cast<const float4*>(x + base + 4);
+    const float4 a = *reinterpret_cast<const float4*>(x);
+    const float4 c = *reinterpret_cast<const float4*>(x + 4);
     xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
     xv[4] = c.x; xv[5] = c.y; xv[6] = c.z; xv[7] = c.w;
   }
+}
+
+// Residual of 8 columns of one token given the fp32 decoder sum acc and x:
+// x_hat = bf16(acc) + b_dec, r = x - x_hat, go = -(scale * 2r) (bf16), and the
+// running per-column go sums. Returns the 8 columns' squared error.
+__device__ __forceinline__ float residual8_x(const float (&acc)[8], const float (&xv)[8],
+                                             const float* __restrict__ b_dec, size_t base, int c0,
+                                             float go_scale, bf16* __restrict__ go,
+                                             float* __restrict__ x_hat, float (&gsum)[8]) {
   float gv[8], xh[8];
   float sq = 0.f;
 #pragma unroll
@@ -994,6 +997,31 @@ __device__ __forceinline__ float residual8(const float (&acc)[8], const XT* __re
   return sq;
 }
 
+template <typename XT>
+__device__ __forceinline__ float residual8(const float (&acc)[8], const XT* __restrict__ x,
+                                           const float* __restrict__ b_dec, size_t base, int c0,
+                                           float go_scale, bf16* __restrict__ go,
+                                           float* __restrict__ x_hat, float (&gsum)[8]) {
+  float xv[8];
+  load_x8(x + base, xv);
+  return residual8_x(acc, xv, b_dec, base, c0, go_scale, go, x_hat, gsum);
+}
+
+// Asynchronous global -> shared copies (LDGSTS): staged without registers.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // x == NULL (inference): the block writes x_hat (fp32, required) and the
 // token's active count only.
 // partial != NULL (dictionary-sharded step): instead of the residual, the
@@ -1001,7 +1029,10 @@ __device__ __forceinline__ float residual8(const float (&acc)[8], const XT* __re
 // partial[b * d + c] and its active count to partial[n_tokens * d + b] (as a
 // float); the shards' partials are summed across GPUs and residual_kernel
 // finishes the forward.
-template <typename XT, int G, int RB = 8>
+// The token's x columns are copied into shared memory (cp.async) when its
+// decode starts, so that they have landed by the residual; the token after
+// next is looked up one token ahead.
+template <typename XT, int G, int RB = 8, bool PAD = true>
 __global__ void __launch_bounds__(1024)
     decode_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
                   const bf16* __restrict__ w_dec, const float* __restrict__ b_dec,
@@ -1014,7 +1045,9 @@ __global__ void __launch_bounds__(1024)
   __shared__ float s_v[DECODE_LIST_CAP];
   __shared__ int s_itmp[33];
   __shared__ float s_ftmp[33];
-  extern __shared__ float4 s_part[];   // (G - 1) x V x 2 float4
+  // dynamic: (G - 1) x V x 2 float4 partial sums, then for the residual
+  // (x != NULL, partial == NULL): V x 2 float4 go sums | V x 8 XT x values
+  extern __shared__ float4 s_dyn[];
   const int tid = threadIdx.x;
   const int V = blockDim.x / G;
   const int g = tid / V;
@@ -1024,14 +1057,31 @@ __global__ void __launch_bounds__(1024)
   const int wpt = (mask_words + blockDim.x - 1) / blockDim.x;
   const int w0 = min(mask_words, tid * wpt);
   const int w1 = min(mask_words, w0 + wpt);
+  float4* s_part = s_dyn;
+  float4* s_gsum = s_dyn + (G - 1) * V * 2;   // this block's per-column go sums
+  XT* s_x = reinterpret_cast<XT*>(s_gsum + V * 2);
+  const bool residual = partial == nullptr && x != nullptr;   // uniform
+  const bool stage_x = residual && g == 0 && has;
 
-  float gsum[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) gsum[j] = 0.f;
+  if (stage_x) {
+    s_gsum[col * 2] = make_float4(0.f, 0.f, 0.f, 0.f);
+    s_gsum[col * 2 + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 
+  auto token_at = [&](int64_t k) -> int {
+    return k < n_tokens ? (order != nullptr ? order[k] : static_cast<int>(k)) : -1;
+  };
+  int b = token_at(blockIdx.x);
+  int bn = token_at(blockIdx.x + static_cast<int64_t>(gridDim.x));
   for (int64_t k = blockIdx.x; k < n_tokens; k += gridDim.x) {
-    const int64_t b = order != nullptr ? order[k] : k;
-    const uint32_t* mrow = mask + b * mask_words;
+    const int bnn = token_at(k + 2 * static_cast<int64_t>(gridDim.x));
+    if (stage_x) {
+      const XT* xs = x + static_cast<size_t>(b) * d + col * 8;
+      cp_async16(s_x + col * 8, xs);
+      if constexpr (sizeof(XT) == 4) cp_async16(s_x + col * 8 + 4, xs + 4);
+      cp_async_commit();
+    }
+    const uint32_t* mrow = mask + static_cast<size_t>(b) * mask_words;
     int mine = 0;
     for (int w = w0; w < w1; ++w) mine += __popc(mrow[w]);
     int total = 0;
@@ -1062,28 +1112,50 @@ __global__ void __launch_bounds__(1024)
       __syncthreads();
       const int n = min(DECODE_LIST_CAP, total - win);
       if (has) {
+        // rows g, g + G, g + 2G, ... of the list in order, RB loads in flight.
+        // The last batch is padded with repeats of the list's last row at
+        // weight 0, so that all of its loads are in flight together:
+        // fma(0, w, acc) = acc for finite w unless acc is -0, which a sum that
+        // starts at +0 reaches only through a product below the subnormal range.
         const uint4* wcol = reinterpret_cast<const uint4*>(w_dec) + col;
         int i = g;
-        for (; i + (RB - 1) * G < n; i += RB * G) {
-          uint4 u[RB];
+        if constexpr (PAD) {
+          for (; i < n; i += RB * G) {
+            uint4 u[RB];
 #pragma unroll
-          for (int r = 0; r < RB; ++r)
-            u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r * G]) * nvec);
+            for (int r = 0; r < RB; ++r)
+              u[r] = __ldg(wcol + static_cast<size_t>(s_f[min(i + r * G, n - 1)]) * nvec);
 #pragma unroll
-          for (int r = 0; r < RB; ++r) {
+            for (int r = 0; r < RB; ++r) {
+              float wf[8];
+              unpack8(u[r], wf);
+              const float a = i + r * G < n ? s_v[i + r * G] : 0.f;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+            }
+          }
+        } else {
+          for (; i + (RB - 1) * G < n; i += RB * G) {
+            uint4 u[RB];
+#pragma unroll
+            for (int r = 0; r < RB; ++r)
+              u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r * G]) * nvec);
+#pragma unroll
+            for (int r = 0; r < RB; ++r) {
+              float wf[8];
+              unpack8(u[r], wf);
+              const float a = s_v[i + r * G];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+            }
+          }
+          for (; i < n; i += G) {
             float wf[8];
-            unpack8(u[r], wf);
-            const float a = s_v[i + r * G];
+            unpack8(__ldg(wcol + static_cast<size_t>(s_f[i]) * nvec), wf);
+            const float a = s_v[i];
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
           }
-        }
-        for (; i < n; i += G) {
-          float wf[8];
-          unpack8(__ldg(wcol + static_cast<size_t>(s_f[i]) * nvec), wf);
-          const float a = s_v[i];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
         }
       }
     }
@@ -1105,14 +1177,17 @@ __global__ void __launch_bounds__(1024)
       }
     }
 
-    const size_t base = static_cast<size_t>(b) * d + col * 8;
+    const int bt = b;
+    b = bn;
+    bn = bnn;
+    const size_t base = static_cast<size_t>(bt) * d + col * 8;
     if (partial != nullptr) {   // uniform across the block
       if (g == 0 && has) {
         *reinterpret_cast<float4*>(partial + base) = make_float4(acc[0], acc[1], acc[2], acc[3]);
         *reinterpret_cast<float4*>(partial + base + 4) =
             make_float4(acc[4], acc[5], acc[6], acc[7]);
       }
-      if (tid == 0) partial[n_tokens * d + b] = static_cast<float>(total);
+      if (tid == 0) partial[n_tokens * d + bt] = static_cast<float>(total);
       continue;
     }
     if (x == nullptr) {         // inference: x_hat only (uniform across the block)
@@ -1123,21 +1198,31 @@ __global__ void __launch_bounds__(1024)
         *reinterpret_cast<float4*>(x_hat + base) = make_float4(xh[0], xh[1], xh[2], xh[3]);
         *reinterpret_cast<float4*>(x_hat + base + 4) = make_float4(xh[4], xh[5], xh[6], xh[7]);
       }
-      if (tid == 0) tok_cnt[b] = total;
+      if (tid == 0) tok_cnt[bt] = total;
       continue;
     }
     float sq = 0.f;
-    if (g == 0 && has) sq = residual8(acc, x, b_dec, base, col * 8, go_scale, go, x_hat, gsum);
+    if (stage_x) {
+      cp_async_wait<0>();   // this thread's x columns have landed
+      float xv[8], gsum[8];
+      load_x8(s_x + col * 8, xv);
+      const float4 g0 = s_gsum[col * 2], g1 = s_gsum[col * 2 + 1];
+      gsum[0] = g0.x; gsum[1] = g0.y; gsum[2] = g0.z; gsum[3] = g0.w;
+      gsum[4] = g1.x; gsum[5] = g1.y; gsum[6] = g1.z; gsum[7] = g1.w;
+      sq = residual8_x(acc, xv, b_dec, base, col * 8, go_scale, go, x_hat, gsum);
+      s_gsum[col * 2] = make_float4(gsum[0], gsum[1], gsum[2], gsum[3]);
+      s_gsum[col * 2 + 1] = make_float4(gsum[4], gsum[5], gsum[6], gsum[7]);
+    }
     const float tot_sq = block_sum(sq, s_ftmp);
     if (tid == 0) {
-      tok_sqerr[b] = tot_sq;
-      tok_cnt[b] = total;
+      tok_sqerr[bt] = tot_sq;
+      tok_cnt[bt] = total;
     }
   }
-  if (partial == nullptr && x != nullptr && g == 0 && has) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      gosum_part[static_cast<size_t>(blockIdx.x) * d + col * 8 + j] = gsum[j];
+  if (stage_x) {
+    float4* dst = reinterpret_cast<float4*>(gosum_part + static_cast<size_t>(blockIdx.x) * d + col * 8);
+    dst[0] = s_gsum[col * 2];
+    dst[1] = s_gsum[col * 2 + 1];
   }
   // sharded step: the partials may be read by other GPUs (peer exchange)
   if (partial != nullptr) __threadfence_system();
