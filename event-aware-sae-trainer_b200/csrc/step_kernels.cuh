@@ -807,12 +807,15 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
   const uint4* go_v = reinterpret_cast<const uint4*>(go) + U * tid;
   const uint4* xc_v = reinterpret_cast<const uint4*>(xc) + U * tid;
   int it = 0, par = 0;
+  if (tid == 0) s_f[0] = atomicAdd(counter, 1);
+  __syncthreads();
   while (true) {
-    if (tid == 0) s_f[it & 1] = atomicAdd(counter, 1);
-    __syncthreads();
     const int sg = s_f[it & 1];
-    ++it;
     if (sg >= n_features) break;
+    // the next feature is claimed now and published at the end of this one,
+    // so the atomic's round trip overlaps this feature's work
+    int next = 0;
+    if (tid == 0) next = atomicAdd(counter, 1);
     const int s = col_offs[sg], e = col_offs[sg + 1];
     const int f = seg_rows != nullptr ? seg_rows[sg] : sg;
     float wf[8 * U];
@@ -833,16 +836,28 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
 #pragma unroll
     for (int j = 0; j < 8 * U; ++j) ad[j] = ae[j] = 0.f;
     float thr = 0.f, db = 0.f;
+    // entries of the current chunk; those of the next chunk are loaded one
+    // chunk ahead, so only the row gathers wait on memory per chunk
+    int t[C];
+    uint32_t v[C];
+#pragma unroll
+    for (int r = 0; r < C; ++r) {
+      t[r] = s + r < e ? csr_tok[s + r] : 0;
+      v[r] = s + r < e ? csr_val[s + r] : 0u;
+    }
     for (int i0 = s; i0 < e; i0 += C) {
       const int n = min(C, e - i0);
-      int t[C];
-      uint32_t v[C];
+      int tn[C];
+      uint32_t vn[C];
 #pragma unroll
       for (int r = 0; r < C; ++r) {
-        // (the clamp only guards the row reads; the fill writes tokens < n_tokens)
-        t[r] = r < n ? min(max(csr_tok[i0 + r], 0), n_tokens - 1) : 0;
-        v[r] = r < n ? csr_val[i0 + r] : 0u;
+        const int k = i0 + C + r;
+        tn[r] = k < e ? csr_tok[k] : 0;
+        vn[r] = k < e ? csr_val[k] : 0u;
       }
+      // (the clamp only guards the row reads; the fill writes tokens < n_tokens)
+#pragma unroll
+      for (int r = 0; r < C; ++r) t[r] = min(max(t[r], 0), n_tokens - 1);
       uint4 gu[C][U], xu[C][U];
 #pragma unroll
       for (int r = 0; r < C; ++r) {
@@ -900,6 +915,11 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
         }
       }
       par ^= 1;
+#pragma unroll
+      for (int r = 0; r < C; ++r) {
+        t[r] = tn[r];
+        v[r] = vn[r];
+      }
     }
     float sq = 0.f;
     if (has) {
@@ -942,6 +962,9 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
       sq = warp_sum(sq);
       if (lane == 0) row_sumsq[static_cast<size_t>(f) * 32 + wid] = sq;
     }
+    ++it;
+    if (tid == 0) s_f[it & 1] = next;
+    __syncthreads();
   }
 }
 
