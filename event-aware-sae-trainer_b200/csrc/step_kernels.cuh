@@ -874,7 +874,11 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
       float part[C];
 #pragma unroll
       for (int r = 0; r < C; ++r) {
-        // even and odd columns in the two halves of packed FMAs
+        // even and odd columns in the two halves of packed FMAs; an active
+        // entry's dW_dec term (pre * go, independent of grad_feat) is added
+        // while its go values are unpacked
+        const bool act = r < n && (v[r] & CSR_ACTIVE);   // uniform across the block
+        const float p = __uint_as_float(v[r] << 16);
         float a0 = 0.f, a1 = 0.f;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -883,6 +887,11 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
 #pragma unroll
           for (int j = 0; j < 8; j += 2)
             fma2(a0, a1, g8[j], g8[j + 1], wf[8 * u + j], wf[8 * u + j + 1]);
+          if (act) {
+#pragma unroll
+            for (int j = 0; j < 8; j += 2)
+              fma2(ad[8 * u + j], ad[8 * u + j + 1], p, p, g8[j], g8[j + 1]);
+          }
         }
         part[r] = a0 + a1;
       }
@@ -900,14 +909,11 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS)
           if (v[r] & CSR_ACTIVE) {
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-              float g8[8], x8[8];
-              unpack8(gu[r][u], g8);
+              float x8[8];
               unpack8(xu[r][u], x8);
 #pragma unroll
-              for (int j = 0; j < 8; j += 2) {
-                fma2(ad[8 * u + j], ad[8 * u + j + 1], p, p, g8[j], g8[j + 1]);
+              for (int j = 0; j < 8; j += 2)
                 fma2(ae[8 * u + j], ae[8 * u + j + 1], gfv, gfv, x8[j], x8[j + 1]);
-              }
             }
             db += gfv;
           }
