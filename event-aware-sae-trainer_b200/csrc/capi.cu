@@ -785,17 +785,6 @@ int decode_groups(int V) {
   return std::min(4, std::max(1, 512 / V));
 }
 
-// SAE_B200_DECODE_PAD=0|1: the decode's last row batch per token is padded
-// (all of its loads in flight together) or finished row by row.
-bool decode_pad(int G) {
-  static const int forced = [] {
-    const char* v = std::getenv("SAE_B200_DECODE_PAD");
-    return v != nullptr ? std::atoi(v) : -1;
-  }();
-  if (forced == 0 || forced == 1) return forced == 1;
-  return G > 1;
-}
-
 int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const ForwardCtx& c,
                    float* x_hat_out, float* partial, cudaStream_t stream) {
   const int64_t B = c.B, d = c.d, F = c.F;
@@ -809,7 +798,6 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
   const bool residual = x != nullptr && partial == nullptr;
   const size_t dyn = static_cast<size_t>(G - 1) * V * 2 * sizeof(float4) +
                      (residual ? static_cast<size_t>(V) * (2 * sizeof(float4) + 8 * x_elem) : 0);
-  const bool pad = decode_pad(G);
   // Tokens' active counts are heavy-tailed: blocks take tokens in order of
   // decreasing count, round robin (a fixed, data-determined assignment, so the
   // per-block go sums stay deterministic).
@@ -822,20 +810,15 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
                                                 count_key_bits(F), stream) != cudaSuccess)
     return fail(SAE_ERR_CUDA, "token order sort failed");
   g_launches.fetch_add(1, std::memory_order_relaxed);
-#define SAE_DECODE_P(XT, GG, PP)                                                               \
+#define SAE_DECODE(XT, GG)                                                                     \
   do {                                                                                         \
-    cudaFuncSetAttribute(decode_kernel<XT, GG, 8, PP>,                                         \
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));  \
-    decode_kernel<XT, GG, 8, PP><<<DECODE_GRID, V * GG, dyn, stream>>>(                       \
+    cudaFuncSetAttribute(decode_kernel<XT, GG>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                         static_cast<int>(dyn));                                               \
+    decode_kernel<XT, GG><<<DECODE_GRID, V * GG, dyn, stream>>>(                              \
         w.mask, w.pre, static_cast<const bf16*>(model->W_dec_bf16), model->b_dec,             \
         static_cast<const XT*>(x), B, static_cast<int>(d), static_cast<int>(F), c.mask_words, \
         static_cast<int>(pre_pitch(B)), c.go_scale, w.go, x_hat_out, w.tok_sqerr, w.tok_cnt,  \
         w.gosum_part, partial, w.order_v1);                                                   \
-  } while (0)
-#define SAE_DECODE(XT, GG)                \
-  do {                                    \
-    if (pad) SAE_DECODE_P(XT, GG, true);  \
-    else SAE_DECODE_P(XT, GG, false);     \
   } while (0)
   timer_begin(SAE_KERNEL_DECODE, stream);
   if (x_dtype == SAE_DTYPE_BF16) {
@@ -848,7 +831,6 @@ int forward_decode(const SaeB200Model* model, const void* x, int x_dtype, const 
     else SAE_DECODE(float, 1);
   }
 #undef SAE_DECODE
-#undef SAE_DECODE_P
   const int rc = check_launch("decode_kernel");
   timer_end(SAE_KERNEL_DECODE, stream);
   return rc;

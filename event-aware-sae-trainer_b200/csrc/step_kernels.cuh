@@ -1043,6 +1043,12 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
                "l"(src)
                : "memory");
 }
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
@@ -1061,8 +1067,10 @@ __device__ __forceinline__ void cp_async_wait() {
 // The token's x columns are copied into shared memory (cp.async) when its
 // decode starts, so that they have landed by the residual; the token after
 // next is looked up one token ahead.
-template <typename XT, int G, int RB = 8, bool PAD = true>
-__global__ void __launch_bounds__(1024)
+// 56 registers: 3 blocks of 384 threads (2 row groups at d = 1536) or 4 of
+// 288 (1 row group at d = 2304) per SM; any block of up to 1024 threads fits.
+template <typename XT, int G, int RB = 8>
+__global__ void __maxnreg__(56)
     decode_kernel(const uint32_t* __restrict__ mask, const bf16* __restrict__ pre,
                   const bf16* __restrict__ w_dec, const float* __restrict__ b_dec,
                   const XT* __restrict__ x, int64_t n_tokens, int d, int n_features,
@@ -1071,7 +1079,7 @@ __global__ void __launch_bounds__(1024)
                   int* __restrict__ tok_cnt, float* __restrict__ gosum_part,
                   float* __restrict__ partial, const int* __restrict__ order) {
   __shared__ int s_f[DECODE_LIST_CAP];
-  __shared__ float s_v[DECODE_LIST_CAP];
+  __shared__ uint32_t s_pw[DECODE_LIST_CAP];   // the words holding the entries' pre values
   __shared__ int s_itmp[33];
   __shared__ float s_ftmp[33];
   // dynamic: (G - 1) x V x 2 float4 partial sums, then for the residual
@@ -1120,8 +1128,13 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
 
+    const uint32_t* pre_w = reinterpret_cast<const uint32_t*>(pre);
+    const bool hi_half = b & 1;   // ldp is even: the token's parity picks the half of a word
     for (int win = 0; win < total; win += DECODE_LIST_CAP) {
       __syncthreads();
+      // the active features in feature order; the 4-byte words holding their
+      // pre values are copied by cp.async, so that their round trip overlaps
+      // the first row batch's instead of preceding it
       if (my_off < win + DECODE_LIST_CAP && my_off + mine > win) {
         int rank = my_off;
         for (int w = w0; w < w1; ++w) {
@@ -1132,59 +1145,61 @@ __global__ void __launch_bounds__(1024)
             if (rank >= win && rank < win + DECODE_LIST_CAP) {
               const int f = w * 32 + bit;
               s_f[rank - win] = f;
-              s_v[rank - win] = __bfloat162float(pre[static_cast<size_t>(f) * ldp + b]);
+              cp_async4(&s_pw[rank - win], pre_w + ((static_cast<size_t>(f) * ldp + b) >> 1));
             }
             ++rank;
           }
         }
       }
-      __syncthreads();
+      cp_async_commit();
+      __syncthreads();   // the feature ids are in place
       const int n = min(DECODE_LIST_CAP, total - win);
+      const uint4* wcol = reinterpret_cast<const uint4*>(w_dec) + col;
+      auto pre_at = [&](int k) {
+        const uint32_t wd = s_pw[k];
+        return hi_half ? bf_hi(wd) : bf_lo(wd);
+      };
+      // rows g, g + G, g + 2G, ... of the list in order, RB loads in flight
+      int i = g;
+      uint4 u[RB];
+      // the first batch's loads go out before the wait for the pre words
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+        u[r] = (has && i < n) ? __ldg(wcol + static_cast<size_t>(s_f[min(i + r * G, n - 1)]) * nvec)
+                              : make_uint4(0u, 0u, 0u, 0u);
+      cp_async_wait<0>();
+      __syncthreads();   // every thread's pre words (and x columns) have landed
       if (has) {
-        // rows g, g + G, g + 2G, ... of the list in order, RB loads in flight.
-        // The last batch is padded with repeats of the list's last row at
-        // weight 0, so that all of its loads are in flight together:
-        // fma(0, w, acc) = acc for finite w unless acc is -0, which a sum that
-        // starts at +0 reaches only through a product below the subnormal range.
-        const uint4* wcol = reinterpret_cast<const uint4*>(w_dec) + col;
-        int i = g;
-        if constexpr (PAD) {
-          for (; i < n; i += RB * G) {
-            uint4 u[RB];
 #pragma unroll
-            for (int r = 0; r < RB; ++r)
-              u[r] = __ldg(wcol + static_cast<size_t>(s_f[min(i + r * G, n - 1)]) * nvec);
-#pragma unroll
-            for (int r = 0; r < RB; ++r) {
-              float wf[8];
-              unpack8(u[r], wf);
-              const float a = i + r * G < n ? s_v[i + r * G] : 0.f;
-#pragma unroll
-              for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
-            }
-          }
-        } else {
-          for (; i + (RB - 1) * G < n; i += RB * G) {
-            uint4 u[RB];
-#pragma unroll
-            for (int r = 0; r < RB; ++r)
-              u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r * G]) * nvec);
-#pragma unroll
-            for (int r = 0; r < RB; ++r) {
-              float wf[8];
-              unpack8(u[r], wf);
-              const float a = s_v[i + r * G];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
-            }
-          }
-          for (; i < n; i += G) {
+        for (int r = 0; r < RB; ++r) {
+          if (i + r * G < n) {
             float wf[8];
-            unpack8(__ldg(wcol + static_cast<size_t>(s_f[i]) * nvec), wf);
-            const float a = s_v[i];
+            unpack8(u[r], wf);
+            const float a = pre_at(i + r * G);
 #pragma unroll
             for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
           }
+        }
+        i += RB * G;
+        for (; i + (RB - 1) * G < n; i += RB * G) {
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            u[r] = __ldg(wcol + static_cast<size_t>(s_f[i + r * G]) * nvec);
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            float wf[8];
+            unpack8(u[r], wf);
+            const float a = pre_at(i + r * G);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
+          }
+        }
+        for (; i < n; i += G) {
+          float wf[8];
+          unpack8(__ldg(wcol + static_cast<size_t>(s_f[i]) * nvec), wf);
+          const float a = pre_at(i);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = fmaf(a, wf[j], acc[j]);
         }
       }
     }
