@@ -554,10 +554,19 @@ __global__ void __launch_bounds__(1024)
                        int* counters, uint8_t* __restrict__ fired) {
   __shared__ int s_tmp[33];
   int local = 0;
-  for (int f = threadIdx.x; f < n_features; f += blockDim.x) {
-    const int a = col_act[f];
-    local += a;
-    if (fired != nullptr && a > 0) fired[f] = 1;
+  // 8 independent loads in flight per thread (one block walks all features)
+  for (int f0 = threadIdx.x; f0 < n_features; f0 += 8 * blockDim.x) {
+    int a[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int f = f0 + u * blockDim.x;
+      a[u] = f < n_features ? col_act[f] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      local += a[u];
+      if (fired != nullptr && a[u] > 0) fired[f0 + u * blockDim.x] = 1;
+    }
   }
   int total = 0;
   block_excl_scan(local, s_tmp, total);
@@ -579,9 +588,11 @@ __global__ void __launch_bounds__(1024)
   const int b = threadIdx.x * per;
   const int e = min(n_features, b + per);
   int local = 0;
+#pragma unroll 8
   for (int i = b; i < e; ++i) local += col_tot[i];
   int total = 0;
   int run = block_excl_scan(local, s_tmp, total);
+#pragma unroll 8
   for (int i = b; i < e; ++i) {
     col_offs[i] = run;
     run += col_tot[i];
@@ -1475,7 +1486,11 @@ __global__ void __launch_bounds__(1024)
   const int k = blockIdx.x * 32 + tx;
   float a = 0.f, b = 0.f;
   if (k < d) {
+    // (unrolled so that several of the independent loads are in flight; the
+    // sums keep their order)
+#pragma unroll 8
     for (int i = ty; i < n_go; i += 32) a += gosum_part[static_cast<size_t>(i) * d + k];
+#pragma unroll 8
     for (int i = ty; i < n_gemv; i += 32) b += gemv_part[static_cast<size_t>(i) * d + k];
   }
   s1[ty][tx] = a;
