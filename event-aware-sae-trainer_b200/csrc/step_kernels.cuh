@@ -1435,8 +1435,10 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
   const uint4* wv = reinterpret_cast<const uint4*>(w_enc) + tid;
-  // 8 rows in flight per thread; a zero coefficient (feature without active
-  // tokens) skips its row's load but keeps the fixed summation order
+  // 8 rows in flight per thread, requested together with their coefficients
+  // (not after them: almost every feature fires in a microbatch); a zero
+  // coefficient (feature without active tokens) skips its FMAs, keeping the
+  // fixed summation order
   int f = blockIdx.x;
   for (; f + 7 * static_cast<int>(gridDim.x) < n_features; f += 8 * gridDim.x) {
     float sc[8];
@@ -1445,7 +1447,7 @@ __global__ void __launch_bounds__(1024)
     for (int r = 0; r < 8; ++r) {
       const int fr = f + r * gridDim.x;
       sc[r] = db_enc[fr];
-      u[r] = sc[r] != 0.f ? __ldg(wv + static_cast<size_t>(fr) * nvec) : make_uint4(0, 0, 0, 0);
+      u[r] = __ldg(wv + static_cast<size_t>(fr) * nvec);
     }
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
